@@ -1,0 +1,387 @@
+"""Benchmark of the packed-GGUF hot path on B200 (driver contract).
+
+One *step* = one pass of the batch-1 decode matvec over BASELINE config 2:
+the 11 packed types x {5120->5120, 5120->17408, 17408->5120}, fp16
+activations N(0,1), seeded synthetic packed weights (886 MB per step, far
+larger than the 126 MB L2, so no step reuses another's weights from L2).
+
+  value       whole-job QMV throughput in packed-weight GB/s: packed bytes of
+              the sweep x steps / device time of the timed region (CUDA graph
+              replays of the step, CUDA events, max over ranks).
+  e2e         the same metric through the public Python API with host
+              buffers: every step copies each projection's activation from
+              pinned host memory and reads the result back.
+  roofline    the QMV kernel: algorithmic bytes (packed + 2K + 4N per call)
+              / CUDA-event duration per launch (cold L2: a 256 MB write
+              between launches), summed over the sweep, vs measured HBM peak.
+  qmm_prefill config 3 at M=512 (tcgen05 QMM) in TFLOP/s vs measured bf16 peak.
+  cpu_baseline the reference's CPU path (gguf-py dequantize, which
+              mlx_gsq/quant/reference.py:10-18 calls, + numpy matvec) on a
+              bounded sample of the same workload.
+
+--gpus N (torchrun): each projection is split by output rows over the N
+ranks and the partial outputs are all-gathered with NCCL (tensor parallel,
+strong scaling: total work fixed).  --impl reference runs the CPU reference
+path only (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "mlx-gsq-rco_b200"))
+
+TYPES = ("IQ1_M", "IQ1_S", "IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ4_XS", "Q2_K", "Q4_K", "Q6_K")
+SHAPES = ((5120, 5120), (17408, 5120), (5120, 17408))  # (N out, K in)
+QMM_TYPES = ("IQ2_XS", "IQ3_S", "IQ4_XS", "Q6_K")
+QMM_SHAPES = ((17408, 5120), (5120, 17408))
+METRIC = "decode tok/s (batch 1) + QMV packed-byte HBM GB/s vs peak; prefill tok/s at M=512"
+BLOCK_BYTES = {"IQ1_M": 56, "IQ1_S": 50, "IQ2_XXS": 66, "IQ2_XS": 74, "IQ2_S": 82, "IQ3_XXS": 98, "IQ3_S": 110,
+               "IQ4_XS": 136, "Q2_K": 84, "Q4_K": 144, "Q6_K": 210}
+
+
+def packed_bytes(q, n, k):
+    return n * (k // 256) * BLOCK_BYTES[q]
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return {"hbm": p["hbm_gbs"], "bf16": p["bf16_tflops"], "src": "measured"}
+    return {"hbm": 6650.0, "bf16": 1590.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_reference_sample(time_budget_s: float = 20.0):
+    """The reference's CPU path: gguf-py dequantize (what dequantize_reference
+    calls) + numpy fp32 matvec, on 5120x5120 matrices of the sweep's types,
+    until the time budget is spent.  Returns packed-byte GB/s and the sample."""
+    import gguf
+    from gsq_b200.quant.synthetic import random_activations, random_matrix
+    done_bytes, spent, sample = 0, 0.0, []
+    for q in ("Q4_K", "IQ2_XS", "IQ3_S", "Q6_K", "IQ4_XS", "IQ1_S"):
+        n = k = 5120
+        packed = random_matrix(q, n, k, seed=0)
+        x = random_activations(1, k, seed=0).astype(np.float32)
+        t0 = time.perf_counter()
+        deq = gguf.dequantize(packed.reshape(-1, BLOCK_BYTES[q]), gguf.GGMLQuantizationType[q]).reshape(n, k)
+        _ = x @ deq.T
+        dt = time.perf_counter() - t0
+        done_bytes += packed.size
+        spent += dt
+        sample.append(f"{q} {n}x{k}")
+        if spent > time_budget_s:
+            break
+    return done_bytes / spent / 1e9, spent, sample
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    gbs, spent, sample = cpu_reference_sample(args.cpu_budget)
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s (packed weight bytes, QMV batch 1)",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config-2 QMV sweep, bounded CPU sample: " + ", ".join(sample),
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "reference",
+                         "sample": f"gguf-py 0.19.0 dequantize + numpy matvec over {', '.join(sample)} "
+                                   f"({spent:.1f} s)"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-qmm", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from gsq_b200 import _lib
+    from gsq_b200.quant.synthetic import random_matrix_torch
+    from gsq_b200.runtime.kernels import quantized_matmul, quantized_matvec
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    pk = peaks()
+
+    # ---- workload: every rank holds its row shard of every projection ----
+    cfgs = []
+    for ti, q in enumerate(TYPES):
+        for si, (n, k) in enumerate(SHAPES):
+            full = random_matrix_torch(q, n, k, seed=100 * ti + si, device=dev)
+            rows = n // world
+            rb = (k // 256) * BLOCK_BYTES[q]
+            shard = full[rank * rows * rb:(rank + 1) * rows * rb].clone()
+            del full
+            x = torch.randn(1, k, device=dev, dtype=torch.float16, generator=torch.Generator(device=dev).manual_seed(ti))
+            y = torch.empty(1, rows, device=dev, dtype=torch.float32)
+            yfull = torch.empty(world, rows, device=dev, dtype=torch.float32)
+            cfgs.append(dict(q=q, n=n, k=k, rows=rows, packed=shard, x=x, y=y, yfull=yfull,
+                             bytes=packed_bytes(q, n, k), alg=packed_bytes(q, rows, k) + 2 * k + 4 * rows))
+    step_bytes = sum(c["bytes"] for c in cfgs)
+    torch.cuda.synchronize()
+
+    def step():
+        for c in cfgs:
+            out = quantized_matvec(c["x"], c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
+                                   out_dtype=torch.float32)
+            if world > 1:
+                dist.all_gather_into_tensor(c["yfull"], out)
+
+    # warm up eagerly (allocates workspaces, sets kernel attributes), then capture
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap_stream = torch.cuda.Stream(device=dev)
+    cap_stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(cap_stream):
+        with torch.cuda.graph(graph, stream=cap_stream):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(cap_stream)
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    ms_per_step = ms / args.steps
+    value = step_bytes * args.steps / (ms / 1e3) / 1e9
+
+    # ---- per-kernel roofline: cold-L2 CUDA-event duration of every launch ----
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    per = []
+    reps = 5
+    for c in cfgs:
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            quantized_matvec(c["x"], c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
+                             out_dtype=torch.float32)
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        t_ms = float(np.median(ts))
+        per.append({"type": c["q"], "N": c["n"], "K": c["k"], "us": round(t_ms * 1e3, 2),
+                    "GBs": round(c["alg"] / (t_ms / 1e3) / 1e9, 1),
+                    "frac": round(c["alg"] / (t_ms / 1e3) / 1e9 / pk["hbm"], 3)})
+    alg_total = sum(c["alg"] for c in cfgs)
+    t_total = sum(p["us"] for p in per) * 1e-6
+    achieved = alg_total / t_total / 1e9
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "qmv_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("dram_bytes_per_launch")
+        except (OSError, ValueError):
+            traffic = None
+    roofline = {"bound": "hbm", "kernel": "gsq::qmv_kernel", "achieved": round(achieved, 1), "peak": pk["hbm"],
+                "unit": "GB/s", "frac": round(achieved / pk["hbm"], 4), "peak_source": pk["src"] + " (burst)",
+                "traffic": traffic,
+                "achieved_definition": "sum over the 33 sweep launches of (packed + 2K + 4N) bytes / sum of "
+                                       "cold-L2 CUDA-event launch durations"}
+
+    # ---- e2e through the public API with host buffers ----
+    host_x = [c["x"].cpu().pin_memory() for c in cfgs]
+    h2d = sum(h.numel() * h.element_size() for h in host_x)
+    d2h = sum(c["rows"] * world * 4 for c in cfgs)
+    for _ in range(2):
+        for c, hx in zip(cfgs, host_x):
+            xd = hx.to(dev, non_blocking=True)
+            out = quantized_matvec(xd, c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
+                                   out_dtype=torch.float32)
+            if world > 1:
+                dist.all_gather_into_tensor(c["yfull"], out)
+                out = c["yfull"]
+            out.cpu()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(3, args.steps // 4)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(e2e_steps):
+        for c, hx in zip(cfgs, host_x):
+            xd = hx.to(dev, non_blocking=True)
+            out = quantized_matvec(xd, c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
+                                   out_dtype=torch.float32)
+            if world > 1:
+                dist.all_gather_into_tensor(c["yfull"], out)
+                out = c["yfull"]
+            out.cpu()
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": round(step_bytes * e2e_steps / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "path": "pinned host x -> quantized_matvec (ctypes C-ABI call per projection) -> y.cpu()"}
+
+    # ---- QMM prefill, config 3 at M=512 (single GPU) ----
+    qmm = None
+    if world == 1 and not args.no_qmm:
+        qres = []
+        flops_total, t_qmm = 0.0, 0.0
+        for q in QMM_TYPES:
+            for (n, k) in QMM_SHAPES:
+                w = random_matrix_torch(q, n, k, seed=7, device=dev)
+                x = torch.randn(512, k, device=dev, dtype=torch.bfloat16)
+                for _ in range(2):
+                    quantized_matmul(x, w, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
+                ts = []
+                for _ in range(3):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    quantized_matmul(x, w, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    ts.append(e0.elapsed_time(e1))
+                t_ms = float(np.median(ts))
+                fl = 2.0 * 512 * n * k
+                flops_total += fl
+                t_qmm += t_ms / 1e3
+                qres.append({"type": q, "N": n, "K": k, "us": round(t_ms * 1e3, 1),
+                             "TFLOPs": round(fl / (t_ms / 1e3) / 1e12, 1)})
+                del w
+        tf = flops_total / t_qmm / 1e12
+        qmm = {"M": 512, "tflops": round(tf, 1), "peak": pk["bf16"], "frac": round(tf / pk["bf16"], 4),
+               "prefill_tok_s_per_projection_set": None, "per_shape": qres,
+               "note": "includes the bf16->fp16 activation pre-pass; weights decoded once per 128x128 tile"}
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        gbs, spent, sample = cpu_reference_sample(args.cpu_budget)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
+               "sample": f"gguf-py 0.19.0 dequantize + numpy matvec over {', '.join(sample)} ({spent:.1f} s)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s (packed weight bytes, QMV batch 1)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "int8 tensor-core dot of decoded packed weights (fp16 x, fp32 accumulate/out)",
+            "data": "synthetic",
+            "config": {"workload": "config-2 QMV sweep: 11 types x {5120->5120, 5120->17408, 17408->5120}, batch 1",
+                       "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (886 MB per step)",
+                       "parallelism": f"tp{world} (output rows, NCCL all-gather)" if world > 1 else "single GPU",
+                       "timing": "CUDA graph of one step, replayed; CUDA events"},
+            "roofline": roofline, "qmv_sweep": per, "qmm_prefill": qmm, "cpu_baseline": cpu, "e2e": e2e,
+            "clocks": clocks.summary(), "gpu_launches": args.steps * len(cfgs),
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

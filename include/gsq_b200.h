@@ -1,0 +1,112 @@
+/*
+ * gsq_b200 -- C ABI of the B200 (sm_100a) packed-GGUF hot path.
+ *
+ * Drop-in replacement for the kernel layer of mlx-GSQ-RCO
+ * (mlx_gsq/runtime/kernels/): dequantize, fused dequantize-matvec (decode),
+ * tiled dequantize-matmul (prefill) and the packed embedding gather, for the
+ * eleven GGUF block types IQ1_M, IQ1_S, IQ2_XXS, IQ2_XS, IQ2_S, IQ3_XXS,
+ * IQ3_S, IQ4_XS, Q2_K, Q4_K, Q6_K, read directly from the unmodified packed
+ * payloads.
+ *
+ * Conventions
+ *  - qtype is the GGML type id (mlx_gsq/gguf/parser.py:26-32): IQ1_M=29,
+ *    IQ1_S=19, IQ2_XXS=16, IQ2_XS=17, IQ2_S=22, IQ3_XXS=18, IQ3_S=21,
+ *    IQ4_XS=23, Q2_K=10, Q4_K=12, Q6_K=14.
+ *  - A packed matrix of N output rows and K inputs is N rows of K/256 blocks,
+ *    row n occupying bytes [n*(K/256)*bb, (n+1)*(K/256)*bb) (bb = block bytes).
+ *  - All pointers are device pointers; every call is asynchronous on
+ *    `stream` (a cudaStream_t; NULL = legacy default stream) and allocates
+ *    nothing: buffers, including workspaces, belong to the caller.
+ *  - Return value: GSQ_OK (0) or a negative gsq_status; gsq_last_error()
+ *    then describes the failure (per calling thread).
+ *  - Calls are thread-safe; concurrent calls that share a workspace must be
+ *    ordered by the caller (same stream, or events).
+ */
+#ifndef GSQ_B200_H
+#define GSQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define GSQ_API __attribute__((visibility("default")))
+#else
+#define GSQ_API
+#endif
+
+typedef struct CUstream_st* gsq_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  GSQ_OK = 0,
+  GSQ_ERR_QTYPE = -1,     /* unsupported quant type (reference: NotImplementedError, registry.py:29-31) */
+  GSQ_ERR_SIZE = -2,      /* shape / payload size mismatch (reference: ValueError, qmv.py:541-544) */
+  GSQ_ERR_ALIGN = -3,     /* pointer alignment requirement not met */
+  GSQ_ERR_ARG = -4,       /* other invalid argument (dtype, null pointer) */
+  GSQ_ERR_CUDA = -5,      /* CUDA runtime error at launch */
+  GSQ_ERR_WORKSPACE = -6, /* workspace missing or too small */
+  GSQ_ERR_DEVICE = -7     /* a kernel reported an error (gsq_device_status) */
+} gsq_status;
+
+typedef enum { GSQ_F32 = 0, GSQ_F16 = 1, GSQ_BF16 = 2 } gsq_dtype;
+
+/* Library version string. */
+GSQ_API const char* gsq_version(void);
+
+/* Description of the last error returned on this thread. */
+GSQ_API const char* gsq_last_error(void);
+
+/* Block geometry of a type: elements and stored bytes per block.
+ * Replaces QUANT_BLOCK_SIZES lookups (mlx_gsq/gguf/parser.py:35-42). */
+GSQ_API int gsq_block_info(int qtype, int* block_elements, int* block_bytes);
+
+/* Flat fp32 dequantization of nblocks packed blocks, bit-identical to
+ * gguf-py 0.19.0 (finite inputs).  out: nblocks*256 floats, 16-byte aligned.
+ * Replaces registry.decode / decode_weight (mlx_gsq/runtime/kernels/registry.py:28-46). */
+GSQ_API int gsq_dequant(int qtype, const uint8_t* packed, int64_t nblocks, float* out, gsq_stream_t stream);
+
+/* Workspace bytes gsq_qmv needs for this shape (0 when none is needed). */
+GSQ_API size_t gsq_qmv_workspace_size(int qtype, int64_t N, int64_t K, int64_t rows);
+
+/* Fused dequantize + matvec for few activation rows (decode):
+ *   y[r, n] = sum_k x[r, k] * deq(W)[n, k],  r < rows, fp32 accumulation.
+ * x: rows x K (x_dtype), 16-byte aligned.  y: rows x N (y_dtype).
+ * packed: 16-byte aligned, N*(K/256)*bb bytes.  K % 256 == 0.
+ * workspace: gsq_qmv_workspace_size() bytes, zero-filled before its first use;
+ * every completed call leaves it zero-filled again.
+ * Replaces quantized_matvec (mlx_gsq/runtime/kernels/qmv.py:537-576). */
+GSQ_API int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t rows,
+            void* y, int y_dtype, void* workspace, size_t workspace_bytes, gsq_stream_t stream);
+
+/* Workspace bytes gsq_qmm needs (an fp16 copy of x unless x is fp16). */
+GSQ_API size_t gsq_qmm_workspace_size(int qtype, int64_t N, int64_t K, int64_t M, int x_dtype);
+
+/* Tiled dequantize + matmul on tcgen05 tensor cores (prefill):
+ *   y[m, n] = sum_k x[m, k] * deq(W)[n, k],  fp32 output, M x N row-major.
+ * x: M x K (x_dtype), 16-byte aligned; weights decoded to fp16, fp32 accumulation.
+ * Replaces quantized_matmul (mlx_gsq/runtime/kernels/qmm.py:559-594). */
+GSQ_API int gsq_qmm(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
+            float* y, void* workspace, size_t workspace_bytes, gsq_stream_t stream);
+
+/* Packed embedding gather: out[t, :] = deq(W)[ids[t], :] rounded once to
+ * out_dtype; W is vocab x dim packed rows.  Out-of-range ids leave their row
+ * untouched and set GSQ_ERR_DEVICE in gsq_device_status.
+ * Replaces iq2_s_embedding (mlx_gsq/runtime/kernels/embedding.py:28-36),
+ * generalised from IQ2_S to all eleven types. */
+GSQ_API int gsq_embed(int qtype, const int32_t* ids, int64_t T, const uint8_t* packed, int64_t vocab, int64_t dim,
+              void* out, int out_dtype, gsq_stream_t stream);
+
+/* Synchronises `stream`, then returns and clears the device error word the
+ * kernels of the current device write (0 = none; 1 = a bounded wait expired;
+ * 2 = an embedding id was out of range).  No reference counterpart: the
+ * reference's Metal kernels have no device-side error path. */
+GSQ_API int gsq_device_status(gsq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSQ_B200_H */

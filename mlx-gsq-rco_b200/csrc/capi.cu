@@ -1,0 +1,165 @@
+// C ABI entry points (include/gsq_b200.h): argument validation, dispatch by
+// quant type, and the per-device error word.  Validation mirrors the
+// reference's Python contract (ValueError on size mismatch, qmv.py:540-544 /
+// qmm.py:571-580; NotImplementedError on an unknown type, registry.py:29-31)
+// as negative status codes.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <algorithm>
+
+#include "gsq_common.cuh"
+#include "../../include/gsq_b200.h"
+
+#include "gsq_host.h"
+
+using namespace gsq;
+
+static __device__ int g_device_error;
+
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+static int* device_error_word() {
+  static int* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+
+static bool supported(int t) {
+  switch (t) {
+#define GSQ_SUP(TT) case TT:
+    GSQ_FOR_EACH_QTYPE(GSQ_SUP)
+    return true;
+#undef GSQ_SUP
+  }
+  return false;
+}
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+static bool dtype_ok(int d) { return d == DT_F32 || d == DT_F16 || d == DT_BF16; }
+static size_t dtype_size(int d) { return d == DT_F32 ? 4 : 2; }
+
+static int cuda_fail(cudaError_t e, const char* what) {
+  return fail(GSQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+extern "C" {
+
+const char* gsq_version(void) { return "gsq_b200 0.1.0 (sm_100a)"; }
+
+const char* gsq_last_error(void) { return g_err; }
+
+int gsq_block_info(int qtype, int* block_elements, int* block_bytes_out) {
+  if (!supported(qtype)) return fail(GSQ_ERR_QTYPE, "unsupported quant type id %d", qtype);
+  if (block_elements) *block_elements = QK;
+  if (block_bytes_out) *block_bytes_out = block_bytes(qtype);
+  return GSQ_OK;
+}
+
+int gsq_dequant(int qtype, const uint8_t* packed, int64_t nblocks, float* out, gsq_stream_t stream) {
+  if (!supported(qtype)) return fail(GSQ_ERR_QTYPE, "validated decoder not available for type id %d", qtype);
+  if (nblocks < 0) return fail(GSQ_ERR_SIZE, "negative block count");
+  if (nblocks == 0) return GSQ_OK;
+  if (!packed || !out) return fail(GSQ_ERR_ARG, "null pointer");
+  if (!aligned(out, 16)) return fail(GSQ_ERR_ALIGN, "out must be 16-byte aligned");
+  cudaError_t e = dequant_launch(qtype, packed, nblocks, out, (cudaStream_t)stream);
+  return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_dequant launch");
+}
+
+static int check_matrix(int qtype, const uint8_t* packed, int64_t N, int64_t K) {
+  if (!supported(qtype)) return fail(GSQ_ERR_QTYPE, "no kernel for quant type id %d", qtype);
+  if (N < 0 || K <= 0 || K % QK) return fail(GSQ_ERR_SIZE, "invalid matrix width K=%lld (must be a positive multiple of 256)", (long long)K);
+  if (!packed) return fail(GSQ_ERR_ARG, "null packed pointer");
+  if (!aligned(packed, 16)) return fail(GSQ_ERR_ALIGN, "packed must be 16-byte aligned");
+  return GSQ_OK;
+}
+
+size_t gsq_qmv_workspace_size(int qtype, int64_t N, int64_t K, int64_t rows) {
+  if (!supported(qtype) || N <= 0 || K <= 0 || K % QK || rows <= 0) return 0;
+  return qmv_plan(qtype, N, K, (int)rows).workspace;
+}
+
+int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t rows,
+            void* y, int y_dtype, void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
+  int rc = check_matrix(qtype, packed, N, K);
+  if (rc) return rc;
+  if (rows < 0 || rows > (1 << 20)) return fail(GSQ_ERR_SIZE, "invalid row count %lld", (long long)rows);
+  if (rows == 0 || N == 0) return GSQ_OK;
+  if (!x || !y) return fail(GSQ_ERR_ARG, "null x or y");
+  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(GSQ_ERR_ARG, "unsupported dtype");
+  if (!aligned(x, dtype_size(x_dtype)) || !aligned(y, dtype_size(y_dtype))) return fail(GSQ_ERR_ALIGN, "x/y misaligned");
+  const QmvPlan p = qmv_plan(qtype, N, K, (int)rows);
+  if (p.workspace > 0 && (!workspace || workspace_bytes < p.workspace || !aligned(workspace, 256)))
+    return fail(GSQ_ERR_WORKSPACE, "gsq_qmv needs %zu workspace bytes (256-byte aligned), got %zu", p.workspace,
+                workspace_bytes);
+  cudaError_t e = qmv_run(qtype, x, x_dtype, packed, N, K, (int)rows, y, y_dtype, workspace, p, device_error_word(),
+                          (cudaStream_t)stream);
+  return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_qmv launch");
+}
+
+size_t gsq_qmm_workspace_size(int qtype, int64_t N, int64_t K, int64_t M, int x_dtype) {
+  (void)qtype; (void)N;
+  if (M <= 0 || K <= 0) return 0;
+  return qmm_x16_bytes(x_dtype, M, K);
+}
+
+int gsq_qmm(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
+            float* y, void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
+  int rc = check_matrix(qtype, packed, N, K);
+  if (rc) return rc;
+  if (M < 0 || M > (1ll << 31)) return fail(GSQ_ERR_SIZE, "invalid row count %lld", (long long)M);
+  if (M == 0 || N == 0) return GSQ_OK;
+  if (!x || !y) return fail(GSQ_ERR_ARG, "null x or y");
+  if (!dtype_ok(x_dtype)) return fail(GSQ_ERR_ARG, "unsupported x dtype");
+  if (!aligned(x, 16) || !aligned(y, 4)) return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned");
+  const size_t need = qmm_x16_bytes(x_dtype, M, K);
+  if (need > 0 && (!workspace || workspace_bytes < need || !aligned(workspace, 16)))
+    return fail(GSQ_ERR_WORKSPACE, "gsq_qmm needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  const char* why = "launch";
+  cudaError_t e = qmm_launch(qtype, x, x_dtype, packed, N, K, M, y, static_cast<__half*>(workspace),
+                             device_error_word(), (cudaStream_t)stream, &why);
+  return e == cudaSuccess ? GSQ_OK : cuda_fail(e, why);
+}
+
+int gsq_embed(int qtype, const int32_t* ids, int64_t T, const uint8_t* packed, int64_t vocab, int64_t dim,
+              void* out, int out_dtype, gsq_stream_t stream) {
+  if (!supported(qtype)) return fail(GSQ_ERR_QTYPE, "unsupported embedding type id %d", qtype);
+  if (dim <= 0 || dim % QK) return fail(GSQ_ERR_SIZE, "embedding dimensions must be divisible by 256");
+  if (T < 0 || vocab <= 0) return fail(GSQ_ERR_SIZE, "invalid token count or vocab");
+  if (T == 0) return GSQ_OK;
+  if (!ids || !packed || !out) return fail(GSQ_ERR_ARG, "null pointer");
+  if (!dtype_ok(out_dtype)) return fail(GSQ_ERR_ARG, "unsupported dtype");
+  if (!aligned(out, 16)) return fail(GSQ_ERR_ALIGN, "out must be 16-byte aligned");
+  cudaError_t e = embed_launch(qtype, ids, T, packed, vocab, dim, out, out_dtype, device_error_word(),
+                               (cudaStream_t)stream);
+  return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_embed launch");
+}
+
+int gsq_device_status(gsq_stream_t stream) {
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "gsq_device_status sync");
+  int* w = device_error_word();
+  if (!w) return fail(GSQ_ERR_CUDA, "device error word unavailable");
+  int v = 0;
+  e = cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "gsq_device_status read");
+  const int zero = 0;
+  cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  return v;
+}
+
+}  // extern "C"

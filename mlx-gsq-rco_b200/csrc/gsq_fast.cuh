@@ -1,0 +1,334 @@
+// Integer-entry decoders for the tensor-core matvec.
+//
+// Every supported format can be written, per sub-block ("unit") of 16 or 32
+// weights, as   w_k = S_u * a_k + B_u   with a_k a small integer that fits in
+// int8 and S_u, B_u fp32 per-unit constants:
+//
+//   Q2_K   (unit 16)  a = q in [0,3]          S = d*(sc&15)      B = -dmin*(sc>>4)
+//   Q4_K   (unit 32)  a = q in [0,15]         S = d*sc           B = -dmin*m
+//   Q6_K   (unit 16)  a = q in [0,63]         S = d*scale        B = -32*S
+//   IQ4_XS (unit 32)  a = kvalues[q]          S = d*(scale-32)   B = 0
+//   IQ2_*  (unit 32/16) a = +-grid            S = d*(0.5+s)/4    B = 0
+//   IQ3_XXS (unit 32) a = +-grid              S = d*(0.5+s)/2    B = 0
+//   IQ3_S  (unit 32)  a = +-grid              S = d*(1+2s)       B = 0
+//   IQ1_S/M           a = 8*grid +- 1         S = d*(2s+1)/8     B = 0
+//
+// (derived from the block layouts that gguf-py 0.19.0 quants.py dequantizes;
+// the reference's fused kernels apply the same decode per weight in fp32,
+// mlx_gsq/runtime/kernels/qmv.py:76-528).  The matvec multiplies the a_k with
+// int8 activations on the tensor cores and applies S_u, B_u once per unit.
+//
+// Entry layout.  For a 32-weight MMA chunk c32 (0..7) of a block and a thread
+// quad index tq (0..3), entry() returns the 8 int8 values that thread feeds to
+// mma.m16n8k32: `lo` holds MMA k = 4tq..4tq+3 and `hi` holds 16+4tq..16+4tq+3.
+// BLOCKED formats map them to block elements 32*c32 + 8tq .. +7 (one grid
+// entry); the identity mapping (IQ4_XS) uses 32*c32 + 4tq.. and +16+4tq...
+// The activation operand is laid out with the same mapping.
+//
+// Blocks live in shared memory at the byte alignment the packed stream gives
+// them: every block start is 2-byte aligned; blocks of 56/84/136/144 bytes are
+// 4/8/16-byte aligned.  The readers below use the widest access that the
+// format's guaranteed alignment allows.
+#pragma once
+
+#include "gsq_common.cuh"
+
+namespace gsq {
+
+// Expand the low 8 bits of s into a byte mask (byte j = 0xFF if bit j set).
+__host__ __device__ inline uint64_t expand_sign_mask(uint32_t s) {
+  uint64_t m = 0;
+  for (int j = 0; j < 8; j++)
+    if ((s >> j) & 1u) m |= (uint64_t)0xFF << (8 * j);
+  return m;
+}
+
+// Negate the bytes of (lo, hi) selected by the mask.  Magnitudes are >= 1, so
+// (v ^ 0xFF) + 1 == -v never carries into the neighbouring byte.
+__device__ __forceinline__ void apply_sign(uint32_t& lo, uint32_t& hi, uint2 m) {
+  lo = (lo ^ m.x) + (m.x & 0x01010101u);
+  hi = (hi ^ m.y) + (m.y & 0x01010101u);
+}
+
+__device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+template <int T> struct Fast;
+
+// Shared table builders -------------------------------------------------------
+template <int T>
+__device__ void copy_grid(uint8_t* dst, int tid, int nthr) {
+  constexpr int n = GridOf<T>::entries * GridOf<T>::width;
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(GridOf<T>::ptr());
+  uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+  for (int i = tid; i < n / 4; i += nthr) d[i] = src[i];
+}
+
+// 128-entry mask table indexed by the 7-bit ksigns index (parity bit folded in).
+__device__ inline void build_kmask(uint8_t* dst, int tid, int nthr) {
+  uint64_t* d = reinterpret_cast<uint64_t*>(dst);
+  for (int i = tid; i < 128; i += nthr) d[i] = expand_sign_mask(kKsigns[i]);
+}
+
+// 256-entry mask table indexed by an explicit sign byte.
+__device__ inline void build_smask(uint8_t* dst, int tid, int nthr) {
+  uint64_t* d = reinterpret_cast<uint64_t*>(dst);
+  for (int i = tid; i < 256; i += nthr) d[i] = expand_sign_mask((uint32_t)i);
+}
+
+// IQ1 grid premultiplied by 8 with the +-1/8 delta folded in: half 0 holds
+// 8*g + 1 (delta +0.125), half 1 holds 8*g - 1 (delta -0.125).
+__device__ inline void build_iq1_dual(uint8_t* dst, int tid, int nthr) {
+  int8_t* d = reinterpret_cast<int8_t*>(dst);
+  for (int i = tid; i < 2048 * 8; i += nthr) {
+    const int g = kGridIQ1S[i];
+    d[i] = (int8_t)(8 * g + 1);
+    d[2048 * 8 + i] = (int8_t)(8 * g - 1);
+  }
+}
+
+// --- K-quants ----------------------------------------------------------------
+
+template <> struct Fast<T_Q2_K> {
+  static constexpr int UNIT = 16, TAB_BYTES = 0;
+  static constexpr bool BLOCKED = true, HAS_BIAS = true;
+  __device__ static void load_tables(uint8_t*, int, int) {}
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t*, uint32_t& lo, uint32_t& hi) {
+    const int i = 4 * c32 + tq;
+    const int chunk = i >> 4, plane = (i & 15) >> 2;
+    const uint2 w = ld64a4(b + 16 + chunk * 32 + 8 * (i & 3));
+    lo = (w.x >> (2 * plane)) & 0x03030303u;
+    hi = (w.y >> (2 * plane)) & 0x03030303u;
+  }
+  __device__ static void affine(const uint8_t* b, int u, float& S, float& B) {
+    const uint32_t sc = b[u];
+    S = h2f_bits(ld16a2(b + 80)) * (float)(sc & 15u);
+    B = -h2f_bits(ld16a2(b + 82)) * (float)(sc >> 4);
+  }
+};
+
+template <> struct Fast<T_Q4_K> {
+  static constexpr int UNIT = 32, TAB_BYTES = 0;
+  static constexpr bool BLOCKED = true, HAS_BIAS = true;
+  __device__ static void load_tables(uint8_t*, int, int) {}
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t*, uint32_t& lo, uint32_t& hi) {
+    const uint2 w = ld64a8(b + 16 + (c32 >> 1) * 32 + 8 * tq);
+    const int sh = 4 * (c32 & 1);
+    lo = (w.x >> sh) & 0x0F0F0F0Fu;
+    hi = (w.y >> sh) & 0x0F0F0F0Fu;
+  }
+  __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
+    const uint8_t* s = b + 4;
+    uint32_t sc, mn;
+    if (g < 4) {
+      sc = s[g] & 63u;
+      mn = s[4 + g] & 63u;
+    } else {
+      const int j = g - 4;
+      sc = (s[8 + j] & 15u) | ((s[j] >> 2) & 48u);
+      mn = (s[8 + j] >> 4) | ((s[4 + j] >> 2) & 48u);
+    }
+    S = h2f_bits(ld16a2(b)) * (float)sc;
+    B = -h2f_bits(ld16a2(b + 2)) * (float)mn;
+  }
+};
+
+template <> struct Fast<T_Q6_K> {
+  static constexpr int UNIT = 16, TAB_BYTES = 0;
+  static constexpr bool BLOCKED = true, HAS_BIAS = true;
+  __device__ static void load_tables(uint8_t*, int, int) {}
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t*, uint32_t& lo, uint32_t& hi) {
+    const int i = 4 * c32 + tq;
+    const int c = i >> 4, r0 = 8 * (i & 15);
+    const uint2 ql = ld64a2(b + c * 64 + (r0 & 63));
+    const uint2 qh = ld64a2(b + 128 + c * 32 + (r0 & 31));
+    const int s1 = 4 * (r0 >> 6), s2 = 2 * (r0 >> 5 & 3);
+    lo = ((ql.x >> s1) & 0x0F0F0F0Fu) | (((qh.x >> s2) & 0x03030303u) << 4);
+    hi = ((ql.y >> s1) & 0x0F0F0F0Fu) | (((qh.y >> s2) & 0x03030303u) << 4);
+  }
+  __device__ static void affine(const uint8_t* b, int u, float& S, float& B) {
+    S = h2f_bits(ld16a2(b + 208)) * (float)(int8_t)b[192 + u];
+    B = -32.0f * S;
+  }
+};
+
+// 16-entry int8 table lookup of the four nibbles in the low 16 bits of `sel`,
+// using byte permutes over the table held in four registers.
+__device__ __forceinline__ uint32_t lut16(uint32_t sel, uint32_t t0, uint32_t t1, uint32_t t2, uint32_t t3) {
+  const uint32_t lowp = __byte_perm(t0, t1, sel & 0x7777u);
+  const uint32_t highp = __byte_perm(t2, t3, sel & 0x7777u);
+  const uint32_t pick = 0x3210u | ((sel >> 1) & 0x4444u);
+  return __byte_perm(lowp, highp, pick);
+}
+
+template <> struct Fast<T_IQ4_XS> {
+  static constexpr int UNIT = 32, TAB_BYTES = 16;
+  static constexpr bool BLOCKED = false, HAS_BIAS = false;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
+    for (int i = tid; i < 16; i += nthr) tab[i] = (uint8_t)kKvalues[i];
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const uint4 kv = *reinterpret_cast<const uint4*>(tab);
+    const uint32_t w = ld32a4(b + 8 + 16 * c32 + 4 * tq);
+    // nibble order in w: lo0 hi0 lo1 hi1 lo2 hi2 lo3 hi3
+    const uint32_t r01 = lut16(w, kv.x, kv.y, kv.z, kv.w);
+    const uint32_t r23 = lut16(w >> 16, kv.x, kv.y, kv.z, kv.w);
+    lo = __byte_perm(r01, r23, 0x6420u);
+    hi = __byte_perm(r01, r23, 0x7531u);
+  }
+  __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
+    const uint32_t l = (b[4 + (g >> 1)] >> (4 * (g & 1))) & 15u;
+    const uint32_t h = (ld16a2(b + 2) >> (2 * g)) & 3u;
+    S = h2f_bits(ld16a2(b)) * (float)((int)(l | (h << 4)) - 32);
+    B = 0.f;
+  }
+};
+
+// --- IQ lookup types ------------------------------------------------------------
+
+template <> struct Fast<T_IQ2_XXS> {
+  static constexpr int UNIT = 32, GRID = 256 * 8, TAB_BYTES = GRID + 128 * 8;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
+    copy_grid<T_IQ2_XXS>(tab, tid, nthr);
+    build_kmask(tab + GRID, tid, nthr);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const uint8_t* q = b + 2 + 8 * c32;
+    const uint32_t aux = ld32a2(q + 4);
+    const uint2 g = lds64(tab + 8 * q[tq]);
+    const uint2 m = lds64(tab + GRID + 8 * ((aux >> (7 * tq)) & 127u));
+    lo = g.x; hi = g.y;
+    apply_sign(lo, hi, m);
+  }
+  __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
+    const uint32_t aux = ld32a2(b + 2 + 8 * g + 4);
+    S = h2f_bits(ld16a2(b)) * (0.5f + (float)(aux >> 28)) * 0.25f;
+    B = 0.f;
+  }
+};
+
+template <> struct Fast<T_IQ2_XS> {
+  static constexpr int UNIT = 16, GRID = 512 * 8, TAB_BYTES = GRID + 128 * 8;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
+    copy_grid<T_IQ2_XS>(tab, tid, nthr);
+    build_kmask(tab + GRID, tid, nthr);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const uint32_t q = ld16a2(b + 2 + 2 * (4 * c32 + tq));
+    const uint2 g = lds64(tab + 8 * (q & 511u));
+    const uint2 m = lds64(tab + GRID + 8 * (q >> 9));
+    lo = g.x; hi = g.y;
+    apply_sign(lo, hi, m);
+  }
+  __device__ static void affine(const uint8_t* b, int s, float& S, float& B) {
+    const uint32_t sc = (b[66 + (s >> 1)] >> (4 * (s & 1))) & 15u;
+    S = h2f_bits(ld16a2(b)) * (0.5f + (float)sc) * 0.25f;
+    B = 0.f;
+  }
+};
+
+template <> struct Fast<T_IQ2_S> {
+  static constexpr int UNIT = 16, GRID = 1024 * 8, TAB_BYTES = GRID + 256 * 8;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
+    copy_grid<T_IQ2_S>(tab, tid, nthr);
+    build_smask(tab + GRID, tid, nthr);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const int i = 4 * c32 + tq;
+    const uint32_t h = (b[66 + (i >> 2)] >> (2 * (i & 3))) & 3u;
+    const uint2 g = lds64(tab + 8 * (b[2 + i] | (h << 8)));
+    const uint2 m = lds64(tab + GRID + 8 * b[34 + i]);
+    lo = g.x; hi = g.y;
+    apply_sign(lo, hi, m);
+  }
+  __device__ static void affine(const uint8_t* b, int s, float& S, float& B) {
+    const uint32_t sc = (b[74 + (s >> 1)] >> (4 * (s & 1))) & 15u;
+    S = h2f_bits(ld16a2(b)) * (0.5f + (float)sc) * 0.25f;
+    B = 0.f;
+  }
+};
+
+template <> struct Fast<T_IQ3_XXS> {
+  static constexpr int UNIT = 32, GRID = 256 * 4, TAB_BYTES = GRID + 128 * 8;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
+    copy_grid<T_IQ3_XXS>(tab, tid, nthr);
+    build_kmask(tab + GRID, tid, nthr);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const uint32_t idx = ld16a2(b + 2 + 8 * c32 + 2 * tq);
+    const uint32_t aux = ld32a2(b + 66 + 4 * c32);
+    lo = lds32(tab + 4 * (idx & 255u));
+    hi = lds32(tab + 4 * (idx >> 8));
+    apply_sign(lo, hi, lds64(tab + GRID + 8 * ((aux >> (7 * tq)) & 127u)));
+  }
+  __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
+    const uint32_t aux = ld32a2(b + 66 + 4 * g);
+    S = h2f_bits(ld16a2(b)) * (0.5f + (float)(aux >> 28)) * 0.5f;
+    B = 0.f;
+  }
+};
+
+template <> struct Fast<T_IQ3_S> {
+  static constexpr int UNIT = 32, GRID = 512 * 4, TAB_BYTES = GRID + 256 * 8;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
+    copy_grid<T_IQ3_S>(tab, tid, nthr);
+    build_smask(tab + GRID, tid, nthr);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const uint32_t idx = ld16a2(b + 2 + 8 * c32 + 2 * tq);
+    const uint32_t qh = b[66 + c32] >> (2 * tq);
+    lo = lds32(tab + 4 * ((idx & 255u) | ((qh & 1u) << 8)));
+    hi = lds32(tab + 4 * ((idx >> 8) | ((qh & 2u) << 7)));
+    apply_sign(lo, hi, lds64(tab + GRID + 8 * b[74 + 4 * c32 + tq]));
+  }
+  __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
+    const uint32_t sc = (b[106 + (g >> 1)] >> (4 * (g & 1))) & 15u;
+    S = h2f_bits(ld16a2(b)) * (float)(1u + 2u * sc);
+    B = 0.f;
+  }
+};
+
+template <> struct Fast<T_IQ1_S> {
+  static constexpr int UNIT = 32, TAB_BYTES = 2 * 2048 * 8;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { build_iq1_dual(tab, tid, nthr); }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const uint32_t qh = ld16a2(b + 34 + 2 * c32);
+    const uint32_t idx = b[2 + 4 * c32 + tq] | (((qh >> (3 * tq)) & 7u) << 8) | ((qh >> 15) << 11);
+    const uint2 g = lds64(tab + 8 * idx);
+    lo = g.x; hi = g.y;
+  }
+  __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
+    const uint32_t qh = ld16a2(b + 34 + 2 * g);
+    S = h2f_bits(ld16a2(b)) * (float)(2u * ((qh >> 12) & 7u) + 1u) * 0.125f;
+    B = 0.f;
+  }
+};
+
+template <> struct Fast<T_IQ1_M> {
+  static constexpr int UNIT = 16, TAB_BYTES = 2 * 2048 * 8;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { build_iq1_dual(tab, tid, nthr); }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const int i = 4 * c32 + tq;
+    const uint32_t hn = (b[32 + (i >> 1)] >> (4 * (i & 1))) & 15u;
+    const uint2 g = lds64(tab + 8 * (b[i] | (hn << 8)));  // bit 3 of hn selects the -1/8 half
+    lo = g.x; hi = g.y;
+  }
+  __device__ static void affine(const uint8_t* b, int s, float& S, float& B) {
+    const uint2 w = ld64a8(b + 48);
+    const uint32_t w0 = w.x & 0xFFFFu, w1 = w.x >> 16, w2 = w.y & 0xFFFFu, w3 = w.y >> 16;
+    const uint32_t dbits = ((w0 & 0xF000u) >> 12) | ((w1 & 0xF000u) >> 8) | ((w2 & 0xF000u) >> 4) | (w3 & 0xF000u);
+    const uint32_t ws = (s >> 2) == 0 ? w0 : (s >> 2) == 1 ? w1 : (s >> 2) == 2 ? w2 : w3;
+    const uint32_t sc = (ws >> (3 * (s & 3))) & 7u;
+    S = h2f_bits(dbits) * (float)(2u * sc + 1u) * 0.125f;
+    B = 0.f;
+  }
+};
+
+}  // namespace gsq

@@ -1,0 +1,36 @@
+// Host-side declarations shared by the kernel translation units and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace gsq {
+
+// Launch plan of one QMV call: grid shape, K-slicing and scratch needs.
+struct QmvPlan {
+  int bps;         // 256-blocks per K-slice
+  int slices;      // K-slices (grid.y); > 1 means partial sums + ticket fixup
+  int row_groups;  // 64-row groups (grid.x)
+  int btiles;      // activation-row tiles (grid.z)
+  int nb;          // activation rows per tile (1 or 2)
+  size_t smem;     // dynamic shared memory bytes
+  size_t workspace;  // scratch bytes (partials + tickets), 0 if slices == 1
+};
+
+QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows);
+
+// Runs QMV with `ws` as scratch (must hold plan.workspace bytes, zero-filled
+// tickets; left zero-filled on completion).
+cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int rows,
+                    void* y, int y_dtype, void* ws, const QmvPlan& p, int* err, cudaStream_t st);
+
+cudaError_t dequant_launch(int t, const uint8_t* packed, int64_t nblocks, float* out, cudaStream_t st);
+cudaError_t embed_launch(int t, const int32_t* ids, int64_t n, const uint8_t* packed, int64_t vocab, int64_t dim,
+                         void* out, int dtype, int* err, cudaStream_t st);
+cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
+                       float* y, __half* x16, int* err, cudaStream_t st, const char** why);
+size_t qmm_x16_bytes(int x_dtype, int64_t M, int64_t K);
+
+}  // namespace gsq

@@ -1,0 +1,376 @@
+// Tiled dequantize + matmul (QMM, prefill) on the 5th-gen tensor cores, sm_100a.
+//
+// Replaces the reference's tiled Metal QMM (mlx_gsq/runtime/kernels/qmm.py:
+// template _source :252-325, decode bodies :38-143, entry quantized_matmul
+// :559-594): Y[m, n] = sum_k X[m, k] * deq(W)[n, k], fp32 accumulation.
+//
+// Output tile = 128 weight rows (MMA M) x BN tokens (MMA N), K stepped 64 at
+// a time.  Warp roles in a 192-thread CTA:
+//   warp 0      producer: TMA tensor-map loads of the fp16 activation tile
+//               (128B swizzle) and 1-D bulk copies of the packed 256-weight
+//               blocks of the 128 rows into a double-buffered staging area;
+//   warp 1      allocates TMEM and issues tcgen05.mma (kind::f16, fp32 accum
+//               in TMEM) from one elected lane, committing to mbarriers;
+//   warps 2..5  decode each row's packed block once per tile into fp16 in the
+//               canonical K-major SW128 layout the MMA reads (every weight is
+//               decoded once per BN tokens), then run the epilogue
+//               (tcgen05.ld TMEM -> registers -> fp32 Y).
+// Weights are decoded to fp16, not bf16: bf16-rounded weights miss the
+// rel-L2 <= 1e-3 bar, fp16 ones pass; activations are converted to fp16 by
+// a pre-pass (exact for |x| >= 2^-14).  All waits are time-bounded.
+#include <cuda.h>
+#include <algorithm>
+
+#include "gsq_exact.cuh"
+#include "gsq_host.h"
+
+namespace gsq {
+
+constexpr int QMM_BM = 128;
+constexpr int QMM_BK = 64;
+constexpr int QMM_THREADS = 192;
+
+template <int T>
+struct QmmGeom {
+  static constexpr int BB = block_bytes(T);
+  static constexpr int PROWB = ((BB + 30) + 15) / 16 * 16;   // staged packed row stride
+  static constexpr int PSTAGE = QMM_BM * PROWB;               // one 256-block column of 128 rows
+};
+
+__host__ __device__ constexpr int qmm_stages(int bn) { return bn > 128 ? 3 : 4; }
+
+template <int T>
+__host__ __device__ constexpr size_t qmm_smem_bytes(int bn) {
+  // [A stages 16K each][B stages bn*128 each][packed 2 stages][barriers][tmem addr]
+  return 1024 /*align slack*/ + (size_t)qmm_stages(bn) * (QMM_BM * 128 + (size_t)bn * 128) +
+         2 * (size_t)QmmGeom<T>::PSTAGE + 256;
+}
+
+struct QmmArgs {
+  const uint8_t* packed;
+  int64_t N, K, M, row_bytes, packed_bytes;
+  float* y;
+  int bn;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31) == 0; }
+
+// tcgen05 wrappers ------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols) : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar)) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row atoms of 1024 B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                 // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                 // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D=f32, A=B=f16, both K-major, M=128, N=bn.
+__host__ __device__ constexpr uint32_t f16_idesc(int bn) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(QMM_BM >> 4) << 24);
+}
+
+// Store 8 fp16 values as one 16-byte chunk of a swizzled K-major row.
+__device__ __forceinline__ void st_sw128(uint8_t* tile, int row, int chunk, const float (&v)[8]) {
+  __half2 h[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+  *reinterpret_cast<uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4)) = *reinterpret_cast<const uint4*>(h);
+}
+
+template <int T>
+__global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, const __grid_constant__ CUtensorMap xmap) {
+  using G = QmmGeom<T>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int bn = a.bn;
+  const int NS = qmm_stages(bn);
+  uint8_t* astage = smem;                                     // NS x 16 KB
+  uint8_t* bstage = astage + (size_t)NS * QMM_BM * 128;       // NS x bn*128
+  uint8_t* pstage = bstage + (size_t)NS * bn * 128;           // 2 x PSTAGE
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pstage + 2 * G::PSTAGE);
+  uint64_t* full_a = bars;          // [NS]  count 4 (decoder warps)
+  uint64_t* full_b = bars + 4;      // [NS]  count 1 (TMA)
+  uint64_t* empty = bars + 8;       // [NS]  count 1 (tcgen05.commit)
+  uint64_t* pfull = bars + 12;      // [2]   count 1
+  uint64_t* pempty = bars + 14;     // [2]   count 4
+  uint64_t* accf = bars + 16;       // [1]   count 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n0 = (int64_t)blockIdx.x * QMM_BM;
+  const int m0 = blockIdx.y * bn;
+  const int nks = (int)(a.K / QMM_BK);
+  const int nkb = (int)(a.K / QK);
+  const uint32_t tcols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; s++) {
+      mbar_init(&full_a[s], 4);
+      mbar_init(&full_b[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; s++) {
+      mbar_init(&pfull[s], 1);
+      mbar_init(&pempty[s], 4);
+    }
+    mbar_init(accf, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, tcols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    const uintptr_t pbase = reinterpret_cast<uintptr_t>(a.packed);
+    const uint64_t policy = l2_policy_evict_first();
+    for (int ks = 0; ks < nks && ok; ks++) {
+      const int s = ks % NS, n = ks / NS;
+      if ((ks & 3) == 0) {
+        const int kb = ks >> 2, ps = kb & 1, pn = kb >> 1;
+        if (pn > 0) ok = mbar_wait_bounded(&pempty[ps], (uint32_t)((pn - 1) & 1), a.err);
+        if (!ok) break;
+        uint32_t bytes = 0;
+        for (int i = 0; i < 4; i++) {
+          const int r = lane + 32 * i;
+          const int64_t row = n0 + r;
+          if (row >= a.N) continue;
+          const int64_t off = row * a.row_bytes + (int64_t)kb * G::BB;
+          const int64_t end = off + G::BB;
+          const int64_t off_al = off & ~int64_t(15);
+          int64_t end_al = (end + 15) & ~int64_t(15);
+          if (end_al > a.packed_bytes) end_al = end & ~int64_t(15);
+          uint8_t* dst = pstage + (size_t)ps * G::PSTAGE + r * G::PROWB;
+          if (end_al > off_al) {
+            fence_proxy_async_smem();
+            bulk_g2s_stream(dst, reinterpret_cast<const void*>(pbase + off_al), (uint32_t)(end_al - off_al),
+                            &pfull[ps], policy);
+            bytes += (uint32_t)(end_al - off_al);
+          }
+          for (int64_t t = max(end_al, off_al); t < end; t++) dst[t - off_al] = a.packed[t];
+        }
+        const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&pfull[ps], total);
+      }
+      if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
+      if (!ok) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full_b[s], (uint32_t)bn * 128u);
+        tma_load_2d(bstage + (size_t)s * bn * 128, &xmap, ks * QMM_BK, m0, &full_b[s]);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = f16_idesc(bn);
+    for (int ks = 0; ks < nks && ok; ks++) {
+      const int s = ks % NS, n = ks / NS;
+      ok = mbar_wait_bounded(&full_a[s], (uint32_t)(n & 1), a.err) &&
+           mbar_wait_bounded(&full_b[s], (uint32_t)(n & 1), a.err);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t aaddr = smem_u32(astage + (size_t)s * QMM_BM * 128);
+        const uint32_t baddr = smem_u32(bstage + (size_t)s * bn * 128);
+#pragma unroll
+        for (int kk = 0; kk < QMM_BK / 16; kk++)
+          tc_mma_f16(tmem_d, sw128_desc(aaddr + kk * 32), sw128_desc(baddr + kk * 32), idesc,
+                     (ks | kk) != 0 ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) tc_commit(accf);
+    __syncwarp();
+  } else {
+    // ---------------- decoders + epilogue ----------------
+    const int r = 32 * (warp & 3) + lane;  // tile row == TMEM lane
+    const int64_t row = n0 + r;
+    const bool live = row < a.N;
+    const int64_t roff = row * a.row_bytes;
+    for (int kb = 0; kb < nkb && ok; kb++) {
+      const int ps = kb & 1;
+      ok = mbar_wait_bounded(&pfull[ps], (uint32_t)((kb >> 1) & 1), a.err);
+      if (!ok) break;
+      const uint8_t* blk = pstage + (size_t)ps * G::PSTAGE + r * G::PROWB + (int)((roff + (int64_t)kb * G::BB) & 15);
+      for (int q = 0; q < 4 && ok; q++) {
+        const int ks = 4 * kb + q, s = ks % NS, n = ks / NS;
+        if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
+        if (!ok) break;
+        uint8_t* tile = astage + (size_t)s * QMM_BM * 128;
+#pragma unroll 2
+        for (int c = 0; c < 8; c++) {
+          float v[8];
+          if (live) Exact<T>::entry(blk, 8 * q + c, v);
+          else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = 0.f;
+          }
+          st_sw128(tile, r, c, v);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_a[s]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[ps]);
+    }
+    // epilogue
+    if (ok) ok = mbar_wait_bounded(accf, 0u, a.err);
+    tc_fence_after();
+    if (ok) {
+      const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+      for (int j0 = 0; j0 < bn; j0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem_d + lane_base + (uint32_t)j0, v);
+        if (live) {
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++) {
+            const int64_t m = (int64_t)m0 + j0 + jj;
+            if (m < a.M) a.y[m * a.N + row] = __uint_as_float(v[jj]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem_d, tcols);
+}
+
+// Activations -> fp16 (row-major [M, K]); the tensor map reads this copy.
+__global__ void to_f16_kernel(const void* x, int dtype, int64_t n, __half* out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = __float2half_rn(load_act(x, dtype, i));
+}
+
+// --------------------------------------------------------------------------
+// Host side.
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int qmm_pick_bn(int64_t M) {
+  if (M <= 16) return 16;
+  if (M <= 256) return (int)((M + 15) / 16 * 16);
+  return 128;
+}
+
+size_t qmm_x16_bytes(int x_dtype, int64_t M, int64_t K) {
+  return x_dtype == DT_F16 ? 0 : (size_t)(((M * K * 2) + 255) / 256 * 256);
+}
+
+#define GSQ_QMM_SMEM_CASE(TT) case TT: return qmm_smem_bytes<TT>(bn);
+size_t qmm_smem(int t, int bn) {
+  switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMM_SMEM_CASE) }
+  return 0;
+}
+
+template <int T>
+static cudaError_t qmm_launch_t(const QmmArgs& a, const CUtensorMap& map, cudaStream_t st) {
+  const size_t smem = qmm_smem_bytes<T>(a.bn);
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && configured[dev] < (int)smem) {
+    cudaError_t e = cudaFuncSetAttribute(qmm_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = (int)smem;
+  }
+  dim3 grid((unsigned)((a.N + QMM_BM - 1) / QMM_BM), (unsigned)((a.M + a.bn - 1) / a.bn));
+  qmm_kernel<T><<<grid, QMM_THREADS, smem, st>>>(a, map);
+  return cudaGetLastError();
+}
+
+#define GSQ_QMM_LAUNCH_CASE(TT) case TT: return qmm_launch_t<TT>(a, map, st);
+
+// x16 must hold M*K fp16 values (16-byte aligned); it may alias x when x is fp16.
+cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
+                       float* y, __half* x16, int* err, cudaStream_t st, const char** why) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) { *why = "cuTensorMapEncodeTiled unavailable"; return cudaErrorNotSupported; }
+  if (x_dtype != DT_F16) {
+    const int64_t n = M * K;
+    const int grid = (int)std::min<int64_t>((n + 255) / 256, 148 * 32);
+    to_f16_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, x16);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  } else {
+    x16 = reinterpret_cast<__half*>(const_cast<void*>(x));
+  }
+  QmmArgs a;
+  a.packed = packed; a.N = N; a.K = K; a.M = M;
+  a.row_bytes = (K / QK) * block_bytes(t);
+  a.packed_bytes = N * a.row_bytes;
+  a.y = y; a.bn = qmm_pick_bn(M); a.err = err;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {QMM_BK, (cuuint32_t)a.bn};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, x16, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) { *why = "cuTensorMapEncodeTiled failed"; return cudaErrorInvalidValue; }
+  switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMM_LAUNCH_CASE) }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace gsq

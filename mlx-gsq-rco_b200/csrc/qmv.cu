@@ -1,0 +1,424 @@
+// Fused dequantize + matvec (QMV) over packed GGUF super-blocks, sm_100a.
+//
+// Replaces the reference's per-type Metal matvec kernels
+// (mlx_gsq/runtime/kernels/qmv.py:76-528, dispatched by quantized_matvec,
+// qmv.py:537-576).  y[b, n] = sum_k x[b, k] * deq(W)[n, k] for a few
+// activation rows b (decode), W stored as N rows of K/256 packed blocks.
+//
+// Design (B200):
+//  * Work unit = 16 weight rows x one K-slice per warp; a CTA of 4 warps owns
+//    64 rows and one K-slice, so the grid is (N/64, slices, row-pairs).  The
+//    host picks the slice count so that the grid fills the 148 SMs in one
+//    wave; partial sums of the slices are combined deterministically by the
+//    last CTA to finish a row group (an atomic ticket, no spinning).
+//  * Packed bytes stream HBM -> shared memory with 1-D bulk async copies
+//    (one per weight row and chunk, issued by 16 lanes in parallel) into a
+//    3-stage per-warp ring completed on mbarriers; waits are time-bounded.
+//  * Activations are quantised once per CTA into two int8 levels per 32-wide
+//    group (x ~= s * (hi + lo/256)), so each weight is decoded to an int8
+//    value a_k (gsq_fast.cuh) and multiplied on the tensor cores with
+//    mma.sync.m16n8k32.s8 -- decode cost is a few integer ops per 8 weights.
+//  * The 8 MMA columns carry (unit, batch row, level) triples; each quad lane
+//    ends up holding the integer dot products of a different sub-block, which
+//    it scales once: acc += S_u * s_x * (256*C_hi + C_lo) + B_u * sum(x_u).
+#include <algorithm>
+
+#include "gsq_fast.cuh"
+#include "gsq_host.h"
+
+namespace gsq {
+
+constexpr int QMV_WARPS = 4;
+constexpr int QMV_ROWS = 16 * QMV_WARPS;
+constexpr int QMV_STAGES = 3;
+constexpr int QMV_THREADS = 32 * QMV_WARPS;
+constexpr int QMV_MAX_SLICE_BLOCKS = 16;
+
+struct QmvArgs {
+  const uint8_t* packed;
+  int64_t N, K, row_bytes;
+  int64_t packed_bytes;
+  const void* x;
+  int x_dtype;
+  int rows;        // activation rows
+  void* y;
+  int y_dtype;
+  int kblocks;     // K / 256
+  int bps;         // blocks per K-slice
+  int slices;
+  float* partial;  // [slices][rows_pad][N] when slices > 1
+  unsigned* tickets;
+  int* err;
+};
+
+template <int T>
+struct QmvGeom {
+  static constexpr int BB = block_bytes(T);
+  static constexpr int CB = BB > 84 ? 2 : 4;                      // blocks per chunk
+  static constexpr int ROWB = ((CB * BB + 30) + 15) / 16 * 16;     // staged row stride
+  static constexpr int STAGE = 16 * ROWB;
+  static constexpr int TAB = (Fast<T>::TAB_BYTES + 127) / 128 * 128;
+};
+
+template <int T, int NB>
+__host__ __device__ constexpr size_t qmv_smem_bytes(int bps) {
+  // tables | mbarriers | xq [NB][2][KS] | xs [NB][KS/32] | xsum [NB][KS/16] | stages
+  return (size_t)QmvGeom<T>::TAB + 128 + (size_t)NB * 2 * bps * 256 + (size_t)NB * bps * 8 * 4 +
+         (size_t)NB * bps * 16 * 4 + (size_t)QMV_WARPS * QMV_STAGES * QmvGeom<T>::STAGE + 128;
+}
+
+// Quantise the activation slice for this CTA into shared memory.
+template <int NB>
+__device__ void qmv_quantize_x(const QmvArgs& a, int k0, int ks, int ksmax, int batch0, int8_t* xq,
+                               float* xs, float* xsum) {
+  const int ng = ks / 32;
+  for (int task = threadIdx.x; task < NB * ng; task += blockDim.x) {
+    const int b = task / ng, gi = task - b * ng;
+    const int row = batch0 + b;
+    int8_t* qh = xq + (size_t)(2 * b) * ksmax + gi * 32;
+    int8_t* ql = qh + ksmax;
+    if (row >= a.rows) {
+      for (int j = 0; j < 32; j += 4) {
+        *reinterpret_cast<uint32_t*>(qh + j) = 0u;
+        *reinterpret_cast<uint32_t*>(ql + j) = 0u;
+      }
+      xs[b * (ksmax / 32) + gi] = 0.f;
+      xsum[b * (ksmax / 16) + 2 * gi] = 0.f;
+      xsum[b * (ksmax / 16) + 2 * gi + 1] = 0.f;
+      continue;
+    }
+    const int64_t base = (int64_t)row * a.K + k0 + gi * 32;
+    float v[32];
+    float amax = 0.f, s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      v[j] = load_act(a.x, a.x_dtype, base + j);
+      amax = fmaxf(amax, fabsf(v[j]));
+      if (j < 16) s0 += v[j]; else s1 += v[j];
+    }
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      uint32_t wh = 0, wl = 0;
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        const float u = v[j + t] * inv;
+        const float h = fminf(fmaxf(rintf(u), -127.f), 127.f);
+        const float l = fminf(fmaxf(rintf((u - h) * 256.f), -127.f), 127.f);
+        wh |= ((uint32_t)(uint8_t)(int8_t)(int)h) << (8 * t);
+        wl |= ((uint32_t)(uint8_t)(int8_t)(int)l) << (8 * t);
+      }
+      *reinterpret_cast<uint32_t*>(qh + j) = wh;
+      *reinterpret_cast<uint32_t*>(ql + j) = wl;
+    }
+    xs[b * (ksmax / 32) + gi] = amax / (127.f * 256.f);
+    xsum[b * (ksmax / 16) + 2 * gi] = s0;
+    xsum[b * (ksmax / 16) + 2 * gi + 1] = s1;
+  }
+}
+
+template <int T, int NB>
+__global__ void __launch_bounds__(QMV_THREADS) qmv_kernel(const QmvArgs a) {
+  using F = Fast<T>;
+  using G = QmvGeom<T>;
+  constexpr int UNIT = F::UNIT;
+  constexpr int UPS = 4 / NB;            // units per set
+  constexpr int KSET = UNIT * UPS;       // k per set
+  constexpr int MMAS = KSET / 32;        // MMAs per set
+  constexpr int SETS = QK / KSET;        // sets per block
+  static_assert(MMAS >= 1, "set must cover at least one MMA");
+  static_assert(F::BLOCKED || UNIT == 32, "identity mapping needs 32-wide units");
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int ksmax = a.bps * QK;
+  uint8_t* tab = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::TAB);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + G::TAB + 128);
+  float* xs = reinterpret_cast<float*>(xq + (size_t)NB * 2 * ksmax);
+  float* xsum = xs + NB * (ksmax / 32);
+  uint8_t* stages = reinterpret_cast<uint8_t*>(xsum + NB * (ksmax / 16));
+  stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(stages) + 127) & ~uintptr_t(127));
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int row_group = blockIdx.x, slice = blockIdx.y, btile = blockIdx.z;
+  const int64_t row0 = (int64_t)row_group * QMV_ROWS + warp * 16;
+  const int blk0 = slice * a.bps;
+  const int nblk = min(a.bps, a.kblocks - blk0);
+  const int nchunks = (nblk + G::CB - 1) / G::CB;
+  uint64_t* wbars = bars + warp * QMV_STAGES;
+  uint8_t* wstage = stages + (size_t)warp * QMV_STAGES * G::STAGE;
+  const uintptr_t pbase = reinterpret_cast<uintptr_t>(a.packed);
+  const uint64_t policy = l2_policy_evict_first();
+
+  if (lane == 0)
+    for (int s = 0; s < QMV_STAGES; s++) mbar_init(&wbars[s], 1);
+  fence_mbar_init();
+  __syncwarp();
+
+  // Stage chunk c of this warp's 16 rows: lanes 0..15 each copy one row span.
+  auto issue = [&](int c) {
+    const int s = c % QMV_STAGES;
+    uint32_t bytes = 0;
+    if (lane < 16) {
+      const int64_t r = row0 + lane;
+      if (r < a.N) {
+        const int nb_c = min(G::CB, nblk - c * G::CB);
+        const int64_t off = r * a.row_bytes + (int64_t)(blk0 + c * G::CB) * G::BB;
+        const int64_t end = off + (int64_t)nb_c * G::BB;
+        const int64_t off_al = off & ~int64_t(15);
+        int64_t end_al = (end + 15) & ~int64_t(15);
+        if (end_al > a.packed_bytes) end_al = end & ~int64_t(15);
+        uint8_t* dst = wstage + (size_t)s * G::STAGE + lane * G::ROWB;
+        if (end_al > off_al) {
+          bytes = (uint32_t)(end_al - off_al);
+          fence_proxy_async_smem();
+          bulk_g2s_stream(dst, reinterpret_cast<const void*>(pbase + off_al), bytes, &wbars[s], policy);
+        }
+        // Tail beyond the last 16-byte boundary of the buffer: plain loads.
+        for (int64_t t = max(end_al, off_al); t < end; t++) dst[t - off_al] = a.packed[t];
+      }
+    }
+    const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
+    __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(&wbars[s], total);
+  };
+
+  const int npro = min(QMV_STAGES, nchunks);
+  for (int c = 0; c < npro; c++) issue(c);
+
+  F::load_tables(tab, threadIdx.x, blockDim.x);
+  qmv_quantize_x<NB>(a, blk0 * QK, nblk * QK, ksmax, btile * NB, xq, xs, xsum);
+  __syncthreads();
+
+  // Per-thread constants of the activation operand (column g of the MMA).
+  const int pcol = g >> 1, level = g & 1;
+  const int s_col = pcol / NB, b_col = pcol % NB;
+  const int8_t* xrow = xq + (size_t)(2 * b_col + level) * ksmax;
+  // Epilogue identity of this lane: unit s_ep of each set, activation row b_ep.
+  const int s_ep = tq / NB, b_ep = tq % NB;
+  const float* xs_row = xs + b_ep * (ksmax / 32);
+  const float* xsum_row = xsum + b_ep * (ksmax / 16);
+
+  const int64_t roff0 = (row0 + g) * a.row_bytes + (int64_t)blk0 * G::BB;
+  const int64_t roff1 = (row0 + g + 8) * a.row_bytes + (int64_t)blk0 * G::BB;
+
+  float acc0 = 0.f, acc1 = 0.f;
+  bool ok = true;
+  int waited = 0;
+  for (int c = 0; c < nchunks && ok; c++) {
+    const int s = c % QMV_STAGES;
+    ok = mbar_wait_bounded(&wbars[s], (uint32_t)((c / QMV_STAGES) & 1), a.err);
+    if (!ok) break;
+    waited = c + 1;
+    const int nb_c = min(G::CB, nblk - c * G::CB);
+    const int64_t coff = (int64_t)c * G::CB * G::BB;
+    const uint8_t* st = wstage + (size_t)s * G::STAGE;
+    const uint8_t* r0p = st + g * G::ROWB + (int)((roff0 + coff) & 15);
+    const uint8_t* r1p = st + (g + 8) * G::ROWB + (int)((roff1 + coff) & 15);
+    for (int bi = 0; bi < nb_c; bi++) {
+      const uint8_t* b0 = r0p + bi * G::BB;
+      const uint8_t* b1 = r1p + bi * G::BB;
+      const int kblk = (c * G::CB + bi) * QK;
+#pragma unroll
+      for (int set = 0; set < SETS; set++) {
+        const int kset = kblk + set * KSET;
+        // Activation words for the one MMA of this set where column g is live.
+        uint32_t xw0, xw1;
+        int jsel;
+        bool live;
+        if constexpr (UNIT == 32) {
+          jsel = s_col;
+          live = true;
+          if constexpr (F::BLOCKED) {
+            const uint2 w = lds64(reinterpret_cast<const uint8_t*>(xrow + kset + 32 * s_col + 8 * tq));
+            xw0 = w.x; xw1 = w.y;
+          } else {
+            xw0 = lds32(reinterpret_cast<const uint8_t*>(xrow + kset + 32 * s_col + 4 * tq));
+            xw1 = lds32(reinterpret_cast<const uint8_t*>(xrow + kset + 32 * s_col + 16 + 4 * tq));
+          }
+        } else {
+          jsel = s_col >> 1;
+          live = (s_col & 1) == (tq >> 1);
+          const uint2 w = lds64(reinterpret_cast<const uint8_t*>(xrow + kset + 32 * jsel + 8 * tq));
+          xw0 = live ? w.x : 0u;
+          xw1 = live ? w.y : 0u;
+        }
+        int C[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int j = 0; j < MMAS; j++) {
+          const int c32 = set * MMAS + j;
+          uint32_t a0, a1, a2, a3;
+          F::entry(b0, c32, tq, tab, a0, a2);
+          F::entry(b1, c32, tq, tab, a1, a3);
+          const bool on = (j == jsel);
+          mma_s8(C, a0, a1, a2, a3, on ? xw0 : 0u, on ? xw1 : 0u);
+        }
+        (void)live;
+        const int unit = set * UPS + s_ep;
+        const int ku = kblk + unit * UNIT;
+        const float xsv = xs_row[ku >> 5];
+        float S0, B0, S1, B1;
+        F::affine(b0, unit, S0, B0);
+        F::affine(b1, unit, S1, B1);
+        const float d0 = (float)(C[0] * 256 + C[1]) * xsv;
+        const float d1 = (float)(C[2] * 256 + C[3]) * xsv;
+        acc0 = fmaf(S0, d0, acc0);
+        acc1 = fmaf(S1, d1, acc1);
+        if constexpr (F::HAS_BIAS) {
+          float xu = xsum_row[ku >> 4];
+          if constexpr (UNIT == 32) xu += xsum_row[(ku >> 4) + 1];
+          acc0 = fmaf(B0, xu, acc0);
+          acc1 = fmaf(B1, xu, acc1);
+        }
+      }
+    }
+    __syncwarp();
+    if (c + QMV_STAGES < nchunks) issue(c + QMV_STAGES);
+  }
+  if (!ok) {
+    // Drain the copies this warp still has in flight before the CTA exits.
+    for (int c = waited; c < min(nchunks, waited + QMV_STAGES); c++)
+      mbar_wait_bounded(&wbars[c % QMV_STAGES], (uint32_t)((c / QMV_STAGES) & 1), nullptr);
+  }
+
+  // Sum the quad lanes that hold the same activation row.
+  if constexpr (NB == 1) {
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+  }
+  acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+  acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+
+  const int batch = btile * NB + b_ep;
+  const int64_t rg0 = row0 + g, rg1 = row0 + g + 8;
+  const bool writer = ok && tq < NB && batch < a.rows;
+  if (a.slices == 1) {
+    if (writer) {
+      if (rg0 < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rg0, acc0);
+      if (rg1 < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rg1, acc1);
+    }
+    return;
+  }
+  const int rows_pad = gridDim.z * NB;
+  if (writer) {
+    float* p = a.partial + ((int64_t)slice * rows_pad + batch) * a.N;
+    if (rg0 < a.N) p[rg0] = acc0;
+    if (rg1 < a.N) p[rg1] = acc1;
+  }
+  __shared__ int s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned t = atomicAdd(&a.tickets[row_group * gridDim.z + btile], 1u);
+    s_last = (t == (unsigned)(a.slices - 1));
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < QMV_ROWS * NB; i += blockDim.x) {
+    const int b = i / QMV_ROWS;
+    const int64_t r = (int64_t)row_group * QMV_ROWS + (i - b * QMV_ROWS);
+    const int bt = btile * NB + b;
+    if (r >= a.N || bt >= a.rows) continue;
+    float sum = 0.f;
+    for (int sl = 0; sl < a.slices; sl++) sum += __ldcg(a.partial + ((int64_t)sl * rows_pad + bt) * a.N + r);
+    store_out(a.y, a.y_dtype, (int64_t)bt * a.N + r, sum);
+  }
+  if (threadIdx.x == 0) a.tickets[row_group * gridDim.z + btile] = 0u;
+}
+
+// --------------------------------------------------------------------------
+// Host side.
+
+template <int T, int NB>
+static size_t qmv_smem(int bps) { return qmv_smem_bytes<T, NB>(bps); }
+
+static int qmv_pick_bps(int64_t N, int kblocks) {
+  const int64_t row_groups = (N + QMV_ROWS - 1) / QMV_ROWS;
+  const int64_t target = 2 * 148;
+  int slices = (int)std::min<int64_t>(std::max<int64_t>(1, (target + row_groups - 1) / row_groups), kblocks);
+  slices = std::max(slices, (kblocks + QMV_MAX_SLICE_BLOCKS - 1) / QMV_MAX_SLICE_BLOCKS);
+  int bps = (kblocks + slices - 1) / slices;
+  return bps;
+}
+
+#define GSQ_QMV_SMEM_CASE(TT)                                                   \
+  case TT:                                                                      \
+    return nb == 1 ? qmv_smem<TT, 1>(bps) : qmv_smem<TT, 2>(bps);
+
+static size_t qmv_smem_dispatch(int t, int nb, int bps) {
+  switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMV_SMEM_CASE) }
+  return 0;
+}
+
+QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
+  QmvPlan p;
+  const int kblocks = (int)(K / QK);
+  p.nb = rows == 1 ? 1 : 2;
+  p.btiles = (rows + p.nb - 1) / p.nb;
+  p.row_groups = (int)((N + QMV_ROWS - 1) / QMV_ROWS);
+  p.bps = qmv_pick_bps(N, kblocks);
+  p.slices = (kblocks + p.bps - 1) / p.bps;
+  p.smem = qmv_smem_dispatch(t, p.nb, p.bps);
+  p.workspace = 0;
+  if (p.slices > 1) {
+    const size_t partial = (size_t)p.slices * p.btiles * p.nb * N * sizeof(float);
+    p.workspace = ((partial + 255) / 256) * 256 + (size_t)p.row_groups * p.btiles * sizeof(unsigned);
+  }
+  return p;
+}
+
+template <int T, int NB>
+static cudaError_t qmv_launch_t(const QmvArgs& a, const QmvPlan& p, cudaStream_t st) {
+  auto kern = qmv_kernel<T, NB>;
+  static int configured[64] = {0};  // max dynamic smem already set, per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || (int)p.smem > configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = (int)p.smem;
+  }
+  dim3 grid(p.row_groups, p.slices, p.btiles);
+  kern<<<grid, QMV_THREADS, p.smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+#define GSQ_QMV_LAUNCH_CASE(TT) \
+  case TT:                      \
+    return p.nb == 1 ? qmv_launch_t<TT, 1>(a, p, st) : qmv_launch_t<TT, 2>(a, p, st);
+
+static cudaError_t qmv_launch(int t, const QmvArgs& a, const QmvPlan& p, cudaStream_t st) {
+  switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMV_LAUNCH_CASE) }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int rows,
+                    void* y, int y_dtype, void* ws, const QmvPlan& p, int* err, cudaStream_t st) {
+  QmvArgs a;
+  a.packed = packed;
+  a.N = N;
+  a.K = K;
+  a.row_bytes = (K / QK) * block_bytes(t);
+  a.packed_bytes = N * a.row_bytes;
+  a.x = x;
+  a.x_dtype = x_dtype;
+  a.rows = rows;
+  a.y = y;
+  a.y_dtype = y_dtype;
+  a.kblocks = (int)(K / QK);
+  a.bps = p.bps;
+  a.slices = p.slices;
+  a.partial = nullptr;
+  a.tickets = nullptr;
+  if (p.slices > 1) {
+    const size_t partial = (size_t)p.slices * p.btiles * p.nb * N * sizeof(float);
+    a.partial = static_cast<float*>(ws);
+    a.tickets = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + ((partial + 255) / 256) * 256);
+  }
+  a.err = err;
+  return qmv_launch(t, a, p, st);
+}
+
+}  // namespace gsq

@@ -1,0 +1,76 @@
+"""The C-ABI library loads, exports every entry point include/gsq_b200.h
+declares, and validates arguments before touching the GPU (these calls only
+exercise host-side validation; no kernel is launched)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from gsq_b200 import _lib
+from gsq_b200.quant.layouts import QUANT_BLOCK_SIZES, SUPPORTED_QUANT_TYPES, type_id
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "gsq_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    return re.findall(r"GSQ_API\s+[\w\s\*]+?\b(gsq_\w+)\s*\(", src)
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    assert set(names) == set(_lib.SIGNATURES), names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    nm = os.popen(f"nm -D --defined-only {_lib.LIB_PATH}").read()
+    for name in declared_functions():
+        assert re.search(rf"\bT {name}\b", nm), name
+
+
+def test_version_and_block_info():
+    lib = _lib.load()
+    assert b"sm_100a" in lib.gsq_version()
+    e, b = ctypes.c_int(), ctypes.c_int()
+    for q in SUPPORTED_QUANT_TYPES:
+        assert lib.gsq_block_info(type_id(q), ctypes.byref(e), ctypes.byref(b)) == 0
+        assert (e.value, b.value) == QUANT_BLOCK_SIZES[type_id(q)]
+    assert lib.gsq_block_info(2, None, None) == _lib.GSQ_ERR_QTYPE  # Q4_0 is not a hot-path type
+    assert "unsupported" in _lib.last_error()
+
+
+def test_validation_errors_before_any_launch():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(1 << 20)
+    q4k = type_id("Q4_K")
+    assert lib.gsq_qmv(2, fake, 0, fake, 16, 256, 1, fake, 0, None, 0, None) == _lib.GSQ_ERR_QTYPE
+    assert lib.gsq_qmv(q4k, fake, 0, fake, 16, 300, 1, fake, 0, None, 0, None) == _lib.GSQ_ERR_SIZE
+    assert lib.gsq_qmv(q4k, fake, 0, None, 16, 256, 1, fake, 0, None, 0, None) == _lib.GSQ_ERR_ARG
+    assert lib.gsq_qmv(q4k, fake, 0, ctypes.c_void_p((1 << 20) + 8), 16, 256, 1, fake, 0, None, 0, None) \
+        == _lib.GSQ_ERR_ALIGN
+    assert lib.gsq_qmv(q4k, fake, 7, fake, 16, 256, 1, fake, 0, None, 0, None) == _lib.GSQ_ERR_ARG
+    # split-K shapes need a workspace
+    need = lib.gsq_qmv_workspace_size(q4k, 5120, 5120, 1)
+    assert need > 0
+    assert lib.gsq_qmv(q4k, fake, 1, fake, 5120, 5120, 1, fake, 0, None, 0, None) == _lib.GSQ_ERR_WORKSPACE
+    assert lib.gsq_qmm(q4k, fake, 2, fake, 16, 256, 4, fake, None, 0, None) == _lib.GSQ_ERR_WORKSPACE
+    assert lib.gsq_qmm(q4k, ctypes.c_void_p((1 << 20) + 4), 1, fake, 16, 256, 4, fake, None, 0, None) \
+        == _lib.GSQ_ERR_ALIGN
+    assert lib.gsq_embed(q4k, fake, 3, fake, 10, 100, fake, 1, None) == _lib.GSQ_ERR_SIZE
+    assert lib.gsq_dequant(99, fake, 1, fake, None) == _lib.GSQ_ERR_QTYPE
+    # empty work is a no-op success
+    assert lib.gsq_qmv(q4k, fake, 0, fake, 16, 256, 0, fake, 0, None, 0, None) == 0
+    assert lib.gsq_dequant(q4k, fake, 0, fake, None) == 0
+
+
+def test_workspace_sizes_are_plain_host_math():
+    lib = _lib.load()
+    for q in SUPPORTED_QUANT_TYPES:
+        t = type_id(q)
+        assert lib.gsq_qmv_workspace_size(t, 17408, 5120, 1) >= 0
+        assert lib.gsq_qmm_workspace_size(t, 17408, 5120, 512, 2) == 512 * 5120 * 2
+        assert lib.gsq_qmm_workspace_size(t, 17408, 5120, 512, 1) == 0

@@ -1,0 +1,64 @@
+"""Tiled dequantize + matmul on tcgen05 (gsq_qmm) vs the oracle.
+
+Mirrors the reference's tests/test_all_qmm.py:41-57 (rows 8/16/33, an fp16
+input case, tolerance rtol=2e-3, atol=2e-3*max|expected|) plus the primary
+rel-L2 <= 1e-3 bar, ragged shapes and the BASELINE config-3 shapes."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import REL_L2, cuda, dense_gpu, random_packed_gpu, rel_l2
+from gsq_b200.quant.layouts import SUPPORTED_QUANT_TYPES
+from gsq_b200.quant.synthetic import random_activations, random_matrix
+from gsq_b200.runtime.kernels import quantized_matmul
+
+pytestmark = pytest.mark.gpu
+
+N, K = 4, 512
+
+
+def _check(actual, expected):
+    actual = np.asarray(actual, dtype=np.float64)
+    assert rel_l2(actual, expected) <= REL_L2
+    np.testing.assert_allclose(actual, expected, rtol=2e-3, atol=2e-3 * np.abs(expected).max())
+
+
+@pytest.mark.parametrize("qtype", SUPPORTED_QUANT_TYPES)
+@pytest.mark.parametrize("rows", [8, 33])
+def test_qmm_golden(qtype, rows, golden):
+    x = cuda(golden[f"x{rows}"].astype(np.float32))
+    y = quantized_matmul(x, cuda(golden[f"{qtype}/packed"]), qtype=qtype, out_features=N, in_features=K)
+    _check(y.cpu(), golden[f"{qtype}/y{rows}"])
+
+
+def test_qmm_fp16_input(golden):
+    x = cuda(golden["x8"])  # fp16 in, fp16 out like the reference
+    y = quantized_matmul(x, cuda(golden["Q4_K/packed"]), qtype="Q4_K", out_features=N, in_features=K,
+                         out_dtype=torch.float32)
+    _check(y.cpu(), golden["Q4_K/y8"])
+
+
+@pytest.mark.parametrize("qtype", SUPPORTED_QUANT_TYPES)
+@pytest.mark.parametrize("m", [2, 16, 33, 182])
+@pytest.mark.parametrize("nk", [(128, 512), (200, 768), (384, 2048)])
+def test_qmm_shapes(qtype, m, nk, oracle_mod):
+    n, k = nk
+    packed = random_matrix(qtype, n, k, seed=n * 7 + k)
+    for xdt in (torch.bfloat16, torch.float16, torch.float32):
+        x = torch.from_numpy(random_activations(m, k, seed=m)).to(xdt)
+        y = quantized_matmul(x.cuda(), cuda(packed), qtype=qtype, out_features=n, in_features=k,
+                             out_dtype=torch.float32)
+        exp = oracle_mod.matmul_c(x.float().numpy(), packed, qtype, n, k)
+        _check(y.cpu(), exp)
+
+
+@pytest.mark.parametrize("qtype", ["IQ2_XS", "IQ3_S", "IQ4_XS", "Q6_K"])
+@pytest.mark.parametrize("nk", [(17408, 5120), (5120, 17408)])
+@pytest.mark.parametrize("m", [16, 512])
+def test_qmm_config3(qtype, nk, m):
+    n, k = nk
+    packed = random_packed_gpu(qtype, n, k, seed=m + n)
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    y = quantized_matmul(x, packed, qtype=qtype, out_features=n, in_features=k, out_dtype=torch.float32)
+    exp = x.double() @ dense_gpu(packed, qtype, n, k).T
+    assert rel_l2(y.cpu(), exp.cpu()) <= REL_L2
