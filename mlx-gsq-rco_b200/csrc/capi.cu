@@ -101,7 +101,8 @@ int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_
   if (rows == 0 || N == 0) return GSQ_OK;
   if (!x || !y) return fail(GSQ_ERR_ARG, "null x or y");
   if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(GSQ_ERR_ARG, "unsupported dtype");
-  if (!aligned(x, dtype_size(x_dtype)) || !aligned(y, dtype_size(y_dtype))) return fail(GSQ_ERR_ALIGN, "x/y misaligned");
+  if (!aligned(x, 16) || !aligned(y, dtype_size(y_dtype)))
+    return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned and y aligned to its dtype");
   const QmvPlan p = qmv_plan(qtype, N, K, (int)rows);
   if (p.workspace > 0 && (!workspace || workspace_bytes < p.workspace || !aligned(workspace, 256)))
     return fail(GSQ_ERR_WORKSPACE, "gsq_qmv needs %zu workspace bytes (256-byte aligned), got %zu", p.workspace,

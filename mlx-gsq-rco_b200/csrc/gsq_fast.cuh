@@ -35,14 +35,6 @@
 
 namespace gsq {
 
-// Expand the low 8 bits of s into a byte mask (byte j = 0xFF if bit j set).
-__host__ __device__ inline uint64_t expand_sign_mask(uint32_t s) {
-  uint64_t m = 0;
-  for (int j = 0; j < 8; j++)
-    if ((s >> j) & 1u) m |= (uint64_t)0xFF << (8 * j);
-  return m;
-}
-
 // Negate the bytes of (lo, hi) selected by the mask.  Magnitudes are >= 1, so
 // (v ^ 0xFF) + 1 == -v never carries into the neighbouring byte.
 __device__ __forceinline__ void apply_sign(uint32_t& lo, uint32_t& hi, uint2 m) {
@@ -55,36 +47,20 @@ __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpre
 
 template <int T> struct Fast;
 
-// Shared table builders -------------------------------------------------------
-template <int T>
-__device__ void copy_grid(uint8_t* dst, int tid, int nthr) {
-  constexpr int n = GridOf<T>::entries * GridOf<T>::width;
-  const uint32_t* src = reinterpret_cast<const uint32_t*>(GridOf<T>::ptr());
-  uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-  for (int i = tid; i < n / 4; i += nthr) d[i] = src[i];
-}
+// Derived lookup tables, generated at build time from the gguf-py codebooks.
+// kKmask128[i]: 8 byte masks (0xFF = negate) for ksigns index i (parity folded in).
+// kSmask256[s]: 8 byte masks for an explicit sign byte s.
+// kIq1Dual: IQ1 grid x 8 with the +1/8 delta folded in (first 2048 entries)
+//           and with -1/8 (next 2048 entries).
+static __device__ __align__(16) const uint8_t kKmask128[128 * 8] = GSQ_INIT_KMASK128;
+static __device__ __align__(16) const uint8_t kSmask256[256 * 8] = GSQ_INIT_SMASK256;
+static __device__ __align__(16) const int8_t kIq1Dual[2 * 2048 * 8] = GSQ_INIT_IQ1_DUAL;
 
-// 128-entry mask table indexed by the 7-bit ksigns index (parity bit folded in).
-__device__ inline void build_kmask(uint8_t* dst, int tid, int nthr) {
-  uint64_t* d = reinterpret_cast<uint64_t*>(dst);
-  for (int i = tid; i < 128; i += nthr) d[i] = expand_sign_mask(kKsigns[i]);
-}
-
-// 256-entry mask table indexed by an explicit sign byte.
-__device__ inline void build_smask(uint8_t* dst, int tid, int nthr) {
-  uint64_t* d = reinterpret_cast<uint64_t*>(dst);
-  for (int i = tid; i < 256; i += nthr) d[i] = expand_sign_mask((uint32_t)i);
-}
-
-// IQ1 grid premultiplied by 8 with the +-1/8 delta folded in: half 0 holds
-// 8*g + 1 (delta +0.125), half 1 holds 8*g - 1 (delta -0.125).
-__device__ inline void build_iq1_dual(uint8_t* dst, int tid, int nthr) {
-  int8_t* d = reinterpret_cast<int8_t*>(dst);
-  for (int i = tid; i < 2048 * 8; i += nthr) {
-    const int g = kGridIQ1S[i];
-    d[i] = (int8_t)(8 * g + 1);
-    d[2048 * 8 + i] = (int8_t)(8 * g - 1);
-  }
+// Copy a 16-byte aligned table into shared memory with 16-byte accesses.
+__device__ __forceinline__ void copy16(uint8_t* dst, const void* src, int bytes, int tid, int nthr) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  for (int i = tid; i < bytes / 16; i += nthr) d[i] = s[i];
 }
 
 // --- K-quants ----------------------------------------------------------------
@@ -165,7 +141,7 @@ template <> struct Fast<T_IQ4_XS> {
   static constexpr int UNIT = 32, TAB_BYTES = 16;
   static constexpr bool BLOCKED = false, HAS_BIAS = false;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    for (int i = tid; i < 16; i += nthr) tab[i] = (uint8_t)kKvalues[i];
+    copy16(tab, kKvalues, 16, tid, nthr);
   }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const uint4 kv = *reinterpret_cast<const uint4*>(tab);
@@ -190,8 +166,8 @@ template <> struct Fast<T_IQ2_XXS> {
   static constexpr int UNIT = 32, GRID = 256 * 8, TAB_BYTES = GRID + 128 * 8;
   static constexpr bool BLOCKED = true, HAS_BIAS = false;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy_grid<T_IQ2_XXS>(tab, tid, nthr);
-    build_kmask(tab + GRID, tid, nthr);
+    copy16(tab, kGridIQ2XXS, GRID, tid, nthr);
+    copy16(tab + GRID, kKmask128, 128 * 8, tid, nthr);
   }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const uint8_t* q = b + 2 + 8 * c32;
@@ -212,8 +188,8 @@ template <> struct Fast<T_IQ2_XS> {
   static constexpr int UNIT = 16, GRID = 512 * 8, TAB_BYTES = GRID + 128 * 8;
   static constexpr bool BLOCKED = true, HAS_BIAS = false;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy_grid<T_IQ2_XS>(tab, tid, nthr);
-    build_kmask(tab + GRID, tid, nthr);
+    copy16(tab, kGridIQ2XS, GRID, tid, nthr);
+    copy16(tab + GRID, kKmask128, 128 * 8, tid, nthr);
   }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const uint32_t q = ld16a2(b + 2 + 2 * (4 * c32 + tq));
@@ -233,8 +209,8 @@ template <> struct Fast<T_IQ2_S> {
   static constexpr int UNIT = 16, GRID = 1024 * 8, TAB_BYTES = GRID + 256 * 8;
   static constexpr bool BLOCKED = true, HAS_BIAS = false;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy_grid<T_IQ2_S>(tab, tid, nthr);
-    build_smask(tab + GRID, tid, nthr);
+    copy16(tab, kGridIQ2S, GRID, tid, nthr);
+    copy16(tab + GRID, kSmask256, 256 * 8, tid, nthr);
   }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const int i = 4 * c32 + tq;
@@ -255,8 +231,8 @@ template <> struct Fast<T_IQ3_XXS> {
   static constexpr int UNIT = 32, GRID = 256 * 4, TAB_BYTES = GRID + 128 * 8;
   static constexpr bool BLOCKED = true, HAS_BIAS = false;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy_grid<T_IQ3_XXS>(tab, tid, nthr);
-    build_kmask(tab + GRID, tid, nthr);
+    copy16(tab, kGridIQ3XXS, GRID, tid, nthr);
+    copy16(tab + GRID, kKmask128, 128 * 8, tid, nthr);
   }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const uint32_t idx = ld16a2(b + 2 + 8 * c32 + 2 * tq);
@@ -276,8 +252,8 @@ template <> struct Fast<T_IQ3_S> {
   static constexpr int UNIT = 32, GRID = 512 * 4, TAB_BYTES = GRID + 256 * 8;
   static constexpr bool BLOCKED = true, HAS_BIAS = false;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy_grid<T_IQ3_S>(tab, tid, nthr);
-    build_smask(tab + GRID, tid, nthr);
+    copy16(tab, kGridIQ3S, GRID, tid, nthr);
+    copy16(tab + GRID, kSmask256, 256 * 8, tid, nthr);
   }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const uint32_t idx = ld16a2(b + 2 + 8 * c32 + 2 * tq);
@@ -296,7 +272,7 @@ template <> struct Fast<T_IQ3_S> {
 template <> struct Fast<T_IQ1_S> {
   static constexpr int UNIT = 32, TAB_BYTES = 2 * 2048 * 8;
   static constexpr bool BLOCKED = true, HAS_BIAS = false;
-  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { build_iq1_dual(tab, tid, nthr); }
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kIq1Dual, TAB_BYTES, tid, nthr); }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const uint32_t qh = ld16a2(b + 34 + 2 * c32);
     const uint32_t idx = b[2 + 4 * c32 + tq] | (((qh >> (3 * tq)) & 7u) << 8) | ((qh >> 15) << 11);
@@ -313,7 +289,7 @@ template <> struct Fast<T_IQ1_S> {
 template <> struct Fast<T_IQ1_M> {
   static constexpr int UNIT = 16, TAB_BYTES = 2 * 2048 * 8;
   static constexpr bool BLOCKED = true, HAS_BIAS = false;
-  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { build_iq1_dual(tab, tid, nthr); }
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kIq1Dual, TAB_BYTES, tid, nthr); }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const int i = 4 * c32 + tq;
     const uint32_t hn = (b[32 + (i >> 1)] >> (4 * (i & 1))) & 15u;

@@ -33,6 +33,12 @@ constexpr int QMV_ROWS = 16 * QMV_WARPS;
 constexpr int QMV_STAGES = 3;
 constexpr int QMV_THREADS = 32 * QMV_WARPS;
 constexpr int QMV_MAX_SLICE_BLOCKS = 16;
+// Split-K scratch layout: a fixed region of ticket counters first, then the
+// partial sums.  Every completed call returns the tickets it used to zero, and
+// no call ever writes partial sums over the ticket region, so one zero-filled
+// workspace can serve calls of any shape in sequence.
+constexpr int QMV_TICKET_SLOTS = 65536;
+constexpr size_t QMV_TICKET_BYTES = QMV_TICKET_SLOTS * sizeof(unsigned);
 
 struct QmvArgs {
   const uint8_t* packed;
@@ -67,8 +73,48 @@ __host__ __device__ constexpr size_t qmv_smem_bytes(int bps) {
          (size_t)NB * bps * 16 * 4 + (size_t)QMV_WARPS * QMV_STAGES * QmvGeom<T>::STAGE + 128;
 }
 
-// Quantise the activation slice for this CTA into shared memory.
-template <int NB>
+// Load 32 consecutive activations starting at element `i` (a multiple of 32;
+// the row base is 16-byte aligned) with 16-byte loads.
+template <typename XT> __device__ __forceinline__ void load32(const void* x, int64_t i, float (&v)[32]);
+template <> __device__ __forceinline__ void load32<float>(const void* x, int64_t i, float (&v)[32]) {
+  const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + i);
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const float4 f = p[j];
+    v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+  }
+}
+template <> __device__ __forceinline__ void load32<__half>(const void* x, int64_t i, float (&v)[32]) {
+  const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(x) + i);
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const uint4 u = p[j];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[t]));
+      v[8 * j + 2 * t] = f.x; v[8 * j + 2 * t + 1] = f.y;
+    }
+  }
+}
+template <> __device__ __forceinline__ void load32<__nv_bfloat16>(const void* x, int64_t i, float (&v)[32]) {
+  const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x) + i);
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const uint4 u = p[j];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      v[8 * j + 2 * t] = __uint_as_float(w[t] << 16);
+      v[8 * j + 2 * t + 1] = __uint_as_float(w[t] & 0xFFFF0000u);
+    }
+  }
+}
+
+// Quantise the activation slice for this CTA into shared memory: per 32-wide
+// group, x ~= s * (hi + lo/256) with int8 hi, lo and s = max|x|/127; also the
+// fp32 sums of each 16-wide half (for the per-unit offsets B_u).
+template <int NB, typename XT>
 __device__ void qmv_quantize_x(const QmvArgs& a, int k0, int ks, int ksmax, int batch0, int8_t* xq,
                                float* xs, float* xsum) {
   const int ng = ks / 32;
@@ -78,39 +124,40 @@ __device__ void qmv_quantize_x(const QmvArgs& a, int k0, int ks, int ksmax, int 
     int8_t* qh = xq + (size_t)(2 * b) * ksmax + gi * 32;
     int8_t* ql = qh + ksmax;
     if (row >= a.rows) {
-      for (int j = 0; j < 32; j += 4) {
-        *reinterpret_cast<uint32_t*>(qh + j) = 0u;
-        *reinterpret_cast<uint32_t*>(ql + j) = 0u;
-      }
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      reinterpret_cast<uint4*>(qh)[0] = z; reinterpret_cast<uint4*>(qh)[1] = z;
+      reinterpret_cast<uint4*>(ql)[0] = z; reinterpret_cast<uint4*>(ql)[1] = z;
       xs[b * (ksmax / 32) + gi] = 0.f;
       xsum[b * (ksmax / 16) + 2 * gi] = 0.f;
       xsum[b * (ksmax / 16) + 2 * gi + 1] = 0.f;
       continue;
     }
-    const int64_t base = (int64_t)row * a.K + k0 + gi * 32;
     float v[32];
+    load32<XT>(a.x, (int64_t)row * a.K + k0 + gi * 32, v);
     float amax = 0.f, s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; j++) {
-      v[j] = load_act(a.x, a.x_dtype, base + j);
       amax = fmaxf(amax, fabsf(v[j]));
       if (j < 16) s0 += v[j]; else s1 += v[j];
     }
     const float inv = amax > 0.f ? 127.f / amax : 0.f;
+    uint32_t wh[8], wl[8];
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      uint32_t wh = 0, wl = 0;
+    for (int j = 0; j < 8; j++) {
+      wh[j] = 0u; wl[j] = 0u;
 #pragma unroll
       for (int t = 0; t < 4; t++) {
-        const float u = v[j + t] * inv;
+        const float u = v[4 * j + t] * inv;
         const float h = fminf(fmaxf(rintf(u), -127.f), 127.f);
         const float l = fminf(fmaxf(rintf((u - h) * 256.f), -127.f), 127.f);
-        wh |= ((uint32_t)(uint8_t)(int8_t)(int)h) << (8 * t);
-        wl |= ((uint32_t)(uint8_t)(int8_t)(int)l) << (8 * t);
+        wh[j] |= ((uint32_t)(uint8_t)(int8_t)(int)h) << (8 * t);
+        wl[j] |= ((uint32_t)(uint8_t)(int8_t)(int)l) << (8 * t);
       }
-      *reinterpret_cast<uint32_t*>(qh + j) = wh;
-      *reinterpret_cast<uint32_t*>(ql + j) = wl;
     }
+    reinterpret_cast<uint4*>(qh)[0] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+    reinterpret_cast<uint4*>(qh)[1] = make_uint4(wh[4], wh[5], wh[6], wh[7]);
+    reinterpret_cast<uint4*>(ql)[0] = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+    reinterpret_cast<uint4*>(ql)[1] = make_uint4(wl[4], wl[5], wl[6], wl[7]);
     xs[b * (ksmax / 32) + gi] = amax / (127.f * 256.f);
     xsum[b * (ksmax / 16) + 2 * gi] = s0;
     xsum[b * (ksmax / 16) + 2 * gi + 1] = s1;
@@ -188,7 +235,12 @@ __global__ void __launch_bounds__(QMV_THREADS) qmv_kernel(const QmvArgs a) {
   for (int c = 0; c < npro; c++) issue(c);
 
   F::load_tables(tab, threadIdx.x, blockDim.x);
-  qmv_quantize_x<NB>(a, blk0 * QK, nblk * QK, ksmax, btile * NB, xq, xs, xsum);
+  if (a.x_dtype == DT_F16)
+    qmv_quantize_x<NB, __half>(a, blk0 * QK, nblk * QK, ksmax, btile * NB, xq, xs, xsum);
+  else if (a.x_dtype == DT_BF16)
+    qmv_quantize_x<NB, __nv_bfloat16>(a, blk0 * QK, nblk * QK, ksmax, btile * NB, xq, xs, xsum);
+  else
+    qmv_quantize_x<NB, float>(a, blk0 * QK, nblk * QK, ksmax, btile * NB, xq, xs, xsum);
   __syncthreads();
 
   // Per-thread constants of the activation operand (column g of the MMA).
@@ -360,11 +412,15 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
   p.row_groups = (int)((N + QMV_ROWS - 1) / QMV_ROWS);
   p.bps = qmv_pick_bps(N, kblocks);
   p.slices = (kblocks + p.bps - 1) / p.bps;
+  if ((int64_t)p.row_groups * p.btiles > QMV_TICKET_SLOTS) {  // too many row groups to ticket: no split
+    p.bps = kblocks;
+    p.slices = 1;
+  }
   p.smem = qmv_smem_dispatch(t, p.nb, p.bps);
   p.workspace = 0;
   if (p.slices > 1) {
     const size_t partial = (size_t)p.slices * p.btiles * p.nb * N * sizeof(float);
-    p.workspace = ((partial + 255) / 256) * 256 + (size_t)p.row_groups * p.btiles * sizeof(unsigned);
+    p.workspace = QMV_TICKET_BYTES + partial;
   }
   return p;
 }
@@ -413,9 +469,8 @@ cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, in
   a.partial = nullptr;
   a.tickets = nullptr;
   if (p.slices > 1) {
-    const size_t partial = (size_t)p.slices * p.btiles * p.nb * N * sizeof(float);
-    a.partial = static_cast<float*>(ws);
-    a.tickets = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(ws) + ((partial + 255) / 256) * 256);
+    a.tickets = static_cast<unsigned*>(ws);
+    a.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + QMV_TICKET_BYTES);
   }
   a.err = err;
   return qmv_launch(t, a, p, st);

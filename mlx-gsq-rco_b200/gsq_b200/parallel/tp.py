@@ -1,0 +1,97 @@
+"""Output-row tensor parallelism for packed projections.
+
+The reference has no parallelism of its own (its only trace is mlx-lm's
+unexercised ``all_sum`` hook, ``mlx_gsq/models/qwen35.py:104-105``).  Row n of
+a packed matrix is one contiguous byte span ``[n*rb, (n+1)*rb)`` with
+``rb = (K/256)*block_bytes``, so a projection shards across ranks by output
+rows with no repacking: rank r of P keeps rows ``[r*N/P, (r+1)*N/P)`` and
+computes its slice of y with the local QMV/QMM kernel; the slices are joined
+with one NCCL ``all_gather_into_tensor`` over NVLink.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..quant.layouts import QUANT_BLOCK_SIZES, type_id
+from ..runtime.store import PackedWeight
+
+
+def shard_bounds(n_rows: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [lo, hi) owned by ``rank``; requires n_rows % world == 0."""
+    if world <= 0 or not (0 <= rank < world):
+        raise ValueError("invalid rank/world")
+    if n_rows % world:
+        raise ValueError(f"{n_rows} output rows do not split evenly over {world} ranks")
+    per = n_rows // world
+    return rank * per, (rank + 1) * per
+
+
+def row_bytes(qtype: str, in_features: int) -> int:
+    elems, bb = QUANT_BLOCK_SIZES[type_id(qtype)]
+    return in_features // elems * bb
+
+
+def shard_packed(packed: torch.Tensor, qtype: str, out_features: int, in_features: int, world: int,
+                 rank: int) -> torch.Tensor:
+    """Byte slice of the packed matrix holding this rank's output rows (a copy)."""
+    lo, hi = shard_bounds(out_features, world, rank)
+    rb = row_bytes(qtype, in_features)
+    flat = packed.reshape(-1)
+    if flat.numel() != out_features * rb:
+        raise ValueError("packed size does not match the matrix shape")
+    return flat[lo * rb:hi * rb].clone()
+
+
+def shard_weight(weight: PackedWeight, world: int, rank: int) -> PackedWeight:
+    n, k = weight.logical_shape
+    data = shard_packed(weight.data, weight.quantization_type, n, k, world, rank)
+    lo, hi = shard_bounds(n, world, rank)
+    return PackedWeight(name=f"{weight.name}[rows {lo}:{hi}]", data=data, gguf_shape=(k, hi - lo),
+                        logical_shape=(hi - lo, k), quantization_type=weight.quantization_type,
+                        quantization_type_id=weight.quantization_type_id, num_elements=(hi - lo) * k,
+                        num_bytes=data.numel())
+
+
+def gather_rows(y_local: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather per-rank output slices (..., N/P) into (..., N), rank-major."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return y_local
+    lead = y_local.shape[:-1]
+    cols = y_local.shape[-1]
+    flat = y_local.reshape(-1, cols).contiguous()
+    rows = flat.shape[0]
+    out = torch.empty((world, rows, cols), dtype=flat.dtype, device=flat.device)
+    if flat.device.type == "cuda":
+        dist.all_gather_into_tensor(out, flat, group=group)
+    else:
+        parts = list(out.unbind(0))
+        dist.all_gather(parts, flat, group=group)
+        out = torch.stack(parts, 0)
+    return out.permute(1, 0, 2).reshape(*lead, world * cols)
+
+
+class RowParallelLinear(torch.nn.Module):
+    """A packed projection split by output rows across the ranks of ``group``.
+
+    ``forward(x)`` runs the local shard with the fused kernels (GSQLinear
+    dispatch: matvec for one row, tiled matmul otherwise) and all-gathers
+    the output slices, so every rank returns the full ``(..., out_features)``.
+    """
+
+    def __init__(self, weight: PackedWeight, group=None, bias: torch.Tensor | None = None, local_fn=None):
+        super().__init__()
+        from ..nn.linear import GSQLinear
+        self.group = group
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world, self.rank = world, rank
+        self.out_features, self.in_features = weight.logical_shape
+        self.shard = shard_weight(weight, world, rank) if world > 1 else weight
+        self.bias = bias
+        self.local = local_fn or GSQLinear(self.shard)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        y = gather_rows(self.local(x), self.group) if self.world > 1 else self.local(x)
+        return y if self.bias is None else y + self.bias

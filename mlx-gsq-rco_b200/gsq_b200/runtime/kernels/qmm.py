@@ -38,6 +38,8 @@ def quantized_matmul(x: torch.Tensor, packed: torch.Tensor, *, qtype: str, out_f
     original = x.shape[:-1]
     rows = x.numel() // in_features
     flat = x.reshape(rows, in_features).contiguous()
+    if flat.data_ptr() % 16:
+        flat = flat.clone()  # TMA / vector loads need 16-byte alignment
     pk = packed.reshape(-1).contiguous()
     y = torch.empty((rows, out_features), dtype=torch.float32, device=dev)
     lib = _lib.load()

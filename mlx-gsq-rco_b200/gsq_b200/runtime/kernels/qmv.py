@@ -49,6 +49,8 @@ def quantized_matvec(x: torch.Tensor, packed: torch.Tensor, *, qtype: str, out_f
                                 out_dtype=out_dtype).reshape(*original, out_features)
     out_dtype = out_dtype or x.dtype
     flat = flat.contiguous()
+    if flat.data_ptr() % 16:
+        flat = flat.clone()  # the kernel reads activations with 16-byte loads
     pk = packed.reshape(-1).contiguous()
     y = torch.empty((rows, out_features), dtype=out_dtype, device=dev)
     lib = _lib.load()

@@ -9,8 +9,7 @@ truth (``tests/test_metal_decoders.py:21``) -- on seeded synthetic blocks.
 Contents, per quant type T:
   T/packed      uint8 (8 blocks) -- also read as a 4 x 512 matrix (2 blocks/row)
   T/deq         float32 dequantize_reference(packed, T)
-  x{rows}       float32 activations shared by every type (fp16-representable
-                values), rows in (1, 2, 5, 8, 33)
+  x{rows}       float16 activations shared by every type, rows in (1, 2, 5, 8, 33)
   T/y{rows}     float64 expected x @ deq.T  (reference tests' expected value,
                 tests/test_all_qmv.py:22, tests/test_all_qmm.py:34-35)
   T/ids, T/emb  embedding ids into the 4-row matrix and the fp16 rows the
