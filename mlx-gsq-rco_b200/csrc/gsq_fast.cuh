@@ -94,16 +94,15 @@ template <> struct Fast<T_Q4_K> {
     hi = (w.y >> sh) & 0x0F0F0F0Fu;
   }
   __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
+    // 6-bit scale/min of group g from the 12 packed bytes (branch-free):
+    // g < 4: low 6 bits of bytes g, 4+g; g >= 4: nibbles of byte 8+j plus the
+    // top 2 bits of bytes j, 4+j (j = g-4).
     const uint8_t* s = b + 4;
-    uint32_t sc, mn;
-    if (g < 4) {
-      sc = s[g] & 63u;
-      mn = s[4 + g] & 63u;
-    } else {
-      const int j = g - 4;
-      sc = (s[8 + j] & 15u) | ((s[j] >> 2) & 48u);
-      mn = (s[8 + j] >> 4) | ((s[4 + j] >> 2) & 48u);
-    }
+    const int j = g & 3;
+    const uint32_t d6 = s[j], m6 = s[4 + j], hl = s[8 + j];
+    const bool hi = g >= 4;
+    const uint32_t sc = hi ? (hl & 15u) | ((d6 >> 2) & 48u) : d6 & 63u;
+    const uint32_t mn = hi ? (hl >> 4) | ((m6 >> 2) & 48u) : m6 & 63u;
     S = h2f_bits(ld16a2(b)) * (float)sc;
     B = -h2f_bits(ld16a2(b + 2)) * (float)mn;
   }

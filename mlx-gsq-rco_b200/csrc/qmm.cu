@@ -22,28 +22,39 @@
 #include <algorithm>
 
 #include "gsq_exact.cuh"
+#include "gsq_fast.cuh"
 #include "gsq_host.h"
 
 namespace gsq {
 
 constexpr int QMM_BM = 128;
 constexpr int QMM_BK = 64;
-constexpr int QMM_THREADS = 192;
+constexpr int QMM_DEC_WARPS = 8;                 // two per TMEM sub-partition
+constexpr int QMM_THREADS = 64 + 32 * QMM_DEC_WARPS;
 
 template <int T>
 struct QmmGeom {
   static constexpr int BB = block_bytes(T);
   static constexpr int PROWB = ((BB + 30) + 15) / 16 * 16;   // staged packed row stride
   static constexpr int PSTAGE = QMM_BM * PROWB;               // one 256-block column of 128 rows
+  static constexpr int TAB = (Fast<T>::TAB_BYTES + 127) / 128 * 128;
+  static constexpr size_t FIXED = 1024 /*align slack*/ + 2 * (size_t)PSTAGE + TAB + 256 /*barriers*/;
 };
 
-__host__ __device__ constexpr int qmm_stages(int bn) { return bn > 128 ? 3 : 4; }
+constexpr size_t QMM_SMEM_LIMIT = 227 * 1024;
+
+// Pipeline depth: as many A/B stages (<= 4) as fit next to the fixed parts.
+template <int T>
+__host__ __device__ constexpr int qmm_stages(int bn) {
+  const size_t per = (size_t)QMM_BM * 128 + (size_t)bn * 128;
+  const size_t n = (QMM_SMEM_LIMIT - QmmGeom<T>::FIXED) / per;
+  return n >= 4 ? 4 : (int)n;
+}
 
 template <int T>
 __host__ __device__ constexpr size_t qmm_smem_bytes(int bn) {
-  // [A stages 16K each][B stages bn*128 each][packed 2 stages][barriers][tmem addr]
-  return 1024 /*align slack*/ + (size_t)qmm_stages(bn) * (QMM_BM * 128 + (size_t)bn * 128) +
-         2 * (size_t)QmmGeom<T>::PSTAGE + 256;
+  // [A stages 16K each][B stages bn*128 each][packed 2 stages][tables][barriers]
+  return QmmGeom<T>::FIXED + (size_t)qmm_stages<T>(bn) * (QMM_BM * 128 + (size_t)bn * 128);
 }
 
 struct QmmArgs {
@@ -121,18 +132,19 @@ template <int T>
 __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, const __grid_constant__ CUtensorMap xmap) {
   using G = QmmGeom<T>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = smem_raw + ((0u - smem_u32(smem_raw)) & 1023u);  // 1024-aligned, shared provenance kept
   const int bn = a.bn;
-  const int NS = qmm_stages(bn);
+  const int NS = qmm_stages<T>(bn);
   uint8_t* astage = smem;                                     // NS x 16 KB
   uint8_t* bstage = astage + (size_t)NS * QMM_BM * 128;       // NS x bn*128
   uint8_t* pstage = bstage + (size_t)NS * bn * 128;           // 2 x PSTAGE
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pstage + 2 * G::PSTAGE);
-  uint64_t* full_a = bars;          // [NS]  count 4 (decoder warps)
+  uint8_t* tab = pstage + 2 * G::PSTAGE;                      // decode tables
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tab + G::TAB);
+  uint64_t* full_a = bars;          // [NS]  count 8 (decoder warps)
   uint64_t* full_b = bars + 4;      // [NS]  count 1 (TMA)
   uint64_t* empty = bars + 8;       // [NS]  count 1 (tcgen05.commit)
   uint64_t* pfull = bars + 12;      // [2]   count 1
-  uint64_t* pempty = bars + 14;     // [2]   count 4
+  uint64_t* pempty = bars + 14;     // [2]   count 8
   uint64_t* accf = bars + 16;       // [1]   count 1
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
 
@@ -145,18 +157,19 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; s++) {
-      mbar_init(&full_a[s], 4);
+      mbar_init(&full_a[s], QMM_DEC_WARPS);
       mbar_init(&full_b[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int s = 0; s < 2; s++) {
       mbar_init(&pfull[s], 1);
-      mbar_init(&pempty[s], 4);
+      mbar_init(&pempty[s], QMM_DEC_WARPS);
     }
     mbar_init(accf, 1);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, tcols);
+  Fast<T>::load_tables(tab, threadIdx.x, blockDim.x);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -228,7 +241,12 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
     __syncwarp();
   } else {
     // ---------------- decoders + epilogue ----------------
-    const int r = 32 * (warp & 3) + lane;  // tile row == TMEM lane
+    // Two warps per TMEM sub-partition: `half` 0 decodes k 0..31 of each
+    // 64-wide step, `half` 1 decodes k 32..63; in the epilogue they split the
+    // BN token columns.
+    using F = Fast<T>;
+    const int dw = warp - 2, half = dw >> 2, sub = warp & 3;
+    const int r = 32 * sub + lane;  // tile row == TMEM lane
     const int64_t row = n0 + r;
     const bool live = row < a.N;
     const int64_t roff = row * a.row_bytes;
@@ -242,15 +260,48 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
         if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
         if (!ok) break;
         uint8_t* tile = astage + (size_t)s * QMM_BM * 128;
-#pragma unroll 2
-        for (int c = 0; c < 8; c++) {
-          float v[8];
-          if (live) Exact<T>::entry(blk, 8 * q + c, v);
-          else {
+        const int c32 = 2 * q + half;
+        float v[32];
+        if (live) {
+          uint32_t lo[4], hi[4];
 #pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = 0.f;
+          for (int tq = 0; tq < 4; tq++) F::entry(blk, c32, tq, tab, lo[tq], hi[tq]);
+          float S[2], B[2];
+          if constexpr (F::UNIT == 32) {
+            F::affine(blk, c32, S[0], B[0]);
+            S[1] = S[0]; B[1] = B[0];
+          } else {
+            F::affine(blk, 2 * c32, S[0], B[0]);
+            F::affine(blk, 2 * c32 + 1, S[1], B[1]);
           }
-          st_sw128(tile, r, c, v);
+#pragma unroll
+          for (int tq = 0; tq < 4; tq++) {
+            const uint32_t tl = lo[tq] ^ 0x80808080u, th = hi[tq] ^ 0x80808080u;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              // exact int8 -> fp32: (2^23 + a + 128) - (2^23 + 128)
+              const float al = __uint_as_float(__byte_perm(tl, 0x4B000000u, 0x7540u | i)) - 8388736.f;
+              const float ah = __uint_as_float(__byte_perm(th, 0x4B000000u, 0x7540u | i)) - 8388736.f;
+              if constexpr (F::BLOCKED) {
+                const int u = (8 * tq) / F::UNIT;  // unit within the 32-chunk
+                v[8 * tq + i] = fmaf(S[u], al, B[u]);
+                v[8 * tq + 4 + i] = fmaf(S[u], ah, B[u]);
+              } else {
+                v[4 * tq + i] = fmaf(S[0], al, B[0]);
+                v[16 + 4 * tq + i] = fmaf(S[0], ah, B[0]);
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j++) v[j] = 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          float w8[8];
+#pragma unroll
+          for (int j = 0; j < 8; j++) w8[j] = v[8 * c + j];
+          st_sw128(tile, r, 4 * half + c, w8);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -259,19 +310,20 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
       __syncwarp();
       if (lane == 0) mbar_arrive(&pempty[ps]);
     }
-    // epilogue
+    // epilogue: this warp's TMEM lanes, half of the BN columns
     if (ok) ok = mbar_wait_bounded(accf, 0u, a.err);
     tc_fence_after();
     if (ok) {
-      const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-      for (int j0 = 0; j0 < bn; j0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem_d + lane_base + (uint32_t)j0, v);
+      const uint32_t lane_base = (uint32_t)(32 * sub) << 16;
+      const int cols = bn / 2;
+      for (int j0 = half * cols; j0 < (half + 1) * cols; j0 += 16) {
+        uint32_t vv[16];
+        tmem_ld16(tmem_d + lane_base + (uint32_t)j0, vv);
         if (live) {
 #pragma unroll
           for (int jj = 0; jj < 16; jj++) {
             const int64_t m = (int64_t)m0 + j0 + jj;
-            if (m < a.M) a.y[m * a.N + row] = __uint_as_float(v[jj]);
+            if (m < a.M) a.y[m * a.N + row] = __uint_as_float(vv[jj]);
           }
         }
       }
@@ -308,8 +360,8 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 int qmm_pick_bn(int64_t M) {
-  if (M <= 16) return 16;
-  if (M <= 256) return (int)((M + 15) / 16 * 16);
+  if (M <= 32) return 32;  // the epilogue splits BN over two warps in 16-column loads
+  if (M <= 256) return (int)((M + 31) / 32 * 32);
   return 128;
 }
 

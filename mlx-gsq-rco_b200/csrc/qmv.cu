@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(QMV_THREADS) qmv_kernel(const QmvArgs a) {
   float* xs = reinterpret_cast<float*>(xq + (size_t)NB * 2 * ksmax);
   float* xsum = xs + NB * (ksmax / 32);
   uint8_t* stages = reinterpret_cast<uint8_t*>(xsum + NB * (ksmax / 16));
-  stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(stages) + 127) & ~uintptr_t(127));
+  stages += (0u - smem_u32(stages)) & 127u;  // align in the shared window, keeping shared provenance
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
@@ -386,13 +386,47 @@ __global__ void __launch_bounds__(QMV_THREADS) qmv_kernel(const QmvArgs a) {
 template <int T, int NB>
 static size_t qmv_smem(int bps) { return qmv_smem_bytes<T, NB>(bps); }
 
-static int qmv_pick_bps(int64_t N, int kblocks) {
-  const int64_t row_groups = (N + QMV_ROWS - 1) / QMV_ROWS;
-  const int64_t target = 2 * 148;
-  int slices = (int)std::min<int64_t>(std::max<int64_t>(1, (target + row_groups - 1) / row_groups), kblocks);
-  slices = std::max(slices, (kblocks + QMV_MAX_SLICE_BLOCKS - 1) / QMV_MAX_SLICE_BLOCKS);
+// Resident CTAs per SM for an instantiation and its shared-memory size (the
+// occupancy API when a device is present, else a shared-memory estimate).
+template <int T, int NB>
+static int qmv_occupancy(size_t smem) {
+  static size_t cached_smem = 0;
+  static int cached_occ = 0;
+  if (cached_occ > 0 && cached_smem == smem) return cached_occ;
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, qmv_kernel<T, NB>, QMV_THREADS, smem) != cudaSuccess ||
+      occ <= 0) {
+    cudaGetLastError();
+    occ = (int)std::max<size_t>(1, std::min<size_t>(16, (227u * 1024u) / (smem + 1024)));
+  }
+  cached_smem = smem;
+  cached_occ = occ;
+  return occ;
+}
+
+static int qmv_sm_count() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+      sms = n;
+    else {
+      cudaGetLastError();
+      sms = 148;
+    }
+  }
+  return sms;
+}
+
+// Blocks per K-slice so that row_groups x slices fills the resident CTA slots
+// of the GPU in a single wave (every CTA streams about the same bytes).
+static int qmv_pick_bps(int64_t row_groups, int kblocks, int slots) {
+  int slices = (int)std::max<int64_t>(1, slots / std::max<int64_t>(1, row_groups));
+  slices = std::min(slices, kblocks);
   int bps = (kblocks + slices - 1) / slices;
-  return bps;
+  bps = std::min(bps, QMV_MAX_SLICE_BLOCKS);
+  return std::max(bps, 1);
 }
 
 #define GSQ_QMV_SMEM_CASE(TT)                                                   \
@@ -404,13 +438,26 @@ static size_t qmv_smem_dispatch(int t, int nb, int bps) {
   return 0;
 }
 
+#define GSQ_QMV_OCC_CASE(TT)                                                                       \
+  case TT:                                                                                         \
+    return nb == 1 ? qmv_occupancy<TT, 1>(qmv_smem<TT, 1>(bps)) : qmv_occupancy<TT, 2>(qmv_smem<TT, 2>(bps));
+
+static int qmv_occ_dispatch(int t, int nb, int bps) {
+  switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMV_OCC_CASE) }
+  return 1;
+}
+
 QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
   QmvPlan p;
   const int kblocks = (int)(K / QK);
   p.nb = rows == 1 ? 1 : 2;
   p.btiles = (rows + p.nb - 1) / p.nb;
   p.row_groups = (int)((N + QMV_ROWS - 1) / QMV_ROWS);
-  p.bps = qmv_pick_bps(N, kblocks);
+  // The occupancy is evaluated at the largest slice (the smem of the x slice
+  // grows with it), so the chosen grid never exceeds one wave.
+  const int occ = qmv_occ_dispatch(t, p.nb, std::min(kblocks, QMV_MAX_SLICE_BLOCKS));
+  const int slots = occ * qmv_sm_count();
+  p.bps = qmv_pick_bps((int64_t)p.row_groups * p.btiles, kblocks, slots);
   p.slices = (kblocks + p.bps - 1) / p.bps;
   if ((int64_t)p.row_groups * p.btiles > QMV_TICKET_SLOTS) {  // too many row groups to ticket: no split
     p.bps = kblocks;
