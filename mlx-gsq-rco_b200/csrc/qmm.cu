@@ -5,15 +5,15 @@
 // :559-594): Y[m, n] = sum_k X[m, k] * deq(W)[n, k], fp32 accumulation.
 //
 // Output tile = 128 weight rows (MMA M) x BN tokens (MMA N), K stepped 64 at
-// a time.  Warp roles in a 192-thread CTA:
-//   warp 0      producer: TMA tensor-map loads of the fp16 activation tile
-//               (128B swizzle) and 1-D bulk copies of the packed 256-weight
-//               blocks of the 128 rows into a double-buffered staging area;
+// a time.  Warp roles in a 352-thread CTA:
+//   warp 0      TMA tensor-map loads of the fp16 activation tile (128B swizzle);
 //   warp 1      allocates TMEM and issues tcgen05.mma (kind::f16, fp32 accum
 //               in TMEM) from one elected lane, committing to mbarriers;
-//   warps 2..5  decode each row's packed block once per tile into fp16 in the
-//               canonical K-major SW128 layout the MMA reads (every weight is
-//               decoded once per BN tokens), then run the epilogue
+//   warp 2      1-D bulk copies of each row's packed 256-weight block into a
+//               PST-deep staging ring, running ahead of the decoders;
+//   warps 3..10 decode the packed blocks into fp16 in the canonical K-major
+//               SW128 layout the MMA reads (each weight once per BN tokens),
+//               two warps per TMEM sub-partition, then run the epilogue
 //               (tcgen05.ld TMEM -> registers -> fp32 Y).
 // Weights are decoded to fp16, not bf16: bf16-rounded weights miss the
 // rel-L2 <= 1e-3 bar, fp16 ones pass; activations are converted to fp16 by
@@ -30,7 +30,8 @@ namespace gsq {
 constexpr int QMM_BM = 128;
 constexpr int QMM_BK = 64;
 constexpr int QMM_DEC_WARPS = 8;                 // two per TMEM sub-partition
-constexpr int QMM_THREADS = 64 + 32 * QMM_DEC_WARPS;
+constexpr int QMM_DEC0 = 3;                       // first decoder warp
+constexpr int QMM_THREADS = 32 * (QMM_DEC0 + QMM_DEC_WARPS);
 
 template <int T>
 struct QmmGeom {
@@ -38,24 +39,26 @@ struct QmmGeom {
   static constexpr int PROWB = ((BB + 30) + 15) / 16 * 16;   // staged packed row stride
   static constexpr int PSTAGE = QMM_BM * PROWB;               // one 256-block column of 128 rows
   static constexpr int TAB = (Fast<T>::TAB_BYTES + 127) / 128 * 128;
-  static constexpr size_t FIXED = 1024 /*align slack*/ + 2 * (size_t)PSTAGE + TAB + 256 /*barriers*/;
 };
 
 constexpr size_t QMM_SMEM_LIMIT = 227 * 1024;
 
-// Pipeline depth: as many A/B stages (<= 4) as fit next to the fixed parts.
+// Pipeline shape for a token tile of bn: PST packed stages (3, or 2 when
+// space is short) and as many A/B stages (<= 4) as fit.
 template <int T>
-__host__ __device__ constexpr int qmm_stages(int bn) {
-  const size_t per = (size_t)QMM_BM * 128 + (size_t)bn * 128;
-  const size_t n = (QMM_SMEM_LIMIT - QmmGeom<T>::FIXED) / per;
-  return n >= 4 ? 4 : (int)n;
-}
-
-template <int T>
-__host__ __device__ constexpr size_t qmm_smem_bytes(int bn) {
-  // [A stages 16K each][B stages bn*128 each][packed 2 stages][tables][barriers]
-  return QmmGeom<T>::FIXED + (size_t)qmm_stages<T>(bn) * (QMM_BM * 128 + (size_t)bn * 128);
-}
+struct QmmPipe {
+  static constexpr size_t fixed(int pst) { return 1024 + (size_t)pst * QmmGeom<T>::PSTAGE + QmmGeom<T>::TAB + 256; }
+  static constexpr int stages_for(int bn, int pst) {
+    const size_t per = (size_t)QMM_BM * 128 + (size_t)bn * 128;
+    const size_t n = fixed(pst) < QMM_SMEM_LIMIT ? (QMM_SMEM_LIMIT - fixed(pst)) / per : 0;
+    return n >= 4 ? 4 : (int)n;
+  }
+  static constexpr int pst(int bn) { return stages_for(bn, 3) >= 3 ? 3 : 2; }
+  static constexpr int ns(int bn) { return stages_for(bn, pst(bn)); }
+  static constexpr size_t smem(int bn) {
+    return fixed(pst(bn)) + (size_t)ns(bn) * ((size_t)QMM_BM * 128 + (size_t)bn * 128);
+  }
+};
 
 struct QmmArgs {
   const uint8_t* packed;
@@ -134,19 +137,20 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((0u - smem_u32(smem_raw)) & 1023u);  // 1024-aligned, shared provenance kept
   const int bn = a.bn;
-  const int NS = qmm_stages<T>(bn);
+  const int NS = QmmPipe<T>::ns(bn);
+  const int PST = QmmPipe<T>::pst(bn);
   uint8_t* astage = smem;                                     // NS x 16 KB
   uint8_t* bstage = astage + (size_t)NS * QMM_BM * 128;       // NS x bn*128
-  uint8_t* pstage = bstage + (size_t)NS * bn * 128;           // 2 x PSTAGE
-  uint8_t* tab = pstage + 2 * G::PSTAGE;                      // decode tables
+  uint8_t* pstage = bstage + (size_t)NS * bn * 128;           // PST x PSTAGE
+  uint8_t* tab = pstage + (size_t)PST * G::PSTAGE;            // decode tables
   uint64_t* bars = reinterpret_cast<uint64_t*>(tab + G::TAB);
   uint64_t* full_a = bars;          // [NS]  count 8 (decoder warps)
   uint64_t* full_b = bars + 4;      // [NS]  count 1 (TMA)
   uint64_t* empty = bars + 8;       // [NS]  count 1 (tcgen05.commit)
-  uint64_t* pfull = bars + 12;      // [2]   count 1
-  uint64_t* pempty = bars + 14;     // [2]   count 8
-  uint64_t* accf = bars + 16;       // [1]   count 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* pfull = bars + 12;      // [PST] count 1
+  uint64_t* pempty = bars + 16;     // [PST] count 8
+  uint64_t* accf = bars + 20;       // [1]   count 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n0 = (int64_t)blockIdx.x * QMM_BM;
@@ -161,7 +165,7 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
       mbar_init(&full_b[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int s = 0; s < 2; s++) {
+    for (int s = 0; s < PST; s++) {
       mbar_init(&pfull[s], 1);
       mbar_init(&pempty[s], QMM_DEC_WARPS);
     }
@@ -177,38 +181,9 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
   bool ok = true;
 
   if (warp == 0) {
-    // ---------------- producer ----------------
-    const uintptr_t pbase = reinterpret_cast<uintptr_t>(a.packed);
-    const uint64_t policy = l2_policy_evict_first();
+    // ---------------- activation tiles (TMA) ----------------
     for (int ks = 0; ks < nks && ok; ks++) {
       const int s = ks % NS, n = ks / NS;
-      if ((ks & 3) == 0) {
-        const int kb = ks >> 2, ps = kb & 1, pn = kb >> 1;
-        if (pn > 0) ok = mbar_wait_bounded(&pempty[ps], (uint32_t)((pn - 1) & 1), a.err);
-        if (!ok) break;
-        uint32_t bytes = 0;
-        for (int i = 0; i < 4; i++) {
-          const int r = lane + 32 * i;
-          const int64_t row = n0 + r;
-          if (row >= a.N) continue;
-          const int64_t off = row * a.row_bytes + (int64_t)kb * G::BB;
-          const int64_t end = off + G::BB;
-          const int64_t off_al = off & ~int64_t(15);
-          int64_t end_al = (end + 15) & ~int64_t(15);
-          if (end_al > a.packed_bytes) end_al = end & ~int64_t(15);
-          uint8_t* dst = pstage + (size_t)ps * G::PSTAGE + r * G::PROWB;
-          if (end_al > off_al) {
-            fence_proxy_async_smem();
-            bulk_g2s_stream(dst, reinterpret_cast<const void*>(pbase + off_al), (uint32_t)(end_al - off_al),
-                            &pfull[ps], policy);
-            bytes += (uint32_t)(end_al - off_al);
-          }
-          for (int64_t t = max(end_al, off_al); t < end; t++) dst[t - off_al] = a.packed[t];
-        }
-        const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&pfull[ps], total);
-      }
       if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
       if (!ok) break;
       if (lane == 0) {
@@ -216,6 +191,37 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
         tma_load_2d(bstage + (size_t)s * bn * 128, &xmap, ks * QMM_BK, m0, &full_b[s]);
       }
       __syncwarp();
+    }
+  } else if (warp == 2) {
+    // ---------------- packed weight blocks ----------------
+    const uintptr_t pbase = reinterpret_cast<uintptr_t>(a.packed);
+    const uint64_t policy = l2_policy_evict_first();
+    for (int kb = 0; kb < nkb && ok; kb++) {
+      const int ps = kb % PST, pn = kb / PST;
+      if (pn > 0) ok = mbar_wait_bounded(&pempty[ps], (uint32_t)((pn - 1) & 1), a.err);
+      if (!ok) break;
+      uint32_t bytes = 0;
+      for (int i = 0; i < 4; i++) {
+        const int r = lane + 32 * i;
+        const int64_t row = n0 + r;
+        if (row >= a.N) continue;
+        const int64_t off = row * a.row_bytes + (int64_t)kb * G::BB;
+        const int64_t end = off + G::BB;
+        const int64_t off_al = off & ~int64_t(15);
+        int64_t end_al = (end + 15) & ~int64_t(15);
+        if (end_al > a.packed_bytes) end_al = end & ~int64_t(15);
+        uint8_t* dst = pstage + (size_t)ps * G::PSTAGE + r * G::PROWB;
+        if (end_al > off_al) {
+          fence_proxy_async_smem();
+          bulk_g2s_stream(dst, reinterpret_cast<const void*>(pbase + off_al), (uint32_t)(end_al - off_al),
+                          &pfull[ps], policy);
+          bytes += (uint32_t)(end_al - off_al);
+        }
+        for (int64_t t = max(end_al, off_al); t < end; t++) dst[t - off_al] = a.packed[t];
+      }
+      const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(&pfull[ps], total);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -245,63 +251,70 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
     // 64-wide step, `half` 1 decodes k 32..63; in the epilogue they split the
     // BN token columns.
     using F = Fast<T>;
-    const int dw = warp - 2, half = dw >> 2, sub = warp & 3;
+    const int dw = warp - QMM_DEC0, half = dw >> 2, sub = warp & 3;
     const int r = 32 * sub + lane;  // tile row == TMEM lane
     const int64_t row = n0 + r;
     const bool live = row < a.N;
     const int64_t roff = row * a.row_bytes;
+    const __half2 off2 = __float2half2_rn(1152.f);
     for (int kb = 0; kb < nkb && ok; kb++) {
-      const int ps = kb & 1;
-      ok = mbar_wait_bounded(&pfull[ps], (uint32_t)((kb >> 1) & 1), a.err);
+      const int ps = kb % PST;
+      ok = mbar_wait_bounded(&pfull[ps], (uint32_t)((kb / PST) & 1), a.err);
       if (!ok) break;
       const uint8_t* blk = pstage + (size_t)ps * G::PSTAGE + r * G::PROWB + (int)((roff + (int64_t)kb * G::BB) & 15);
       for (int q = 0; q < 4 && ok; q++) {
         const int ks = 4 * kb + q, s = ks % NS, n = ks / NS;
         if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
         if (!ok) break;
-        uint8_t* tile = astage + (size_t)s * QMM_BM * 128;
+        uint8_t* trow = astage + (size_t)s * QMM_BM * 128 + r * 128;
         const int c32 = 2 * q + half;
-        float v[32];
+        // 32 weights of this row: int8 entries -> exact fp16 integers via a
+        // 0x64xx byte-permute (1024 + a + 128) - 1152, then one fp16 FMA with
+        // the unit's scale/offset: w = a * S + B.
+        uint32_t out[16];
         if (live) {
-          uint32_t lo[4], hi[4];
-#pragma unroll
-          for (int tq = 0; tq < 4; tq++) F::entry(blk, c32, tq, tab, lo[tq], hi[tq]);
-          float S[2], B[2];
+          __half2 S2[2], B2[2];
           if constexpr (F::UNIT == 32) {
-            F::affine(blk, c32, S[0], B[0]);
-            S[1] = S[0]; B[1] = B[0];
+            float S, B;
+            F::affine(blk, c32, S, B);
+            S2[0] = S2[1] = __float2half2_rn(S);
+            B2[0] = B2[1] = __float2half2_rn(B);
           } else {
-            F::affine(blk, 2 * c32, S[0], B[0]);
-            F::affine(blk, 2 * c32 + 1, S[1], B[1]);
+            float S0, B0, S1, B1;
+            F::affine(blk, 2 * c32, S0, B0);
+            F::affine(blk, 2 * c32 + 1, S1, B1);
+            S2[0] = __float2half2_rn(S0); B2[0] = __float2half2_rn(B0);
+            S2[1] = __float2half2_rn(S1); B2[1] = __float2half2_rn(B1);
           }
 #pragma unroll
           for (int tq = 0; tq < 4; tq++) {
-            const uint32_t tl = lo[tq] ^ 0x80808080u, th = hi[tq] ^ 0x80808080u;
+            uint32_t lo, hi;
+            F::entry(blk, c32, tq, tab, lo, hi);
+            const int u = F::BLOCKED ? (8 * tq) / F::UNIT : 0;
+            const uint32_t w2[2] = {lo ^ 0x80808080u, hi ^ 0x80808080u};
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-              // exact int8 -> fp32: (2^23 + a + 128) - (2^23 + 128)
-              const float al = __uint_as_float(__byte_perm(tl, 0x4B000000u, 0x7540u | i)) - 8388736.f;
-              const float ah = __uint_as_float(__byte_perm(th, 0x4B000000u, 0x7540u | i)) - 8388736.f;
-              if constexpr (F::BLOCKED) {
-                const int u = (8 * tq) / F::UNIT;  // unit within the 32-chunk
-                v[8 * tq + i] = fmaf(S[u], al, B[u]);
-                v[8 * tq + 4 + i] = fmaf(S[u], ah, B[u]);
-              } else {
-                v[4 * tq + i] = fmaf(S[0], al, B[0]);
-                v[16 + 4 * tq + i] = fmaf(S[0], ah, B[0]);
+            for (int h = 0; h < 2; h++) {
+#pragma unroll
+              for (int p = 0; p < 2; p++) {
+                const uint32_t m = __byte_perm(w2[h], 0x64646464u, p ? 0x4342u : 0x4140u);
+                __half2 v = __hsub2(*reinterpret_cast<const __half2*>(&m), off2);
+                v = __hfma2(v, S2[u], B2[u]);
+                // BLOCKED: 8 consecutive weights per entry; identity: lo/hi are
+                // the 4-weight runs at 4tq and 16+4tq.
+                const int idx = F::BLOCKED ? 4 * tq + 2 * h + p : (h ? 8 : 0) + 2 * tq + p;
+                out[idx] = *reinterpret_cast<const uint32_t*>(&v);
               }
             }
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; j++) v[j] = 0.f;
+          for (int j = 0; j < 16; j++) out[j] = 0u;
         }
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-          float w8[8];
-#pragma unroll
-          for (int j = 0; j < 8; j++) w8[j] = v[8 * c + j];
-          st_sw128(tile, r, 4 * half + c, w8);
+          const int chunk = 4 * half + c;
+          *reinterpret_cast<uint4*>(trow + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(out[4 * c], out[4 * c + 1], out[4 * c + 2], out[4 * c + 3]);
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -359,17 +372,19 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+// Token tile: the whole M when it fits one MMA (N <= 256, multiple of 32 so
+// the two epilogue warps take 16-column TMEM loads), else 256.
 int qmm_pick_bn(int64_t M) {
-  if (M <= 32) return 32;  // the epilogue splits BN over two warps in 16-column loads
+  if (M <= 32) return 32;
   if (M <= 256) return (int)((M + 31) / 32 * 32);
-  return 128;
+  return 256;
 }
 
 size_t qmm_x16_bytes(int x_dtype, int64_t M, int64_t K) {
   return x_dtype == DT_F16 ? 0 : (size_t)(((M * K * 2) + 255) / 256 * 256);
 }
 
-#define GSQ_QMM_SMEM_CASE(TT) case TT: return qmm_smem_bytes<TT>(bn);
+#define GSQ_QMM_SMEM_CASE(TT) case TT: return QmmPipe<TT>::smem(bn);
 size_t qmm_smem(int t, int bn) {
   switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMM_SMEM_CASE) }
   return 0;
@@ -377,7 +392,7 @@ size_t qmm_smem(int t, int bn) {
 
 template <int T>
 static cudaError_t qmm_launch_t(const QmmArgs& a, const CUtensorMap& map, cudaStream_t st) {
-  const size_t smem = qmm_smem_bytes<T>(a.bn);
+  const size_t smem = QmmPipe<T>::smem(a.bn);
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);

@@ -30,9 +30,9 @@ namespace gsq {
 
 constexpr int QMV_WARPS = 4;
 constexpr int QMV_ROWS = 16 * QMV_WARPS;
-constexpr int QMV_STAGES = 3;
+constexpr int QMV_STAGES = 2;
 constexpr int QMV_THREADS = 32 * QMV_WARPS;
-constexpr int QMV_MAX_SLICE_BLOCKS = 16;
+constexpr int QMV_MAX_SLICE_BLOCKS = 32;
 // Split-K scratch layout: a fixed region of ticket counters first, then the
 // partial sums.  Every completed call returns the tickets it used to zero, and
 // no call ever writes partial sums over the ticket region, so one zero-filled
@@ -60,7 +60,7 @@ struct QmvArgs {
 template <int T>
 struct QmvGeom {
   static constexpr int BB = block_bytes(T);
-  static constexpr int CB = BB > 84 ? 2 : 4;                      // blocks per chunk
+  static constexpr int CB = BB <= 66 ? 8 : BB <= 98 ? 4 : 2;       // blocks per chunk (~400-600 B a row)
   static constexpr int ROWB = ((CB * BB + 30) + 15) / 16 * 16;     // staged row stride
   static constexpr int STAGE = 16 * ROWB;
   static constexpr int TAB = (Fast<T>::TAB_BYTES + 127) / 128 * 128;
@@ -165,7 +165,7 @@ __device__ void qmv_quantize_x(const QmvArgs& a, int k0, int ks, int ksmax, int 
 }
 
 template <int T, int NB>
-__global__ void __launch_bounds__(QMV_THREADS) qmv_kernel(const QmvArgs a) {
+__global__ void __launch_bounds__(QMV_THREADS, 4) qmv_kernel(const QmvArgs a) {
   using F = Fast<T>;
   using G = QmvGeom<T>;
   constexpr int UNIT = F::UNIT;
@@ -296,7 +296,9 @@ __global__ void __launch_bounds__(QMV_THREADS) qmv_kernel(const QmvArgs a) {
           xw0 = live ? w.x : 0u;
           xw1 = live ? w.y : 0u;
         }
-        int C[4] = {0, 0, 0, 0};
+        // Two independent accumulator chains (even / odd MMAs) halve the
+        // dependent tensor-core latency per set.
+        int C[4] = {0, 0, 0, 0}, Cb[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int j = 0; j < MMAS; j++) {
           const int c32 = set * MMAS + j;
@@ -304,7 +306,12 @@ __global__ void __launch_bounds__(QMV_THREADS) qmv_kernel(const QmvArgs a) {
           F::entry(b0, c32, tq, tab, a0, a2);
           F::entry(b1, c32, tq, tab, a1, a3);
           const bool on = (j == jsel);
-          mma_s8(C, a0, a1, a2, a3, on ? xw0 : 0u, on ? xw1 : 0u);
+          if (j & 1) mma_s8(Cb, a0, a1, a2, a3, on ? xw0 : 0u, on ? xw1 : 0u);
+          else mma_s8(C, a0, a1, a2, a3, on ? xw0 : 0u, on ? xw1 : 0u);
+        }
+        if constexpr (MMAS > 1) {
+#pragma unroll
+          for (int i = 0; i < 4; i++) C[i] += Cb[i];
         }
         (void)live;
         const int unit = set * UPS + s_ep;
