@@ -141,6 +141,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or about `ns` nanoseconds pass, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(ns) : "memory");
+  return ok != 0;
+}
+
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while the previous kernel in the
+// stream is still running; pdl_wait() blocks the calling thread until that
+// kernel has completed and its memory is visible, so it must precede every
+// read of the previous kernel's outputs and every global write.
+// pdl_launch_dependents() lets the next kernel start its own prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Error codes a kernel can record in the device status word.
 enum DeviceError : int { DEV_OK = 0, DEV_WAIT_TIMEOUT = 1 };
 
@@ -151,7 +171,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (clock64() - t0 > (1ll << 31)) {
       if (err) atomicExch(err, DEV_WAIT_TIMEOUT);
       return false;

@@ -6,7 +6,28 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace gsq {
+
+// Launch with programmatic stream serialization (PDL): the kernel may begin
+// while the previous kernel of the stream finishes; it synchronises with
+// griddepcontrol.wait before touching that kernel's results.
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                     cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Launch plan of one QMV call: grid shape, K-slicing and scratch needs.
 struct QmvPlan {

@@ -182,6 +182,7 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
 
   if (warp == 0) {
     // ---------------- activation tiles (TMA) ----------------
+    pdl_wait();  // the activations are written by the preceding kernel
     for (int ks = 0; ks < nks && ok; ks++) {
       const int s = ks % NS, n = ks / NS;
       if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
@@ -324,6 +325,8 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
       if (lane == 0) mbar_arrive(&pempty[ps]);
     }
     // epilogue: this warp's TMEM lanes, half of the BN columns
+    pdl_launch_dependents();
+    pdl_wait();  // global writes only after the preceding kernel completed
     if (ok) ok = mbar_wait_bounded(accf, 0u, a.err);
     tc_fence_after();
     if (ok) {
@@ -349,6 +352,8 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
 
 // Activations -> fp16 (row-major [M, K]); the tensor map reads this copy.
 __global__ void to_f16_kernel(const void* x, int dtype, int64_t n, __half* out) {
+  pdl_launch_dependents();
+  pdl_wait();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = __float2half_rn(load_act(x, dtype, i));
 }
@@ -402,8 +407,7 @@ static cudaError_t qmm_launch_t(const QmmArgs& a, const CUtensorMap& map, cudaSt
     configured[dev] = (int)smem;
   }
   dim3 grid((unsigned)((a.N + QMM_BM - 1) / QMM_BM), (unsigned)((a.M + a.bn - 1) / a.bn));
-  qmm_kernel<T><<<grid, QMM_THREADS, smem, st>>>(a, map);
-  return cudaGetLastError();
+  return launch_pdl(qmm_kernel<T>, grid, dim3(QMM_THREADS), smem, st, a, map);
 }
 
 #define GSQ_QMM_LAUNCH_CASE(TT) case TT: return qmm_launch_t<TT>(a, map, st);

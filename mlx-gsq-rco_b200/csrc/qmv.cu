@@ -235,6 +235,9 @@ __global__ void __launch_bounds__(QMV_THREADS, 4) qmv_kernel(const QmvArgs a) {
   for (int c = 0; c < npro; c++) issue(c);
 
   F::load_tables(tab, threadIdx.x, blockDim.x);
+  // Everything above reads only weights and tables; from here on the kernel
+  // reads activations / scratch that an earlier kernel in the stream may write.
+  pdl_wait();
   if (a.x_dtype == DT_F16)
     qmv_quantize_x<NB, __half>(a, blk0 * QK, nblk * QK, ksmax, btile * NB, xq, xs, xsum);
   else if (a.x_dtype == DT_BF16)
@@ -335,6 +338,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 4) qmv_kernel(const QmvArgs a) {
     __syncwarp();
     if (c + QMV_STAGES < nchunks) issue(c + QMV_STAGES);
   }
+  pdl_launch_dependents();
   if (!ok) {
     // Drain the copies this warp still has in flight before the CTA exits.
     for (int c = waited; c < min(nchunks, waited + QMV_STAGES); c++)
@@ -490,9 +494,7 @@ static cudaError_t qmv_launch_t(const QmvArgs& a, const QmvPlan& p, cudaStream_t
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = (int)p.smem;
   }
-  dim3 grid(p.row_groups, p.slices, p.btiles);
-  kern<<<grid, QMV_THREADS, p.smem, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(p.row_groups, p.slices, p.btiles), dim3(QMV_THREADS), p.smem, st, a);
 }
 
 #define GSQ_QMV_LAUNCH_CASE(TT) \
