@@ -99,6 +99,21 @@ GSQ_API int gsq_qmm(int qtype, const void* x, int x_dtype, const uint8_t* packed
 GSQ_API int gsq_embed(int qtype, const int32_t* ids, int64_t T, const uint8_t* packed, int64_t vocab, int64_t dim,
               void* out, int out_dtype, gsq_stream_t stream);
 
+/* Fixed size of the device scratch array behind gsq_qmv_noalloc. */
+#define GSQ_QMV_NOALLOC_SCRATCH_BYTES (2u * 1024u * 1024u)
+
+/* gsq_qmv for callers that cannot allocate device memory (no reference
+ * counterpart: the reference's Metal kernels need no scratch).  Same
+ * arguments and results as gsq_qmv, without the workspace: the split-K
+ * scratch is a fixed GSQ_QMV_NOALLOC_SCRATCH_BYTES array inside the library
+ * (held by every GPU that loads it until exit), so the call allocates nothing.
+ * Shapes that need more scratch return GSQ_ERR_WORKSPACE.  The first call on
+ * a device looks up the array's address and should come before any stream
+ * capture.  Every call shares the array: calls that overlap on the GPU race,
+ * so order them (one stream, or events). */
+GSQ_API int gsq_qmv_noalloc(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
+                            int64_t rows, void* y, int y_dtype, gsq_stream_t stream);
+
 /* Synchronises `stream`, then returns and clears the device error word the
  * kernels of the current device write (0 = none; 1 = a bounded wait expired;
  * 2 = an embedding id was out of range).  No reference counterpart: the

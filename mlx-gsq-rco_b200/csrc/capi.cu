@@ -27,6 +27,14 @@ static int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+namespace gsq {
+// Lets other translation units of the library report through gsq_last_error().
+int set_last_error(int code, const char* msg) {
+  snprintf(g_err, sizeof(g_err), "%s", msg);
+  return code;
+}
+}  // namespace gsq
+
 static int* device_error_word() {
   static int* cache[64] = {nullptr};
   int dev = 0;

@@ -54,4 +54,7 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
                        float* y, __half* x16, int* err, cudaStream_t st, const char** why);
 size_t qmm_x16_bytes(int x_dtype, int64_t M, int64_t K);
 
+// Records `msg` as this thread's gsq_last_error() text and returns `code`.
+int set_last_error(int code, const char* msg);
+
 }  // namespace gsq

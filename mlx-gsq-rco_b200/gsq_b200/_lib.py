@@ -38,6 +38,7 @@ SIGNATURES = {
     "gsq_qmm": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, _P, _P, _SZ, _P]),
     "gsq_embed": (_I, [_I, _P, _I64, _P, _I64, _I64, _P, _I, _P]),
     "gsq_device_status": (_I, [_P]),
+    "gsq_qmv_noalloc": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, _P, _I, _P]),
 }
 
 _lib = None
