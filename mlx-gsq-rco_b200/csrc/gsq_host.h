@@ -29,15 +29,17 @@ static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 b
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// Launch plan of one QMV call: grid shape, K-slicing and scratch needs.
+// Launch plan of one QMV call: grid shape, work split and scratch layout.
 struct QmvPlan {
-  int bps;         // 256-blocks per K-slice
-  int slices;      // K-slices (grid.y); > 1 means partial sums + ticket fixup
-  int row_groups;  // 64-row groups (grid.x)
-  int btiles;      // activation-row tiles (grid.z)
-  int nb;          // activation rows per tile (1 or 2)
-  size_t smem;     // dynamic shared memory bytes
-  size_t workspace;  // scratch bytes (partials + tickets), 0 if slices == 1
+  int nb;            // activation rows per tile (1 or 2)
+  int btiles;        // activation-row tiles (grid.y)
+  int64_t tiles;     // 16-row weight tiles
+  int64_t units;     // tiles x (K/256) work units
+  int ctas;          // CTAs per activation-row tile (grid.x)
+  int aligned;       // 1: warps own whole tiles (no split tiles, no tickets)
+  size_t smem;       // dynamic shared memory bytes
+  size_t off_xq, off_xs, off_xsum, off_partial;  // scratch layout (bytes)
+  size_t workspace;  // scratch bytes (tickets + quantised x + partial sums)
 };
 
 QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows);
