@@ -25,6 +25,12 @@
 // entry); the identity mapping (IQ4_XS) uses 32*c32 + 4tq.. and +16+4tq...
 // The activation operand is laid out with the same mapping.
 //
+// Sign-carrying IQ types (SPLIT = true) also expose entry_split(): the
+// unsigned grid magnitudes and the byte mask of the negative positions, so
+// the matvec computes sum x*(+-g) = sum x*g - 2*sum x*(g & mask) with two
+// integer MMAs instead of negating bytes.  Sign masks are expanded from the
+// 8 sign bits in registers (multiply to spread, prmt to sign-replicate).
+//
 // Blocks live in shared memory at the byte alignment the packed stream gives
 // them: every block start is 2-byte aligned; blocks of 56/84/136/144 bytes are
 // 4/8/16-byte aligned.  The readers below use the widest access that the
@@ -43,17 +49,28 @@ __device__ __forceinline__ void apply_sign(uint32_t& lo, uint32_t& hi, uint2 m) 
 }
 
 __device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+
+// Byte masks for 4 sign bits (s4 in [0,15]): byte j = 0xFF if bit j is set.
+// The multiply moves bit j to bit 8j+7 (no carries between the four terms);
+// prmt's sign-replicate mode (selector nibbles 8..B) spreads each byte's msb.
+__device__ __forceinline__ uint32_t byte_mask4(uint32_t s4) {
+  const uint32_t t = s4 * 0x10204080u;
+  uint32_t m;
+  asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(m) : "r"(t));
+  return m;
+}
+
+__device__ __forceinline__ void sign_masks(uint32_t s8, uint32_t& mlo, uint32_t& mhi) {
+  mlo = byte_mask4(s8 & 15u);
+  mhi = byte_mask4((s8 >> 4) & 15u);
+}
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
 template <int T> struct Fast;
 
 // Derived lookup tables, generated at build time from the gguf-py codebooks.
-// kKmask128[i]: 8 byte masks (0xFF = negate) for ksigns index i (parity folded in).
-// kSmask256[s]: 8 byte masks for an explicit sign byte s.
 // kIq1Dual: IQ1 grid x 8 with the +1/8 delta folded in (first 2048 entries)
 //           and with -1/8 (next 2048 entries).
-static __device__ __align__(16) const uint8_t kKmask128[128 * 8] = GSQ_INIT_KMASK128;
-static __device__ __align__(16) const uint8_t kSmask256[256 * 8] = GSQ_INIT_SMASK256;
 static __device__ __align__(16) const int8_t kIq1Dual[2 * 2048 * 8] = GSQ_INIT_IQ1_DUAL;
 
 // Copy a 16-byte aligned table into shared memory with 16-byte accesses.
@@ -67,7 +84,7 @@ __device__ __forceinline__ void copy16(uint8_t* dst, const void* src, int bytes,
 
 template <> struct Fast<T_Q2_K> {
   static constexpr int UNIT = 16, TAB_BYTES = 0;
-  static constexpr bool BLOCKED = true, HAS_BIAS = true;
+  static constexpr bool BLOCKED = true, HAS_BIAS = true, SPLIT = false;
   __device__ static void load_tables(uint8_t*, int, int) {}
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t*, uint32_t& lo, uint32_t& hi) {
     const int i = 4 * c32 + tq;
@@ -85,7 +102,7 @@ template <> struct Fast<T_Q2_K> {
 
 template <> struct Fast<T_Q4_K> {
   static constexpr int UNIT = 32, TAB_BYTES = 0;
-  static constexpr bool BLOCKED = true, HAS_BIAS = true;
+  static constexpr bool BLOCKED = true, HAS_BIAS = true, SPLIT = false;
   __device__ static void load_tables(uint8_t*, int, int) {}
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t*, uint32_t& lo, uint32_t& hi) {
     const uint2 w = ld64a8(b + 16 + (c32 >> 1) * 32 + 8 * tq);
@@ -110,7 +127,7 @@ template <> struct Fast<T_Q4_K> {
 
 template <> struct Fast<T_Q6_K> {
   static constexpr int UNIT = 16, TAB_BYTES = 0;
-  static constexpr bool BLOCKED = true, HAS_BIAS = true;
+  static constexpr bool BLOCKED = true, HAS_BIAS = true, SPLIT = false;
   __device__ static void load_tables(uint8_t*, int, int) {}
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t*, uint32_t& lo, uint32_t& hi) {
     const int i = 4 * c32 + tq;
@@ -138,7 +155,7 @@ __device__ __forceinline__ uint32_t lut16(uint32_t sel, uint32_t t0, uint32_t t1
 
 template <> struct Fast<T_IQ4_XS> {
   static constexpr int UNIT = 32, TAB_BYTES = 16;
-  static constexpr bool BLOCKED = false, HAS_BIAS = false;
+  static constexpr bool BLOCKED = false, HAS_BIAS = false, SPLIT = false;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
     copy16(tab, kKvalues, 16, tid, nthr);
   }
@@ -162,19 +179,24 @@ template <> struct Fast<T_IQ4_XS> {
 // --- IQ lookup types ------------------------------------------------------------
 
 template <> struct Fast<T_IQ2_XXS> {
-  static constexpr int UNIT = 32, GRID = 256 * 8, TAB_BYTES = GRID + 128 * 8;
-  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  static constexpr int UNIT = 32, GRID = 256 * 8, TAB_BYTES = GRID + 128;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = true;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
     copy16(tab, kGridIQ2XXS, GRID, tid, nthr);
-    copy16(tab + GRID, kKmask128, 128 * 8, tid, nthr);
+    copy16(tab + GRID, kKsigns, 128, tid, nthr);
   }
-  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+  __device__ static void entry_split(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo,
+                                     uint32_t& hi, uint32_t& mlo, uint32_t& mhi) {
     const uint8_t* q = b + 2 + 8 * c32;
     const uint32_t aux = ld32a2(q + 4);
     const uint2 g = lds64(tab + 8 * q[tq]);
-    const uint2 m = lds64(tab + GRID + 8 * ((aux >> (7 * tq)) & 127u));
     lo = g.x; hi = g.y;
-    apply_sign(lo, hi, m);
+    sign_masks(tab[GRID + ((aux >> (7 * tq)) & 127u)], mlo, mhi);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    uint32_t mlo, mhi;
+    entry_split(b, c32, tq, tab, lo, hi, mlo, mhi);
+    apply_sign(lo, hi, make_uint2(mlo, mhi));
   }
   __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
     const uint32_t aux = ld32a2(b + 2 + 8 * g + 4);
@@ -184,18 +206,23 @@ template <> struct Fast<T_IQ2_XXS> {
 };
 
 template <> struct Fast<T_IQ2_XS> {
-  static constexpr int UNIT = 16, GRID = 512 * 8, TAB_BYTES = GRID + 128 * 8;
-  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  static constexpr int UNIT = 16, GRID = 512 * 8, TAB_BYTES = GRID + 128;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = true;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
     copy16(tab, kGridIQ2XS, GRID, tid, nthr);
-    copy16(tab + GRID, kKmask128, 128 * 8, tid, nthr);
+    copy16(tab + GRID, kKsigns, 128, tid, nthr);
   }
-  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+  __device__ static void entry_split(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo,
+                                     uint32_t& hi, uint32_t& mlo, uint32_t& mhi) {
     const uint32_t q = ld16a2(b + 2 + 2 * (4 * c32 + tq));
     const uint2 g = lds64(tab + 8 * (q & 511u));
-    const uint2 m = lds64(tab + GRID + 8 * (q >> 9));
     lo = g.x; hi = g.y;
-    apply_sign(lo, hi, m);
+    sign_masks(tab[GRID + (q >> 9)], mlo, mhi);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    uint32_t mlo, mhi;
+    entry_split(b, c32, tq, tab, lo, hi, mlo, mhi);
+    apply_sign(lo, hi, make_uint2(mlo, mhi));
   }
   __device__ static void affine(const uint8_t* b, int s, float& S, float& B) {
     const uint32_t sc = (b[66 + (s >> 1)] >> (4 * (s & 1))) & 15u;
@@ -205,19 +232,21 @@ template <> struct Fast<T_IQ2_XS> {
 };
 
 template <> struct Fast<T_IQ2_S> {
-  static constexpr int UNIT = 16, GRID = 1024 * 8, TAB_BYTES = GRID + 256 * 8;
-  static constexpr bool BLOCKED = true, HAS_BIAS = false;
-  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy16(tab, kGridIQ2S, GRID, tid, nthr);
-    copy16(tab + GRID, kSmask256, 256 * 8, tid, nthr);
-  }
-  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+  static constexpr int UNIT = 16, GRID = 1024 * 8, TAB_BYTES = GRID;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = true;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kGridIQ2S, GRID, tid, nthr); }
+  __device__ static void entry_split(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo,
+                                     uint32_t& hi, uint32_t& mlo, uint32_t& mhi) {
     const int i = 4 * c32 + tq;
     const uint32_t h = (b[66 + (i >> 2)] >> (2 * (i & 3))) & 3u;
     const uint2 g = lds64(tab + 8 * (b[2 + i] | (h << 8)));
-    const uint2 m = lds64(tab + GRID + 8 * b[34 + i]);
     lo = g.x; hi = g.y;
-    apply_sign(lo, hi, m);
+    sign_masks(b[34 + i], mlo, mhi);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    uint32_t mlo, mhi;
+    entry_split(b, c32, tq, tab, lo, hi, mlo, mhi);
+    apply_sign(lo, hi, make_uint2(mlo, mhi));
   }
   __device__ static void affine(const uint8_t* b, int s, float& S, float& B) {
     const uint32_t sc = (b[74 + (s >> 1)] >> (4 * (s & 1))) & 15u;
@@ -227,18 +256,24 @@ template <> struct Fast<T_IQ2_S> {
 };
 
 template <> struct Fast<T_IQ3_XXS> {
-  static constexpr int UNIT = 32, GRID = 256 * 4, TAB_BYTES = GRID + 128 * 8;
-  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  static constexpr int UNIT = 32, GRID = 256 * 4, TAB_BYTES = GRID + 128;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = true;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
     copy16(tab, kGridIQ3XXS, GRID, tid, nthr);
-    copy16(tab + GRID, kKmask128, 128 * 8, tid, nthr);
+    copy16(tab + GRID, kKsigns, 128, tid, nthr);
   }
-  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+  __device__ static void entry_split(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo,
+                                     uint32_t& hi, uint32_t& mlo, uint32_t& mhi) {
     const uint32_t idx = ld16a2(b + 2 + 8 * c32 + 2 * tq);
     const uint32_t aux = ld32a2(b + 66 + 4 * c32);
     lo = lds32(tab + 4 * (idx & 255u));
     hi = lds32(tab + 4 * (idx >> 8));
-    apply_sign(lo, hi, lds64(tab + GRID + 8 * ((aux >> (7 * tq)) & 127u)));
+    sign_masks(tab[GRID + ((aux >> (7 * tq)) & 127u)], mlo, mhi);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    uint32_t mlo, mhi;
+    entry_split(b, c32, tq, tab, lo, hi, mlo, mhi);
+    apply_sign(lo, hi, make_uint2(mlo, mhi));
   }
   __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
     const uint32_t aux = ld32a2(b + 66 + 4 * g);
@@ -248,18 +283,21 @@ template <> struct Fast<T_IQ3_XXS> {
 };
 
 template <> struct Fast<T_IQ3_S> {
-  static constexpr int UNIT = 32, GRID = 512 * 4, TAB_BYTES = GRID + 256 * 8;
-  static constexpr bool BLOCKED = true, HAS_BIAS = false;
-  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy16(tab, kGridIQ3S, GRID, tid, nthr);
-    copy16(tab + GRID, kSmask256, 256 * 8, tid, nthr);
-  }
-  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+  static constexpr int UNIT = 32, GRID = 512 * 4, TAB_BYTES = GRID;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = true;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kGridIQ3S, GRID, tid, nthr); }
+  __device__ static void entry_split(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo,
+                                     uint32_t& hi, uint32_t& mlo, uint32_t& mhi) {
     const uint32_t idx = ld16a2(b + 2 + 8 * c32 + 2 * tq);
     const uint32_t qh = b[66 + c32] >> (2 * tq);
     lo = lds32(tab + 4 * ((idx & 255u) | ((qh & 1u) << 8)));
     hi = lds32(tab + 4 * ((idx >> 8) | ((qh & 2u) << 7)));
-    apply_sign(lo, hi, lds64(tab + GRID + 8 * b[74 + 4 * c32 + tq]));
+    sign_masks(b[74 + 4 * c32 + tq], mlo, mhi);
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    uint32_t mlo, mhi;
+    entry_split(b, c32, tq, tab, lo, hi, mlo, mhi);
+    apply_sign(lo, hi, make_uint2(mlo, mhi));
   }
   __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
     const uint32_t sc = (b[106 + (g >> 1)] >> (4 * (g & 1))) & 15u;
@@ -270,7 +308,7 @@ template <> struct Fast<T_IQ3_S> {
 
 template <> struct Fast<T_IQ1_S> {
   static constexpr int UNIT = 32, TAB_BYTES = 2 * 2048 * 8;
-  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = false;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kIq1Dual, TAB_BYTES, tid, nthr); }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const uint32_t qh = ld16a2(b + 34 + 2 * c32);
@@ -287,7 +325,7 @@ template <> struct Fast<T_IQ1_S> {
 
 template <> struct Fast<T_IQ1_M> {
   static constexpr int UNIT = 16, TAB_BYTES = 2 * 2048 * 8;
-  static constexpr bool BLOCKED = true, HAS_BIAS = false;
+  static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = false;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kIq1Dual, TAB_BYTES, tid, nthr); }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     const int i = 4 * c32 + tq;

@@ -218,12 +218,14 @@ __global__ void __launch_bounds__(QMV_THREADS, 4) qmv_kernel(const QmvArgs a) {
 
   // Producer: stage the next chunk (16 rows of one tile, up to CB blocks,
   // never crossing the tile's end or the warp's range end).
-  int64_t pu = u0;
+  // Iterators walk (tile, block) incrementally: no divisions in the loop.
+  int64_t pu = u0, ptile = u0 / kb;
+  int pkb = (int)(u0 - ptile * kb);
   int issued = 0;
   auto issue_next = [&]() {
     const int s = issued % QMV_STAGES;
-    const int64_t tile = pu / kb;
-    const int kb0 = (int)(pu - tile * kb);
+    const int64_t tile = ptile;
+    const int kb0 = pkb;
     const int nb = (int)(u1 - pu < (int64_t)min(G::CB, kb - kb0) ? u1 - pu : (int64_t)min(G::CB, kb - kb0));
     uint32_t bytes = 0;
     if (lane < 16) {
@@ -248,6 +250,8 @@ __global__ void __launch_bounds__(QMV_THREADS, 4) qmv_kernel(const QmvArgs a) {
     __syncwarp();
     if (lane == 0) mbar_arrive_expect_tx(&wbars[s], total);
     pu += nb;
+    pkb += nb;
+    if (pkb == kb) { pkb = 0; ptile++; }
     issued++;
   };
   while (issued < QMV_STAGES && pu < u1) issue_next();
@@ -273,13 +277,15 @@ __global__ void __launch_bounds__(QMV_THREADS, 4) qmv_kernel(const QmvArgs a) {
   float acc0 = 0.f, acc1 = 0.f;
   bool ok = true;
   int consumed = 0;
-  int64_t cu = u0, seg = u0;
+  int64_t cu = u0, seg = u0, ctile = u0 / kb;
+  int ckb = (int)(u0 - ctile * kb);
+  const int64_t first_tile = ctile;
   while (cu < u1) {
     const int s = consumed % QMV_STAGES;
     ok = mbar_wait_bounded(&wbars[s], (uint32_t)((consumed / QMV_STAGES) & 1), a.err);
     if (!ok) break;
-    const int64_t tile = cu / kb;
-    const int kb0 = (int)(cu - tile * kb);
+    const int64_t tile = ctile;
+    const int kb0 = ckb;
     const int nb = (int)(u1 - cu < (int64_t)min(G::CB, kb - kb0) ? u1 - cu : (int64_t)min(G::CB, kb - kb0));
     const int64_t row0 = tile * 16 + g;
     const uint8_t* st = wstage + (size_t)s * G::STAGE;
@@ -288,57 +294,81 @@ __global__ void __launch_bounds__(QMV_THREADS, 4) qmv_kernel(const QmvArgs a) {
     for (int bi = 0; bi < nb; bi++) {
       const uint8_t* b0 = r0p + bi * G::BB;
       const uint8_t* b1 = r1p + bi * G::BB;
-      const int64_t kblk = (int64_t)(kb0 + bi) * QK;
+      const int kblk = (kb0 + bi) * QK;
+      // Per-block activation bases: the set loop below then uses immediate offsets.
+      const int8_t* xb = xrow + kblk;
+      const float* xsb = xs_row + (kblk >> 5);
+      const float* xub = xsum_row + (kblk >> 4);
 #pragma unroll
       for (int set = 0; set < SETS; set++) {
-        const int64_t kset = kblk + set * KSET;
+        const int kset = set * KSET;
         // Activation words for the one MMA of this set where column g is live.
         uint32_t xw0, xw1;
         int jsel;
         if constexpr (UNIT == 32) {
           jsel = s_col;
           if constexpr (F::BLOCKED) {
-            const uint2 w = __ldg(reinterpret_cast<const uint2*>(xrow + kset + 32 * s_col + 8 * tq));
+            const uint2 w = __ldg(reinterpret_cast<const uint2*>(xb + kset + 32 * s_col + 8 * tq));
             xw0 = w.x; xw1 = w.y;
           } else {
-            xw0 = __ldg(reinterpret_cast<const uint32_t*>(xrow + kset + 32 * s_col + 4 * tq));
-            xw1 = __ldg(reinterpret_cast<const uint32_t*>(xrow + kset + 32 * s_col + 16 + 4 * tq));
+            xw0 = __ldg(reinterpret_cast<const uint32_t*>(xb + kset + 32 * s_col + 4 * tq));
+            xw1 = __ldg(reinterpret_cast<const uint32_t*>(xb + kset + 32 * s_col + 16 + 4 * tq));
           }
         } else {
           jsel = s_col >> 1;
           const bool live = (s_col & 1) == (tq >> 1);
-          const uint2 w = __ldg(reinterpret_cast<const uint2*>(xrow + kset + 32 * jsel + 8 * tq));
+          const uint2 w = __ldg(reinterpret_cast<const uint2*>(xb + kset + 32 * jsel + 8 * tq));
           xw0 = live ? w.x : 0u;
           xw1 = live ? w.y : 0u;
         }
         // Two independent accumulator chains (even / odd MMAs) halve the
-        // dependent tensor-core latency per set.
+        // dependent tensor-core latency per set.  Sign-carrying formats run a
+        // second pair of chains on the negative-position magnitudes.
         int C[4] = {0, 0, 0, 0}, Cb[4] = {0, 0, 0, 0};
+        int Nn[4] = {0, 0, 0, 0}, Nb[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int j = 0; j < MMAS; j++) {
           const int c32 = set * MMAS + j;
-          uint32_t a0, a1, a2, a3;
-          F::entry(b0, c32, tq, tab, a0, a2);
-          F::entry(b1, c32, tq, tab, a1, a3);
           const bool on = (j == jsel);
-          if (j & 1) mma_s8(Cb, a0, a1, a2, a3, on ? xw0 : 0u, on ? xw1 : 0u);
-          else mma_s8(C, a0, a1, a2, a3, on ? xw0 : 0u, on ? xw1 : 0u);
+          const uint32_t bx0 = on ? xw0 : 0u, bx1 = on ? xw1 : 0u;
+          if constexpr (F::SPLIT) {
+            uint32_t a0, a1, a2, a3, m0, m1, m2, m3;
+            F::entry_split(b0, c32, tq, tab, a0, a2, m0, m2);
+            F::entry_split(b1, c32, tq, tab, a1, a3, m1, m3);
+            if (j & 1) {
+              mma_s8(Cb, a0, a1, a2, a3, bx0, bx1);
+              mma_s8(Nb, a0 & m0, a1 & m1, a2 & m2, a3 & m3, bx0, bx1);
+            } else {
+              mma_s8(C, a0, a1, a2, a3, bx0, bx1);
+              mma_s8(Nn, a0 & m0, a1 & m1, a2 & m2, a3 & m3, bx0, bx1);
+            }
+          } else {
+            uint32_t a0, a1, a2, a3;
+            F::entry(b0, c32, tq, tab, a0, a2);
+            F::entry(b1, c32, tq, tab, a1, a3);
+            if (j & 1) mma_s8(Cb, a0, a1, a2, a3, bx0, bx1);
+            else mma_s8(C, a0, a1, a2, a3, bx0, bx1);
+          }
         }
         if constexpr (MMAS > 1) {
 #pragma unroll
           for (int i = 0; i < 4; i++) C[i] += Cb[i];
         }
+        if constexpr (F::SPLIT) {
+#pragma unroll
+          for (int i = 0; i < 4; i++) C[i] -= 2 * (Nn[i] + Nb[i]);
+        }
         const int unit = set * UPS + s_ep;
-        const int64_t ku = kblk + unit * UNIT;
-        const float xsv = __ldg(xs_row + (ku >> 5));
+        const int ku = unit * UNIT;  // within the block
+        const float xsv = __ldg(xsb + (ku >> 5));
         float S0, B0, S1, B1;
         F::affine(b0, unit, S0, B0);
         F::affine(b1, unit, S1, B1);
         acc0 = fmaf(S0, (float)(C[0] * 256 + C[1]) * xsv, acc0);
         acc1 = fmaf(S1, (float)(C[2] * 256 + C[3]) * xsv, acc1);
         if constexpr (F::HAS_BIAS) {
-          float xu = __ldg(xsum_row + (ku >> 4));
-          if constexpr (UNIT == 32) xu += __ldg(xsum_row + (ku >> 4) + 1);
+          float xu = __ldg(xub + (ku >> 4));
+          if constexpr (UNIT == 32) xu += __ldg(xub + (ku >> 4) + 1);
           acc0 = fmaf(B0, xu, acc0);
           acc1 = fmaf(B1, xu, acc1);
         }
@@ -348,6 +378,8 @@ __global__ void __launch_bounds__(QMV_THREADS, 4) qmv_kernel(const QmvArgs a) {
     consumed++;
     if (pu < u1) issue_next();  // refill the stage just released
     cu += nb;
+    ckb += nb;
+    if (ckb == kb) { ckb = 0; ctile++; }
 
     if (kb0 + nb == kb || cu == u1) {
       // ---- end of this warp's segment of `tile`: reduce the quad lanes that
@@ -366,7 +398,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 4) qmv_kernel(const QmvArgs a) {
           if (rg1 < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rg1, acc1);
         }
       } else {
-        const int slot = (tile == u0 / kb) ? 0 : 1;
+        const int slot = (tile == first_tile) ? 0 : 1;
         float* pp = a.partial + (((int64_t)btile * GW + gw) * 2 + slot) * NB * 16 + b_ep * 16;
         if (writer) {
           pp[g] = acc0;
