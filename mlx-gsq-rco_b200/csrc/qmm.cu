@@ -183,8 +183,8 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
   if (warp == 0) {
     // ---------------- activation tiles (TMA) ----------------
     pdl_wait();  // the activations are written by the preceding kernel
+    int s = 0, n = 0;  // stage and its use count, advanced without divisions
     for (int ks = 0; ks < nks && ok; ks++) {
-      const int s = ks % NS, n = ks / NS;
       if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
       if (!ok) break;
       if (lane == 0) {
@@ -192,13 +192,14 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
         tma_load_2d(bstage + (size_t)s * bn * 128, &xmap, ks * QMM_BK, m0, &full_b[s]);
       }
       __syncwarp();
+      if (++s == NS) { s = 0; n++; }
     }
   } else if (warp == 2) {
     // ---------------- packed weight blocks ----------------
     const uintptr_t pbase = reinterpret_cast<uintptr_t>(a.packed);
     const uint64_t policy = l2_policy_evict_first();
-    for (int kb = 0; kb < nkb && ok; kb++) {
-      const int ps = kb % PST, pn = kb / PST;
+    int ps = 0, pn = 0;
+    for (int kb = 0; kb < nkb && ok; kb++, (++ps == PST ? (ps = 0, pn++) : 0)) {
       if (pn > 0) ok = mbar_wait_bounded(&pempty[ps], (uint32_t)((pn - 1) & 1), a.err);
       if (!ok) break;
       uint32_t bytes = 0;
@@ -227,8 +228,8 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     const uint32_t idesc = f16_idesc(bn);
-    for (int ks = 0; ks < nks && ok; ks++) {
-      const int s = ks % NS, n = ks / NS;
+    int s = 0, n = 0;
+    for (int ks = 0; ks < nks && ok; ks++, (++s == NS ? (s = 0, n++) : 0)) {
       ok = mbar_wait_bounded(&full_a[s], (uint32_t)(n & 1), a.err) &&
            mbar_wait_bounded(&full_b[s], (uint32_t)(n & 1), a.err);
       if (!ok) break;
@@ -258,13 +259,13 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
     const bool live = row < a.N;
     const int64_t roff = row * a.row_bytes;
     const __half2 off2 = __float2half2_rn(1152.f);
-    for (int kb = 0; kb < nkb && ok; kb++) {
-      const int ps = kb % PST;
-      ok = mbar_wait_bounded(&pfull[ps], (uint32_t)((kb / PST) & 1), a.err);
+    int ps = 0, pn = 0;  // packed stage / use count
+    int s = 0, n = 0;    // A/B stage / use count
+    for (int kb = 0; kb < nkb && ok; kb++, (++ps == PST ? (ps = 0, pn++) : 0)) {
+      ok = mbar_wait_bounded(&pfull[ps], (uint32_t)(pn & 1), a.err);
       if (!ok) break;
       const uint8_t* blk = pstage + (size_t)ps * G::PSTAGE + r * G::PROWB + (int)((roff + (int64_t)kb * G::BB) & 15);
-      for (int q = 0; q < 4 && ok; q++) {
-        const int ks = 4 * kb + q, s = ks % NS, n = ks / NS;
+      for (int q = 0; q < 4 && ok; q++, (++s == NS ? (s = 0, n++) : 0)) {
         if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
         if (!ok) break;
         uint8_t* trow = astage + (size_t)s * QMM_BM * 128 + r * 128;
