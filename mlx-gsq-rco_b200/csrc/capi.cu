@@ -112,6 +112,8 @@ int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_
   if (!aligned(x, 16) || !aligned(y, dtype_size(y_dtype)))
     return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned and y aligned to its dtype");
   const QmvPlan p = qmv_plan(qtype, N, K, (int)rows);
+  if (p.ctas <= 0)
+    return fail(GSQ_ERR_SIZE, "matrix too large for the matvec (N=%lld, K=%lld)", (long long)N, (long long)K);
   if (p.workspace > 0 && (!workspace || workspace_bytes < p.workspace || !aligned(workspace, 256)))
     return fail(GSQ_ERR_WORKSPACE, "gsq_qmv needs %zu workspace bytes (256-byte aligned), got %zu", p.workspace,
                 workspace_bytes);

@@ -60,6 +60,11 @@ __device__ __forceinline__ uint32_t byte_mask4(uint32_t s4) {
   return m;
 }
 
+// The IQ2/IQ3 sign byte of a 7-bit sign index: bit 7 is the parity of the
+// seven stored bits, so that every 8-sign group has an even count of minus
+// signs (equal to gguf-py's ksigns table, entry for entry).
+__device__ __forceinline__ uint32_t ksign(uint32_t i7) { return i7 | ((__popc(i7) & 1u) << 7); }
+
 __device__ __forceinline__ void sign_masks(uint32_t s8, uint32_t& mlo, uint32_t& mhi) {
   mlo = byte_mask4(s8 & 15u);
   mhi = byte_mask4((s8 >> 4) & 15u);
@@ -113,15 +118,16 @@ template <> struct Fast<T_Q4_K> {
   __device__ static void affine(const uint8_t* b, int g, float& S, float& B) {
     // 6-bit scale/min of group g from the 12 packed bytes (branch-free):
     // g < 4: low 6 bits of bytes g, 4+g; g >= 4: nibbles of byte 8+j plus the
-    // top 2 bits of bytes j, 4+j (j = g-4).
-    const uint8_t* s = b + 4;
-    const int j = g & 3;
-    const uint32_t d6 = s[j], m6 = s[4 + j], hl = s[8 + j];
+    // top 2 bits of bytes j, 4+j (j = g-4).  Q4_K blocks are 16-byte aligned,
+    // so the header is read as four words that every call on the same block
+    // shares.
+    const uint32_t dm = ld32a4(b), q0 = ld32a4(b + 4), q1 = ld32a4(b + 8), q2 = ld32a4(b + 12);
+    const int sh = 8 * (g & 3);
     const bool hi = g >= 4;
-    const uint32_t sc = hi ? (hl & 15u) | ((d6 >> 2) & 48u) : d6 & 63u;
-    const uint32_t mn = hi ? (hl >> 4) | ((m6 >> 2) & 48u) : m6 & 63u;
-    S = h2f_bits(ld16a2(b)) * (float)sc;
-    B = -h2f_bits(ld16a2(b + 2)) * (float)mn;
+    const uint32_t sc = hi ? ((q2 >> sh) & 15u) | ((q0 >> (sh + 2)) & 48u) : (q0 >> sh) & 63u;
+    const uint32_t mn = hi ? ((q2 >> (sh + 4)) & 15u) | ((q1 >> (sh + 2)) & 48u) : (q1 >> sh) & 63u;
+    S = h2f_bits(dm & 0xFFFFu) * (float)sc;
+    B = -h2f_bits(dm >> 16) * (float)mn;
   }
 };
 
@@ -179,19 +185,16 @@ template <> struct Fast<T_IQ4_XS> {
 // --- IQ lookup types ------------------------------------------------------------
 
 template <> struct Fast<T_IQ2_XXS> {
-  static constexpr int UNIT = 32, GRID = 256 * 8, TAB_BYTES = GRID + 128;
+  static constexpr int UNIT = 32, GRID = 256 * 8, TAB_BYTES = GRID;
   static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = true;
-  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy16(tab, kGridIQ2XXS, GRID, tid, nthr);
-    copy16(tab + GRID, kKsigns, 128, tid, nthr);
-  }
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kGridIQ2XXS, GRID, tid, nthr); }
   __device__ static void entry_split(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo,
                                      uint32_t& hi, uint32_t& mlo, uint32_t& mhi) {
     const uint8_t* q = b + 2 + 8 * c32;
     const uint32_t aux = ld32a2(q + 4);
     const uint2 g = lds64(tab + 8 * q[tq]);
     lo = g.x; hi = g.y;
-    sign_masks(tab[GRID + ((aux >> (7 * tq)) & 127u)], mlo, mhi);
+    sign_masks(ksign((aux >> (7 * tq)) & 127u), mlo, mhi);
   }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     uint32_t mlo, mhi;
@@ -206,18 +209,15 @@ template <> struct Fast<T_IQ2_XXS> {
 };
 
 template <> struct Fast<T_IQ2_XS> {
-  static constexpr int UNIT = 16, GRID = 512 * 8, TAB_BYTES = GRID + 128;
+  static constexpr int UNIT = 16, GRID = 512 * 8, TAB_BYTES = GRID;
   static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = true;
-  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy16(tab, kGridIQ2XS, GRID, tid, nthr);
-    copy16(tab + GRID, kKsigns, 128, tid, nthr);
-  }
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kGridIQ2XS, GRID, tid, nthr); }
   __device__ static void entry_split(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo,
                                      uint32_t& hi, uint32_t& mlo, uint32_t& mhi) {
     const uint32_t q = ld16a2(b + 2 + 2 * (4 * c32 + tq));
     const uint2 g = lds64(tab + 8 * (q & 511u));
     lo = g.x; hi = g.y;
-    sign_masks(tab[GRID + (q >> 9)], mlo, mhi);
+    sign_masks(ksign(q >> 9), mlo, mhi);
   }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     uint32_t mlo, mhi;
@@ -256,19 +256,16 @@ template <> struct Fast<T_IQ2_S> {
 };
 
 template <> struct Fast<T_IQ3_XXS> {
-  static constexpr int UNIT = 32, GRID = 256 * 4, TAB_BYTES = GRID + 128;
+  static constexpr int UNIT = 32, GRID = 256 * 4, TAB_BYTES = GRID;
   static constexpr bool BLOCKED = true, HAS_BIAS = false, SPLIT = true;
-  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) {
-    copy16(tab, kGridIQ3XXS, GRID, tid, nthr);
-    copy16(tab + GRID, kKsigns, 128, tid, nthr);
-  }
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kGridIQ3XXS, GRID, tid, nthr); }
   __device__ static void entry_split(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo,
                                      uint32_t& hi, uint32_t& mlo, uint32_t& mhi) {
     const uint32_t idx = ld16a2(b + 2 + 8 * c32 + 2 * tq);
     const uint32_t aux = ld32a2(b + 66 + 4 * c32);
     lo = lds32(tab + 4 * (idx & 255u));
     hi = lds32(tab + 4 * (idx >> 8));
-    sign_masks(tab[GRID + ((aux >> (7 * tq)) & 127u)], mlo, mhi);
+    sign_masks(ksign((aux >> (7 * tq)) & 127u), mlo, mhi);
   }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     uint32_t mlo, mhi;

@@ -32,14 +32,15 @@ static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 b
 // Launch plan of one QMV call: grid shape, work split and scratch layout.
 struct QmvPlan {
   int nb;            // activation rows per tile (1 or 2)
-  int btiles;        // activation-row tiles (grid.y)
+  int btiles;        // activation-row tiles (grid.z)
   int64_t tiles;     // 16-row weight tiles
-  int64_t units;     // tiles x (K/256) work units
-  int ctas;          // CTAs per activation-row tile (grid.x)
-  int aligned;       // 1: warps own whole tiles (no split tiles, no tickets)
+  int slices;        // K-slices (grid.y)
+  int bps;           // 256-blocks per K-slice
+  int ctas;          // persistent CTAs per K-slice (grid.x)
+  int aligned;       // 1: CTAs own whole tiles (no partial sums, no tickets)
   size_t smem;       // dynamic shared memory bytes
-  size_t off_xq, off_xs, off_xsum, off_partial;  // scratch layout (bytes)
-  size_t workspace;  // scratch bytes (tickets + quantised x + partial sums)
+  size_t off_full, off_piece;  // scratch layout (bytes)
+  size_t workspace;  // scratch bytes (tickets + partial sums), 0 when no tile is split
 };
 
 QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows);

@@ -85,6 +85,7 @@ extern "C" GSQ_API int gsq_qmv_noalloc(int qtype, const void* x, int x_dtype, co
       (reinterpret_cast<uintptr_t>(y) % ysz))
     return set_last_error(GSQ_ERR_ALIGN, "gsq_qmv_noalloc: packed and x must be 16-byte aligned");
   const gsq::QmvPlan p = gsq::qmv_plan(qtype, N, K, (int)rows);
+  if (p.ctas <= 0) return set_last_error(GSQ_ERR_SIZE, "gsq_qmv_noalloc: matrix too large for the matvec");
   if (p.workspace > kScratchBytes) {
     char msg[256];
     snprintf(msg, sizeof(msg),
