@@ -38,6 +38,7 @@ struct QmvPlan {
   int bps;           // 256-blocks per K-slice
   int ctas;          // persistent CTAs per K-slice (grid.x)
   int aligned;       // 1: CTAs own whole tiles (no partial sums, no tickets)
+  int ns;            // ring stages (2..4)
   size_t smem;       // dynamic shared memory bytes
   size_t off_full, off_piece;  // scratch layout (bytes)
   size_t workspace;  // scratch bytes (tickets + partial sums), 0 when no tile is split

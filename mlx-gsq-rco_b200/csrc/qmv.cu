@@ -41,13 +41,15 @@
 
 namespace gsq {
 
-constexpr int QMV_CWARPS = 8;                          // consumer warps per CTA
+constexpr int QMV_CWARPS = 8;                          // consumer (tensor-core) warps per CTA
 constexpr int QMV_CTHREADS = 32 * QMV_CWARPS;
-constexpr int QMV_THREADS = QMV_CTHREADS + 32;         // + one producer warp
+constexpr int QMV_PRODUCER = QMV_CWARPS;               // warp streaming packed bytes into the ring
+constexpr int QMV_COMBINER = QMV_CWARPS + 1;           // warp combining tiles split between CTAs
+constexpr int QMV_THREADS = QMV_CTHREADS + 64;
+constexpr int QMV_NS_MAX = 4;                          // ring stages at most
 constexpr int QMV_CTA_SMEM = 112 * 1024;               // two CTAs per SM
 constexpr int QMV_XBYTES_PER_BLOCK = 2 * QK + 8 * 4 + 16 * 4;  // per activation row: levels, scales, half sums
-constexpr int QMV_XBUDGET = 24 * 1024;                 // activation slice bytes per CTA
-constexpr int QMV_RED_BUFS = 5;                       // per-warp row-sum buffers (>= ring depth + 1)
+constexpr int QMV_RED_BUFS = QMV_NS_MAX + 1;          // per-warp row-sum buffers (ring depth + 1)
 constexpr int QMV_RED_BYTES = QMV_RED_BUFS * QMV_CWARPS * 32 * 4;
 // Scratch layout: a fixed region of ticket counters first, then the partial
 // sums.  Every completed call returns the tickets it used to zero and nothing
@@ -65,7 +67,7 @@ struct QmvArgs {
   unsigned* tickets;   // [btiles][tiles]
   int* err;
   int64_t N, K, row_bytes, packed_bytes, tiles;
-  int rows, x_dtype, y_dtype, kb, bps, slices, aligned;
+  int rows, x_dtype, y_dtype, kb, bps, slices, aligned, ns;
 };
 
 template <int T>
@@ -80,12 +82,9 @@ struct QmvGeom {
   static constexpr int STAGE = 16 * ROWB;
   static constexpr int TAB = (Fast<T>::TAB_BYTES + 127) / 128 * 128;
   static constexpr int FIXED = 128 /*align*/ + TAB + 256 /*mbarriers*/ + QMV_RED_BYTES;
-  static constexpr int NS_FIT = (QMV_CTA_SMEM - FIXED - QMV_XBUDGET) / STAGE;
-  static constexpr int NS = NS_FIT > 4 ? 4 : NS_FIT;
-  static_assert(NS >= 2, "ring must hold two stages");
-  static constexpr int RING = NS * STAGE;
-  static_assert(NS + 1 <= QMV_RED_BUFS, "row-sum buffers must outnumber the ring stages");
-  static constexpr size_t SMEM_MAX = (size_t)FIXED + RING + QMV_XBUDGET;
+  // Two stages plus the activations of one block must fit; the ring depth
+  // (2..4 stages) and the K-slice width are chosen per call.
+  static_assert(FIXED + 2 * STAGE + 2 * QMV_XBYTES_PER_BLOCK <= QMV_CTA_SMEM, "ring must hold two stages");
 };
 
 __device__ __forceinline__ void named_sync_consumers() {
@@ -95,39 +94,35 @@ __device__ __forceinline__ void named_sync_consumers() {
 // ---------------------------------------------------------------------------
 // Activation quantisation (CTA prologue).
 
-template <typename XT> __device__ __forceinline__ void load32(const void* x, int64_t i, float (&v)[32]);
-template <> __device__ __forceinline__ void load32<float>(const void* x, int64_t i, float (&v)[32]) {
-  const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + i);
+// 8 consecutive activations, as raw 16-byte words (two for fp32).
+template <typename XT>
+__device__ __forceinline__ void load8(const void* x, int64_t i, uint4 (&r)[2]) {
+  const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const XT*>(x) + i);
+  r[0] = __ldcg(p);
+  r[1] = sizeof(XT) == 4 ? __ldcg(p + 1) : make_uint4(0, 0, 0, 0);
+}
+
+template <typename XT> __device__ __forceinline__ void unpack8(const uint4 (&r)[2], float (&v)[8]);
+template <> __device__ __forceinline__ void unpack8<float>(const uint4 (&r)[2], float (&v)[8]) {
+  v[0] = __uint_as_float(r[0].x); v[1] = __uint_as_float(r[0].y);
+  v[2] = __uint_as_float(r[0].z); v[3] = __uint_as_float(r[0].w);
+  v[4] = __uint_as_float(r[1].x); v[5] = __uint_as_float(r[1].y);
+  v[6] = __uint_as_float(r[1].z); v[7] = __uint_as_float(r[1].w);
+}
+template <> __device__ __forceinline__ void unpack8<__half>(const uint4 (&r)[2], float (&v)[8]) {
+  const uint32_t w[4] = {r[0].x, r[0].y, r[0].z, r[0].w};
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const float4 f = __ldcg(p + j);
-    v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+  for (int t = 0; t < 4; t++) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[t]));
+    v[2 * t] = f.x; v[2 * t + 1] = f.y;
   }
 }
-template <> __device__ __forceinline__ void load32<__half>(const void* x, int64_t i, float (&v)[32]) {
-  const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(x) + i);
+template <> __device__ __forceinline__ void unpack8<__nv_bfloat16>(const uint4 (&r)[2], float (&v)[8]) {
+  const uint32_t w[4] = {r[0].x, r[0].y, r[0].z, r[0].w};
 #pragma unroll
-  for (int j = 0; j < 4; j++) {
-    const uint4 u = __ldcg(p + j);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[t]));
-      v[8 * j + 2 * t] = f.x; v[8 * j + 2 * t + 1] = f.y;
-    }
-  }
-}
-template <> __device__ __forceinline__ void load32<__nv_bfloat16>(const void* x, int64_t i, float (&v)[32]) {
-  const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(x) + i);
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    const uint4 u = __ldcg(p + j);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-      v[8 * j + 2 * t] = __uint_as_float(w[t] << 16);
-      v[8 * j + 2 * t + 1] = __uint_as_float(w[t] & 0xFFFF0000u);
-    }
+  for (int t = 0; t < 4; t++) {
+    v[2 * t] = __uint_as_float(w[t] << 16);
+    v[2 * t + 1] = __uint_as_float(w[t] & 0xFFFF0000u);
   }
 }
 
@@ -143,93 +138,109 @@ __device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2,
   return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
 }
 
-// Quantise 32 values: hi/lo int8 levels into qh/ql (32 bytes each), returns
-// s/256 and the two 16-wide sums.
-__device__ __forceinline__ void quant32(const float (&v)[32], int8_t* qh, int8_t* ql, float& xs, float& s0,
-                                        float& s1) {
-  float amax = 0.f;
-  s0 = 0.f; s1 = 0.f;
+// Slice layout in shared memory (KS = bps*256 activations per row):
+//   xq   [NB][2][KS] int8   levels hi, lo:  x ~= s * (hi + lo/256)
+//   xs   [NB][KS/32] fp32   s/256 per 32-group (s = max|x|/127)
+//   xsum [NB][KS/16] fp32   sum of each 16-wide half
+// Every consumer thread issues the loads of up to CH chunks of 8 values
+// first (one round trip per CH * 256 chunks, a K = 20480 row at fp16), then
+// quantises them; the four lanes holding a 32-group combine max and sums with
+// shuffles.
+template <int NB, typename XT, int CH>
+__device__ __forceinline__ void quantise_round(const QmvArgs& a, int btile, int kb0, int KS, int per_row, int total,
+                                               int base, int8_t* xq, float* xs, float* xsum) {
+  uint4 raw[CH][2];
 #pragma unroll
-  for (int j = 0; j < 32; j++) {
-    amax = fmaxf(amax, fabsf(v[j]));
-    if (j < 16) s0 += v[j]; else s1 += v[j];
+  for (int i = 0; i < CH; i++) {
+    const int c = base + threadIdx.x + i * QMV_CTHREADS;
+    const int b = c >= per_row ? 1 : 0;  // NB <= 2
+    const int row = btile * NB + b;
+    if (c < total && row < a.rows)
+      load8<XT>(a.x, (int64_t)row * a.K + (int64_t)kb0 * QK + (c - b * per_row) * 8, raw[i]);
+    else
+      raw[i][0] = raw[i][1] = make_uint4(0, 0, 0, 0);
   }
-  const float inv = amax > 0.f ? 127.f / amax : 0.f;
-  // |u| <= 127 (up to rounding), so hi never saturates below -127; the
-  // residual level lo = 256 (u - hi) saturates to [-128, 127].
-  uint32_t wh[8], wl[8];
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
-    uint32_t h[4], l[4];
+  for (int i = 0; i < CH; i++) {
+    if (base + i * QMV_CTHREADS >= total) break;  // uniform over the CTA
+    const int c = base + threadIdx.x + i * QMV_CTHREADS;
+    float v[8];
+    unpack8<XT>(raw[i], v);
+    float am = 0.f, sum = 0.f;
 #pragma unroll
-    for (int t = 0; t < 4; t++) {
-      const float u = v[4 * j + t] * inv;
-      const float hr = rintf(u);
-      h[t] = cvt_s8(hr);
-      l[t] = cvt_s8((u - hr) * 256.f);
+    for (int j = 0; j < 8; j++) {
+      am = fmaxf(am, fabsf(v[j]));
+      sum += v[j];
     }
-    wh[j] = pack4(h[0], h[1], h[2], h[3]);
-    wl[j] = pack4(l[0], l[1], l[2], l[3]);
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    const float half = sum + __shfl_xor_sync(0xffffffffu, sum, 1);
+    const float inv = am > 0.f ? 127.f / am : 0.f;
+    // |u| <= 127 (up to rounding), so hi never saturates below -127; the
+    // residual level lo = 256 (u - hi) saturates to [-128, 127].
+    uint32_t h[8], l[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float u = v[j] * inv;
+      const float hr = rintf(u);
+      h[j] = cvt_s8(hr);
+      l[j] = cvt_s8((u - hr) * 256.f);
+    }
+    if (c < total) {
+      const int b = c >= per_row ? 1 : 0;
+      const int cc = c - b * per_row;
+      int8_t* qh = xq + (b * 2) * KS + cc * 8;
+      *reinterpret_cast<uint2*>(qh) = make_uint2(pack4(h[0], h[1], h[2], h[3]), pack4(h[4], h[5], h[6], h[7]));
+      *reinterpret_cast<uint2*>(qh + KS) = make_uint2(pack4(l[0], l[1], l[2], l[3]), pack4(l[4], l[5], l[6], l[7]));
+      if ((cc & 3) == 0) xs[b * (KS / 32) + (cc >> 2)] = am / (127.f * 256.f);
+      if ((cc & 1) == 0) xsum[b * (KS / 16) + (cc >> 1)] = half;
+    }
   }
-  reinterpret_cast<uint4*>(qh)[0] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-  reinterpret_cast<uint4*>(qh)[1] = make_uint4(wh[4], wh[5], wh[6], wh[7]);
-  reinterpret_cast<uint4*>(ql)[0] = make_uint4(wl[0], wl[1], wl[2], wl[3]);
-  reinterpret_cast<uint4*>(ql)[1] = make_uint4(wl[4], wl[5], wl[6], wl[7]);
-  xs = amax / (127.f * 256.f);
 }
 
-// Slice layout in shared memory (KS = bps*256 activations per row):
-//   xq   [NB][2][KS] int8   levels hi, lo
-//   xs   [NB][KS/32] fp32   s/256 per 32-group
-//   xsum [NB][KS/16] fp32   sum of each 16-wide half
+
+template <int NB, typename XT>
+__device__ void quantise_slice_t(const QmvArgs& a, int btile, int kb0, int w, int KS, int8_t* xq, float* xs,
+                                 float* xsum) {
+  constexpr int CH = sizeof(XT) == 4 ? 5 : 10;
+  const int per_row = w * 32;  // 8-value chunks per activation row
+  const int total = NB * per_row;
+  for (int base = 0; base < total; base += CH * QMV_CTHREADS)
+    quantise_round<NB, XT, CH>(a, btile, kb0, KS, per_row, total, base, xq, xs, xsum);
+}
+
 template <int NB>
-__device__ void quantise_slice(const QmvArgs& a, int btile, int kb0, int w, int KS, int8_t* xq, float* xs,
-                               float* xsum) {
-  const int groups = w * 8;
-  for (int task = threadIdx.x; task < NB * groups; task += QMV_CTHREADS) {
-    const int b = task >= groups ? 1 : 0;  // NB <= 2
-    const int gi = task - b * groups;
-    const int row = btile * NB + b;
-    int8_t* qh = xq + (b * 2) * KS + gi * 32;
-    int8_t* ql = qh + KS;
-    float sc = 0.f, s0 = 0.f, s1 = 0.f;
-    if (row < a.rows) {
-      float v[32];
-      const int64_t off = (int64_t)row * a.K + (int64_t)kb0 * QK + gi * 32;
-      if (a.x_dtype == DT_F16) load32<__half>(a.x, off, v);
-      else if (a.x_dtype == DT_BF16) load32<__nv_bfloat16>(a.x, off, v);
-      else load32<float>(a.x, off, v);
-      quant32(v, qh, ql, sc, s0, s1);
-    } else {
-      const uint4 z = make_uint4(0, 0, 0, 0);
-      reinterpret_cast<uint4*>(qh)[0] = z; reinterpret_cast<uint4*>(qh)[1] = z;
-      reinterpret_cast<uint4*>(ql)[0] = z; reinterpret_cast<uint4*>(ql)[1] = z;
-    }
-    xs[b * (KS / 32) + gi] = sc;
-    xsum[b * (KS / 16) + 2 * gi] = s0;
-    xsum[b * (KS / 16) + 2 * gi + 1] = s1;
-  }
+__device__ __forceinline__ void quantise_slice(const QmvArgs& a, int btile, int kb0, int w, int KS, int8_t* xq,
+                                               float* xs, float* xsum) {
+  if (a.x_dtype == DT_F16) quantise_slice_t<NB, __half>(a, btile, kb0, w, KS, xq, xs, xsum);
+  else if (a.x_dtype == DT_BF16) quantise_slice_t<NB, __nv_bfloat16>(a, btile, kb0, w, KS, xq, xs, xsum);
+  else quantise_slice_t<NB, float>(a, btile, kb0, w, KS, xq, xs, xsum);
 }
 
 // ---------------------------------------------------------------------------
-// Work cursor over the (tile, block) units of one CTA's range in its slice:
-// the current tile, the block within the slice, and the units left.
+// Work cursor over the (tile, block) units of one CTA's range [u0, u1) in its
+// slice, in order (tile-major, `w` blocks per tile).
 struct QmvCursor {
-  int64_t tile;
-  int blk, w, left;
+  int64_t tile, t0;  // current tile, first tile of the range
+  int blk, w, left;  // block within the slice, slice width, units left
   __device__ QmvCursor(int64_t u0, int64_t u1, int width) : w(width) {
-    tile = u0 / width;
+    t0 = tile = u0 / width;
     blk = (int)(u0 - tile * width);
     left = (int)(u1 - u0);
   }
-  __device__ int chunk(int cb) const {
-    const int n = min(cb, w - blk);
-    return min(n, left);
-  }
-  __device__ void advance(int n) {
+  __device__ bool done() const { return left <= 0; }
+  __device__ int chunk(int cb) const { return min(min(cb, w - blk), left); }
+  // Advances by n blocks; returns true when this ends the CTA's part of the
+  // current tile (the tile's end, or the end of the range).
+  __device__ bool advance(int n) {
     left -= n;
     blk += n;
-    if (blk == w) { blk = 0; tile++; }
+    if (blk == w) {
+      blk = 0;
+      tile++;
+      return true;
+    }
+    return left == 0;
   }
 };
 
@@ -249,6 +260,60 @@ __device__ __forceinline__ void cta_range(const QmvArgs& a, int64_t U, int w, in
 // ---------------------------------------------------------------------------
 // The matvec kernel.
 
+// Global combination of one piece of a tile shared with other CTAs (other
+// slices and/or neighbouring CTAs of the same slice): publish the piece, take
+// a ticket, and if this was the last piece, sum all pieces of the tile in
+// slice order then CTA order and write y.  Executed by the combiner warp; v
+// is this piece's row sum (lane = b*16 + r).
+template <int NB>
+__device__ void combine_piece(const QmvArgs& a, int btile, int slice, int C, int c, int w, int64_t tile,
+                              int64_t first_tile, int seg_len, float v) {
+  const int lane = threadIdx.x & 31;
+  float* pp;
+  if (seg_len == w)
+    pp = a.part_full + (((int64_t)btile * a.slices + slice) * a.tiles + tile) * (NB * 16);
+  else
+    pp = a.part_piece + ((((int64_t)btile * a.slices + slice) * C + c) * 2 + (tile == first_tile ? 0 : 1)) * (NB * 16);
+  if (lane < NB * 16) pp[lane] = v;
+  __threadfence();
+  __syncwarp();
+  unsigned last = 0;
+  unsigned* tk = a.tickets + (int64_t)btile * a.tiles + tile;
+  if (lane == 0) {
+    const unsigned prev = atomicAdd(tk, (unsigned)seg_len);
+    last = (prev + (unsigned)seg_len == (unsigned)a.kb);
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __threadfence();
+  if (lane < NB * 16) {
+    float sum = 0.f;
+    for (int s2 = 0; s2 < a.slices; s2++) {
+      const int w2 = min(a.bps, a.kb - s2 * a.bps);
+      const int64_t U2 = a.tiles * w2;
+      const int64_t ut0 = tile * w2, ut1 = ut0 + w2;
+      const int64_t c0 = ((ut0 + 1) * C - 1) / U2;
+      const int64_t c1 = (ut1 * C - 1) / U2;
+      const int64_t base = (int64_t)btile * a.slices + s2;
+      if (c0 == c1) {  // one CTA covered the whole slice of this tile
+        sum += __ldcg(a.part_full + (base * a.tiles + tile) * (NB * 16) + lane);
+        continue;
+      }
+      for (int64_t c2 = c0; c2 <= c1; c2++) {
+        const int64_t s0 = c2 * U2 / C, s1 = (c2 + 1) * U2 / C;
+        if (s0 == s1 || s1 <= ut0 || s0 >= ut1) continue;  // empty or not covering this tile
+        const int sl = (s0 / w2 == tile) ? 0 : 1;
+        sum += __ldcg(a.part_piece + ((base * C + c2) * 2 + sl) * (NB * 16) + lane);
+      }
+    }
+    const int b = lane >> 4, r = lane & 15;
+    const int batch = btile * NB + b;
+    const int64_t rr = tile * 16 + r;
+    if (batch < a.rows && rr < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, sum);
+  }
+  if (lane == 0) *tk = 0u;
+}
+
 template <int T, int NB>
 __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   using F = Fast<T>;
@@ -258,21 +323,23 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   constexpr int KSET = UNIT * UPS;       // k per set
   constexpr int MMAS = KSET / 32;        // MMAs per set
   constexpr int SETS = QK / KSET;        // sets per block
-  constexpr int NS = G::NS;
   static_assert(MMAS >= 1, "set must cover at least one MMA");
   static_assert(F::BLOCKED || UNIT == 32, "identity mapping needs 32-wide units");
+  const int NS = a.ns, RB = a.ns + 1;
 
+  // Shared memory: tables | mbarriers | row-sum buffers | ring | activations.
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((0u - smem_u32(smem_raw)) & 127u);  // keeps shared provenance
   uint8_t* tab = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::TAB);
-  uint64_t* empty = full + NS;
-  uint64_t* segb = empty + NS;  // [NS + 1] row sums of a segment written by all consumer warps
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::TAB);  // [NS] stage landed (tx bytes)
+  uint64_t* empty = full + QMV_NS_MAX;                          // [NS] stage released by all consumers
+  uint64_t* segb = empty + QMV_NS_MAX;                          // [RB] segment row sums posted by all consumers
+  uint64_t* rfree = segb + QMV_RED_BUFS;                        // [RB] segment row sums read
   float* red = reinterpret_cast<float*>(smem + G::TAB + 256);
   uint8_t* ring = smem + G::TAB + 256 + QMV_RED_BYTES;
   const int KS = a.bps * QK;
-  int8_t* xq_s = reinterpret_cast<int8_t*>(ring + G::RING);
-  float* xs_s = reinterpret_cast<float*>(ring + G::RING + NB * 2 * KS);
+  int8_t* xq_s = reinterpret_cast<int8_t*>(ring + NS * G::STAGE);
+  float* xs_s = reinterpret_cast<float*>(ring + NS * G::STAGE + NB * 2 * KS);
   float* xsum_s = xs_s + NB * (KS / 32);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -289,13 +356,16 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], QMV_CWARPS);
     }
-    for (int s = 0; s <= NS; s++) mbar_init(&segb[s], QMV_CWARPS);
+    for (int s = 0; s < RB; s++) {
+      mbar_init(&segb[s], QMV_CWARPS);
+      mbar_init(&rfree[s], 1);
+    }
     fence_mbar_init();
   }
   __syncthreads();
   pdl_launch_dependents();
 
-  if (warp == QMV_CWARPS) {
+  if (warp == QMV_PRODUCER) {
     // ------------------------------------------------------------ producer
     const uintptr_t pbase = reinterpret_cast<uintptr_t>(a.packed);
     const uint64_t policy = l2_policy_evict_first();
@@ -303,7 +373,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     int i = 0, s = 0;
     uint32_t ph = 0;
     bool dead = false;
-    while (cur.left > 0) {
+    while (!cur.done()) {
       if (i >= NS && !dead && !mbar_wait_bounded(&empty[s], ph ^ 1u, a.err)) dead = true;
       const int nblk = cur.chunk(G::CB);
       uint32_t bytes = 0;
@@ -339,6 +409,37 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     return;
   }
 
+  if (warp == QMV_COMBINER) {
+    // ------------------------------------------------------------ combiner
+    // Walks the same segments as the consumers (one per tile touched) and
+    // takes over every piece that needs other CTAs' pieces, so that the
+    // tensor-core warps never wait on global-memory round trips.
+    pdl_wait();  // before any global write
+    QmvCursor cur(ub, ue, w);
+    const int64_t first_tile = cur.t0;
+    int rbuf = 0;
+    uint32_t rph = 0;
+    bool dead = false;
+    while (!cur.done()) {
+      const int64_t tile = cur.tile;
+      const int seg_len = cur.chunk(1 << 30);
+      cur.advance(seg_len);
+      if (seg_len != a.kb) {
+        if (!dead && !mbar_wait_bounded(&segb[rbuf], rph, a.err)) dead = true;
+        float v = 0.f;
+        if (lane < NB * 16) {
+#pragma unroll
+          for (int w2 = 0; w2 < QMV_CWARPS; w2++) v += red[(rbuf * QMV_CWARPS + w2) * 32 + lane];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rfree[rbuf]);
+        combine_piece<NB>(a, btile, slice, C, c, w, tile, first_tile, seg_len, v);
+      }
+      if (++rbuf == RB) { rbuf = 0; rph ^= 1u; }
+    }
+    return;
+  }
+
   // -------------------------------------------------------------- consumers
   F::load_tables(tab, threadIdx.x, QMV_CTHREADS);
   // Everything above reads only weights and tables; from here on the kernel
@@ -366,12 +467,11 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
 
   float acc0 = 0.f, acc1 = 0.f;
   QmvCursor cur(ub, ue, w);
-  const int64_t first_tile = cur.tile;
   int seg_len = 0;
   int s = 0, rbuf = 0, seg_no = 0;
   uint32_t ph = 0, rph = 0;
   bool dead = false;
-  while (cur.left > 0) {
+  while (!cur.done()) {
     if (!dead && !mbar_wait_bounded(&full[s], ph, a.err)) dead = true;
     const int nblk = cur.chunk(G::CB);
     const int64_t tile = cur.tile;
@@ -463,23 +563,18 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     if (++s == NS) { s = 0; ph ^= 1u; }
-    const bool tile_end = cur.blk + nblk == w;
-    cur.advance(nblk);
     seg_len += nblk;
-
-    if (tile_end || cur.left == 0) {
+    if (cur.advance(nblk)) {
       // ---- end of this CTA's segment of `tile`: reduce the quad lanes that
-      // hold the same activation row, then across warps in warp order.
+      // hold the same activation row, post the warp's row sums, move on.
       if constexpr (NB == 1) {
         acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
         acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
       }
       acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
       acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-      // Each warp posts its row sums and moves on; only the warp that
-      // finishes this segment waits for all of them.  A warp can run at most
-      // NS stages (hence NS segments) ahead of the slowest one, so NS + 1
-      // buffers are never overwritten before they are read.
+      // Buffer rbuf was last used RB segments ago; wait until it was read.
+      if (seg_no >= RB && !dead && !mbar_wait_bounded(&rfree[rbuf], rph ^ 1u, a.err)) dead = true;
       float* rb = red + (rbuf * QMV_CWARPS + warp) * 32;
       if (tq < NB) {
         rb[b_ep * 16 + g] = acc0;
@@ -487,65 +582,23 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&segb[rbuf]);
-      if (warp == (seg_no & (QMV_CWARPS - 1))) {
+      // A whole tile is finished here by one consumer warp (rotating); tiles
+      // shared with other CTAs go to the combiner warp.
+      if (seg_len == a.kb && warp == (seg_no & (QMV_CWARPS - 1))) {
         if (!dead && !mbar_wait_bounded(&segb[rbuf], rph, a.err)) dead = true;
         float v = 0.f;
         if (lane < NB * 16) {
 #pragma unroll
           for (int w2 = 0; w2 < QMV_CWARPS; w2++) v += red[(rbuf * QMV_CWARPS + w2) * 32 + lane];
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rfree[rbuf]);
         const int b = lane >> 4, r = lane & 15;
         const int batch = btile * NB + b;
         const int64_t rr = tile * 16 + r;
-        if (seg_len == a.kb) {
-          if (lane < NB * 16 && batch < a.rows && rr < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, v);
-        } else {
-          float* pp;
-          if (seg_len == w)
-            pp = a.part_full + (((int64_t)btile * a.slices + slice) * a.tiles + tile) * (NB * 16);
-          else
-            pp = a.part_piece + ((((int64_t)btile * a.slices + slice) * C + c) * 2 + (tile == first_tile ? 0 : 1)) *
-                                    (NB * 16);
-          if (lane < NB * 16) pp[lane] = v;
-          __threadfence();
-          __syncwarp();
-          unsigned last = 0;
-          unsigned* tk = a.tickets + (int64_t)btile * a.tiles + tile;
-          if (lane == 0) {
-            const unsigned prev = atomicAdd(tk, (unsigned)seg_len);
-            last = (prev + (unsigned)seg_len == (unsigned)a.kb);
-          }
-          last = __shfl_sync(0xffffffffu, last, 0);
-          if (last) {
-            __threadfence();
-            // Sum the pieces of this tile in slice order, CTA order.
-            float sum = 0.f;
-            if (lane < NB * 16) {
-              for (int s2 = 0; s2 < a.slices; s2++) {
-                const int w2 = min(a.bps, a.kb - s2 * a.bps);
-                const int64_t U2 = a.tiles * w2;
-                const int64_t ut0 = tile * w2, ut1 = ut0 + w2;
-                const int64_t c0 = ((ut0 + 1) * C - 1) / U2;
-                const int64_t c1 = (ut1 * C - 1) / U2;
-                const int64_t base = (int64_t)btile * a.slices + s2;
-                if (c0 == c1) {  // one CTA covered the whole slice of this tile
-                  sum += __ldcg(a.part_full + (base * a.tiles + tile) * (NB * 16) + lane);
-                  continue;
-                }
-                for (int64_t c2 = c0; c2 <= c1; c2++) {
-                  const int64_t s0 = c2 * U2 / C, s1 = (c2 + 1) * U2 / C;
-                  if (s0 == s1 || s1 <= ut0 || s0 >= ut1) continue;  // empty or not covering this tile
-                  const int sl = (s0 / w2 == tile) ? 0 : 1;
-                  sum += __ldcg(a.part_piece + ((base * C + c2) * 2 + sl) * (NB * 16) + lane);
-                }
-              }
-              if (batch < a.rows && rr < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, sum);
-            }
-            if (lane == 0) *tk = 0u;
-          }
-        }
+        if (lane < NB * 16 && batch < a.rows && rr < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, v);
       }
-      if (++rbuf == NS + 1) { rbuf = 0; rph ^= 1u; }
+      if (++rbuf == RB) { rbuf = 0; rph ^= 1u; }
       seg_no++;
       acc0 = acc1 = 0.f;
       seg_len = 0;
@@ -563,7 +616,7 @@ static int qmv_occupancy() {
   static int cached = 0;
   if (cached > 0) return cached;
   int occ = 0;
-  const size_t smem = QmvGeom<T>::SMEM_MAX;
+  const size_t smem = QMV_CTA_SMEM;
   if (cudaFuncSetAttribute(qmv_kernel<T, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
           cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, qmv_kernel<T, NB>, QMV_THREADS, smem) != cudaSuccess ||
@@ -592,7 +645,8 @@ static int qmv_sm_count() {
 
 #define GSQ_QMV_GEOM_CASE(TT)                                                           \
   case TT:                                                                              \
-    fixed = (size_t)QmvGeom<TT>::FIXED + QmvGeom<TT>::RING;                              \
+    fixed = QmvGeom<TT>::FIXED;                                                         \
+    stage = QmvGeom<TT>::STAGE;                                                         \
     occ = nb == 1 ? qmv_occupancy<TT, 1>() : qmv_occupancy<TT, 2>();                    \
     break;
 
@@ -604,15 +658,20 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
   p.nb = rows == 1 ? 1 : 2;
   p.btiles = (rows + p.nb - 1) / p.nb;
   p.tiles = (N + 15) / 16;
-  size_t fixed = 0;
+  size_t fixed = 0, stage = 0;
   int occ = 1;
   const int nb = p.nb;
   switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMV_GEOM_CASE) default: break; }
-  // K-slices: as few as the activation budget allows.
-  const int bps_max = QMV_XBUDGET / (QMV_XBYTES_PER_BLOCK * nb);
-  p.slices = (kb + bps_max - 1) / bps_max;
+  // Shared memory per CTA = fixed part + ring (2..4 stages) + the activations
+  // of one K-slice.  Use as few slices as fit next to a two-stage ring, then
+  // as many stages as fit next to the slice.
+  const size_t avail = QMV_CTA_SMEM - fixed;
+  auto xbytes = [&](int bps) { return align256((size_t)nb * bps * QMV_XBYTES_PER_BLOCK); };
+  p.slices = 1;
+  while (p.slices < kb && xbytes((kb + p.slices - 1) / p.slices) + 2 * stage > avail) p.slices++;
   p.bps = (kb + p.slices - 1) / p.slices;
   p.slices = (kb + p.bps - 1) / p.bps;
+  p.ns = (int)std::min<size_t>(QMV_NS_MAX, (avail - xbytes(p.bps)) / stage);
   const int w_min = kb - (p.slices - 1) * p.bps;  // the last slice is the narrowest
   // CTAs per slice: fill every resident slot once.
   const int64_t slots = std::max<int64_t>(1, (int64_t)occ * qmv_sm_count() / p.btiles);
@@ -626,7 +685,7 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
     ctas = std::min<int64_t>(ctas, p.tiles);
   }
   p.ctas = (int)ctas;
-  p.smem = fixed + align256((size_t)nb * p.bps * QMV_XBYTES_PER_BLOCK);
+  p.smem = fixed + (size_t)p.ns * stage + xbytes(p.bps);
   const bool split = !(p.slices == 1 && (p.aligned || p.tiles % p.ctas == 0));
   if (split && p.aligned) {
     p.ctas = 0;  // not plannable: slices need tickets (K beyond the activation budget with > 1M rows)
@@ -652,7 +711,7 @@ static cudaError_t qmv_launch_t(const QmvArgs& a, const QmvPlan& p, cudaStream_t
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)QmvGeom<T>::SMEM_MAX);
+                                         (int)QMV_CTA_SMEM);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = 1;
   }
@@ -692,6 +751,7 @@ cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, in
   a.bps = p.bps;
   a.slices = p.slices;
   a.aligned = p.aligned;
+  a.ns = p.ns;
   return qmv_launch(t, a, p, st);
 }
 
