@@ -179,6 +179,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Atomic add with acquire-release semantics at GPU scope: one round trip
+// that publishes the caller's earlier writes and sees the earlier writers'.
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned r;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(r) : "l"(p), "r"(v) : "memory");
+  return r;
+}
+
 // One-dimensional bulk async copy global -> shared, completing on an mbarrier.
 // dst, src and bytes must all be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

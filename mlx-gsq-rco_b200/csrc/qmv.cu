@@ -51,10 +51,10 @@ constexpr int QMV_CTA_SMEM = 112 * 1024;               // two CTAs per SM
 constexpr int QMV_XBYTES_PER_BLOCK = 2 * QK + 8 * 4 + 16 * 4;  // per activation row: levels, scales, half sums
 constexpr int QMV_RED_BUFS = QMV_NS_MAX + 1;          // per-warp row-sum buffers (ring depth + 1)
 constexpr int QMV_RED_BYTES = QMV_RED_BUFS * QMV_CWARPS * 32 * 4;
-// Scratch layout: a fixed region of ticket counters first, then the partial
-// sums.  Every completed call returns the tickets it used to zero and nothing
-// else is ever written over the ticket region, so one zero-filled workspace
-// serves calls of any shape.
+// Scratch layout: a fixed region that every completed call leaves zero-filled
+// (ticket counters, or the published-piece slots of single-slice plans), then
+// the partial sums of multi-slice plans.  Nothing else is ever written over
+// the fixed region, so one zero-filled workspace serves calls of any shape.
 constexpr int QMV_TICKET_SLOTS = 65536;
 constexpr size_t QMV_TICKET_BYTES = QMV_TICKET_SLOTS * sizeof(unsigned);
 
@@ -65,6 +65,7 @@ struct QmvArgs {
   float* part_full;    // [btiles][slices][tiles][NB*16]   whole-slice pieces of a tile
   float* part_piece;   // [btiles][slices][ctas][2][NB*16] first / last piece of a CTA's range
   unsigned* tickets;   // [btiles][tiles]
+  uint32_t* slots;     // [btiles][ctas][NB*16] published pieces, one slice (encoded, 0 = empty)
   int* err;
   int64_t N, K, row_bytes, packed_bytes, tiles;
   int rows, x_dtype, y_dtype, kb, bps, slices, aligned, ns;
@@ -219,28 +220,61 @@ __device__ __forceinline__ void quantise_slice(const QmvArgs& a, int btile, int 
 
 // ---------------------------------------------------------------------------
 // Work cursor over the (tile, block) units of one CTA's range [u0, u1) in its
-// slice, in order (tile-major, `w` blocks per tile).
+// slice (tile-major, `w` blocks per tile).  The range is whole tiles framed by
+// at most two tiles shared with neighbouring CTAs.  The cursor visits the
+// shared tiles first -- the last one (whose piece other CTAs wait for), then
+// the first one -- and the whole tiles after them, so that pieces are
+// published early and the end of the kernel only finishes whole tiles.
 struct QmvCursor {
-  int64_t tile, t0;  // current tile, first tile of the range
-  int blk, w, left;  // block within the slice, slice width, units left
+  int64_t tile, t_hi;   // current tile, end of the current phase's tiles
+  int64_t t0, t1;       // first / last tile of the range
+  int blk, bend;        // current block, end block of the current tile
+  int w, b0, e1;        // slice width, first block in t0, end block in t1
+  int phase;            // 0 last shared tile, 1 first shared tile, 2 whole tiles, 3 done
   __device__ QmvCursor(int64_t u0, int64_t u1, int width) : w(width) {
-    t0 = tile = u0 / width;
-    blk = (int)(u0 - tile * width);
-    left = (int)(u1 - u0);
+    t0 = u0 / width;
+    b0 = (int)(u0 - t0 * width);
+    t1 = (u1 - 1) / width;
+    e1 = (int)(u1 - t1 * width);
+    phase = u1 > u0 ? 0 : 3;
+    enter();
   }
-  __device__ bool done() const { return left <= 0; }
-  __device__ int chunk(int cb) const { return min(min(cb, w - blk), left); }
-  // Advances by n blocks; returns true when this ends the CTA's part of the
-  // current tile (the tile's end, or the end of the range).
-  __device__ bool advance(int n) {
-    left -= n;
-    blk += n;
-    if (blk == w) {
-      blk = 0;
-      tile++;
-      return true;
+  __device__ void set(int64_t t, int64_t hi, int b, int e) {
+    tile = t; t_hi = hi; blk = b; bend = e;
+  }
+  // Set up the current phase, skipping empty ones.
+  __device__ void enter() {
+    if (phase == 0) {
+      if (t0 == t1) { set(t0, t0 + 1, b0, e1); return; }  // the range lies in one tile
+      if (e1 < w) { set(t1, t1 + 1, 0, e1); return; }
+      phase = 1;
     }
-    return left == 0;
+    if (phase == 1) {
+      if (b0 > 0) { set(t0, t0 + 1, b0, w); return; }
+      phase = 2;
+    }
+    if (phase == 2) {
+      const int64_t lo = b0 > 0 ? t0 + 1 : t0, hi = e1 < w ? t1 : t1 + 1;
+      if (lo < hi) { set(lo, hi, 0, w); return; }
+      phase = 3;
+    }
+  }
+  __device__ bool done() const { return phase == 3; }
+  __device__ int chunk(int cb) const { return min(cb, bend - blk); }
+  // Advances by n blocks; returns true when this ends the CTA's part of the
+  // current tile.
+  __device__ bool advance(int n) {
+    blk += n;
+    if (blk < bend) return false;
+    tile++;
+    if (tile < t_hi) {
+      blk = 0;
+      bend = w;
+    } else {
+      phase = (phase == 0 && t0 == t1) ? 3 : phase + 1;
+      enter();
+    }
+    return true;
   }
 };
 
@@ -260,6 +294,60 @@ __device__ __forceinline__ void cta_range(const QmvArgs& a, int64_t U, int w, in
 // ---------------------------------------------------------------------------
 // The matvec kernel.
 
+// Single-slice plans: a tile shared by consecutive CTAs c0 < ... < ck is
+// finished by ck, the CTA holding its last block.  Every other CTA publishes
+// its piece (one per CTA: the end of its range) with plain stores, encoded so
+// that no float maps to 0 (the one 32-bit pattern that would, 0xFFBFFFFF, is
+// a NaN payload arithmetic never produces); ck reads them in CTA order,
+// resets the slots to 0 and writes y.  The pieces are visited first by their
+// CTAs, so ck rarely waits; the wait is bounded.
+__device__ __forceinline__ uint32_t piece_enc(float v) { return __float_as_uint(v) + 0x00400001u; }
+__device__ __forceinline__ float piece_dec(uint32_t e) { return __uint_as_float(e - 0x00400001u); }
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int NB>
+__device__ void publish_piece(const QmvArgs& a, int btile, int C, int c, float v) {
+  const int lane = threadIdx.x & 31;
+  if (lane < NB * 16) st_relaxed_gpu(a.slots + ((int64_t)btile * C + c) * (NB * 16) + lane, piece_enc(v));
+}
+
+template <int NB>
+__device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t U, int w, int64_t tile, float v) {
+  const int lane = threadIdx.x & 31;
+  if (lane >= NB * 16) return;
+  const int64_t c0 = ((tile * w + 1) * C - 1) / U;  // first CTA touching the tile
+  float sum = 0.f;
+  for (int64_t c2 = c0; c2 < c; c2++) {
+    uint32_t* p = a.slots + ((int64_t)btile * C + c2) * (NB * 16) + lane;
+    uint32_t e = ld_relaxed_gpu(p);
+    if (e == 0u) {
+      const long long t0 = clock64();
+      while (e == 0u) {
+        __nanosleep(64);
+        e = ld_relaxed_gpu(p);
+        if (e == 0u && clock64() - t0 > (1ll << 31)) {
+          atomicExch(a.err, DEV_WAIT_TIMEOUT);
+          break;
+        }
+      }
+    }
+    sum += piece_dec(e);
+    st_relaxed_gpu(p, 0u);
+  }
+  sum += v;
+  const int b = lane >> 4, r = lane & 15;
+  const int batch = btile * NB + b;
+  const int64_t rr = tile * 16 + r;
+  if (batch < a.rows && rr < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, sum);
+}
+
 // Global combination of one piece of a tile shared with other CTAs (other
 // slices and/or neighbouring CTAs of the same slice): publish the piece, take
 // a ticket, and if this was the last piece, sum all pieces of the tile in
@@ -275,17 +363,18 @@ __device__ void combine_piece(const QmvArgs& a, int btile, int slice, int C, int
   else
     pp = a.part_piece + ((((int64_t)btile * a.slices + slice) * C + c) * 2 + (tile == first_tile ? 0 : 1)) * (NB * 16);
   if (lane < NB * 16) pp[lane] = v;
-  __threadfence();
+  // The warp barrier orders every lane's store before lane 0's ticket, whose
+  // release makes them visible with it; its acquire (for the last piece)
+  // orders the reads of the other pieces after all of their tickets.
   __syncwarp();
   unsigned last = 0;
   unsigned* tk = a.tickets + (int64_t)btile * a.tiles + tile;
   if (lane == 0) {
-    const unsigned prev = atomicAdd(tk, (unsigned)seg_len);
+    const unsigned prev = atom_add_acq_rel_gpu(tk, (unsigned)seg_len);
     last = (prev + (unsigned)seg_len == (unsigned)a.kb);
   }
   last = __shfl_sync(0xffffffffu, last, 0);
   if (!last) return;
-  __threadfence();
   if (lane < NB * 16) {
     float sum = 0.f;
     for (int s2 = 0; s2 < a.slices; s2++) {
@@ -422,6 +511,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     bool dead = false;
     while (!cur.done()) {
       const int64_t tile = cur.tile;
+      const int sb = cur.blk;
       const int seg_len = cur.chunk(1 << 30);
       cur.advance(seg_len);
       if (seg_len != a.kb) {
@@ -433,7 +523,12 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&rfree[rbuf]);
-        combine_piece<NB>(a, btile, slice, C, c, w, tile, first_tile, seg_len, v);
+        if (a.slices > 1)
+          combine_piece<NB>(a, btile, slice, C, c, w, tile, first_tile, seg_len, v);
+        else if (sb + seg_len < w)
+          publish_piece<NB>(a, btile, C, c, v);  // later CTAs hold the rest of this tile
+        else
+          gather_pieces<NB>(a, btile, C, c, U, w, tile, v);
       }
       if (++rbuf == RB) { rbuf = 0; rph ^= 1u; }
     }
@@ -677,6 +772,8 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
   const int64_t slots = std::max<int64_t>(1, (int64_t)occ * qmv_sm_count() / p.btiles);
   int64_t ctas = std::max<int64_t>(1, slots / p.slices);
   ctas = std::min<int64_t>(ctas, p.tiles * w_min);
+  // Single-slice piece slots must fit the always-zero fixed region.
+  ctas = std::min<int64_t>(ctas, (int64_t)(QMV_TICKET_BYTES / ((size_t)p.btiles * nb * 16 * sizeof(float))));
   p.aligned = 0;
   if (p.tiles * p.btiles > QMV_TICKET_SLOTS) {
     // Too many tiles for the ticket region: CTAs own whole tiles.  With that
@@ -691,7 +788,11 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
     p.ctas = 0;  // not plannable: slices need tickets (K beyond the activation budget with > 1M rows)
     return p;
   }
-  if (split) {
+  if (split && p.slices == 1) {
+    // Published-piece slots only, inside the always-zero fixed region.
+    p.off_full = p.off_piece = 0;
+    p.workspace = align256((size_t)p.btiles * p.ctas * nb * 16 * sizeof(float));
+  } else if (split) {
     const size_t seg = (size_t)nb * 16 * sizeof(float);
     p.off_full = QMV_TICKET_BYTES;
     p.off_piece = p.off_full + align256((size_t)p.btiles * p.slices * p.tiles * seg);
@@ -736,6 +837,7 @@ cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, in
   a.x = x;
   a.y = y;
   a.tickets = p.workspace ? reinterpret_cast<unsigned*>(w) : nullptr;
+  a.slots = p.workspace ? reinterpret_cast<uint32_t*>(w) : nullptr;
   a.part_full = p.workspace ? reinterpret_cast<float*>(w + p.off_full) : nullptr;
   a.part_piece = p.workspace ? reinterpret_cast<float*>(w + p.off_piece) : nullptr;
   a.err = err;
