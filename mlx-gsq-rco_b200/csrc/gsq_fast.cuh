@@ -341,4 +341,44 @@ template <> struct Fast<T_IQ1_M> {
   }
 };
 
+// Matvec-only variants of the integer entries.  Where an entry read in place
+// (a nibble or 2-bit plane masked but not shifted) is the true entry times a
+// power of two, the matvec feeds it unshifted to the u8 x s8 tensor-core MMA
+// and folds the power of two into the scale of that 32-wide activation group
+// (xgroup_scale(g), g = group index along K).  Entries stay below 256.
+template <int T>
+struct MvDecode {
+  static constexpr bool UNSIGNED = false;
+  __device__ static float xgroup_scale(int) { return 1.f; }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    Fast<T>::entry(b, c32, tq, tab, lo, hi);
+  }
+};
+
+template <>
+struct MvDecode<T_Q4_K> {  // odd 32-groups are the high nibbles: 16 q <= 240
+  static constexpr bool UNSIGNED = true;
+  __device__ static float xgroup_scale(int g) { return (g & 1) ? 0.0625f : 1.f; }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t*, uint32_t& lo, uint32_t& hi) {
+    const uint2 w = ld64a8(b + 16 + (c32 >> 1) * 32 + 8 * tq);
+    const uint32_t m = (c32 & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+    lo = w.x & m;
+    hi = w.y & m;
+  }
+};
+
+template <>
+struct MvDecode<T_Q2_K> {  // 32-group g reads bit plane g & 3: 4^p q <= 192
+  static constexpr bool UNSIGNED = true;
+  __device__ static float xgroup_scale(int g) {
+    return (g & 3) == 0 ? 1.f : (g & 3) == 1 ? 0.25f : (g & 3) == 2 ? 0.0625f : 0.015625f;
+  }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t*, uint32_t& lo, uint32_t& hi) {
+    const uint2 w = ld64a4(b + 16 + (c32 >> 2) * 32 + 8 * tq);
+    const uint32_t m = 0x03030303u << (2 * (c32 & 3));
+    lo = w.x & m;
+    hi = w.y & m;
+  }
+};
+
 }  // namespace gsq

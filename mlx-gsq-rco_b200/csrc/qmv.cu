@@ -127,18 +127,6 @@ template <> __device__ __forceinline__ void unpack8<__nv_bfloat16>(const uint4 (
   }
 }
 
-// Round to nearest even and saturate to int8 in one conversion; the byte is
-// in the low 8 bits of the result.
-__device__ __forceinline__ uint32_t cvt_s8(float v) {
-  uint32_t r;
-  asm("cvt.rni.sat.s8.f32 %0, %1;" : "=r"(r) : "f"(v));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
-  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
-}
-
 // Slice layout in shared memory (KS = bps*256 activations per row):
 //   xq   [NB][2][KS] int8   levels hi, lo:  x ~= s * (hi + lo/256)
 //   xs   [NB][KS/32] fp32   s/256 per 32-group (s = max|x|/127)
@@ -147,7 +135,7 @@ __device__ __forceinline__ uint32_t pack4(uint32_t b0, uint32_t b1, uint32_t b2,
 // first (one round trip per CH * 256 chunks, a K = 20480 row at fp16), then
 // quantises them; the four lanes holding a 32-group combine max and sums with
 // shuffles.
-template <int NB, typename XT, int CH>
+template <int T, int NB, bool SUMS, typename XT, int CH>
 __device__ __forceinline__ void quantise_round(const QmvArgs& a, int btile, int kb0, int KS, int per_row, int total,
                                                int base, int8_t* xq, float* xs, float* xsum) {
   uint4 raw[CH][2];
@@ -171,51 +159,59 @@ __device__ __forceinline__ void quantise_round(const QmvArgs& a, int btile, int 
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       am = fmaxf(am, fabsf(v[j]));
-      sum += v[j];
+      if constexpr (SUMS) sum += v[j];
     }
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
     am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-    const float half = sum + __shfl_xor_sync(0xffffffffu, sum, 1);
-    const float inv = am > 0.f ? 127.f / am : 0.f;
-    // |u| <= 127 (up to rounding), so hi never saturates below -127; the
-    // residual level lo = 256 (u - hi) saturates to [-128, 127].
-    uint32_t h[8], l[8];
+    float half = 0.f;
+    if constexpr (SUMS) half = sum + __shfl_xor_sync(0xffffffffu, sum, 1);
+    // With u = x * 127 / max|x| in [-127, 127], t = rint(256 u) + 128 is
+    // 256 hi + (lo + 128) with lo in [-128, 127]: byte 1 of t is the level
+    // hi, byte 0 is lo + 128, and hi + lo/256 = rint(256 u)/256.  The scale
+    // and its reciprocal need only agree to a few ulps: the levels are
+    // reconstructed with xs, never with inv.
+    const float inv = am > 0.f ? __fdividef(127.f * 256.f, am) : 0.f;
+    uint32_t t[8];
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const float u = v[j] * inv;
-      const float hr = rintf(u);
-      h[j] = cvt_s8(hr);
-      l[j] = cvt_s8((u - hr) * 256.f);
+    for (int j = 0; j < 8; j++) t[j] = (uint32_t)__float2int_rn(fmaf(v[j], inv, 128.f));
+    uint32_t hw[2], lw[2];
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const uint32_t z01 = __byte_perm(t[4 * q], t[4 * q + 1], 0x5140);      // b0(t0) b0(t1) b1(t0) b1(t1)
+      const uint32_t z23 = __byte_perm(t[4 * q + 2], t[4 * q + 3], 0x5140);
+      lw[q] = __byte_perm(z01, z23, 0x5410) ^ 0x80808080u;
+      hw[q] = __byte_perm(z01, z23, 0x7632);
     }
     if (c < total) {
       const int b = c >= per_row ? 1 : 0;
       const int cc = c - b * per_row;
       int8_t* qh = xq + (b * 2) * KS + cc * 8;
-      *reinterpret_cast<uint2*>(qh) = make_uint2(pack4(h[0], h[1], h[2], h[3]), pack4(h[4], h[5], h[6], h[7]));
-      *reinterpret_cast<uint2*>(qh + KS) = make_uint2(pack4(l[0], l[1], l[2], l[3]), pack4(l[4], l[5], l[6], l[7]));
-      if ((cc & 3) == 0) xs[b * (KS / 32) + (cc >> 2)] = am / (127.f * 256.f);
-      if ((cc & 1) == 0) xsum[b * (KS / 16) + (cc >> 1)] = half;
+      *reinterpret_cast<uint2*>(qh) = make_uint2(hw[0], hw[1]);
+      *reinterpret_cast<uint2*>(qh + KS) = make_uint2(lw[0], lw[1]);
+      if ((cc & 3) == 0) xs[b * (KS / 32) + (cc >> 2)] = am * (1.f / (127.f * 256.f)) * MvDecode<T>::xgroup_scale(cc >> 2);
+      if constexpr (SUMS) {
+        if ((cc & 1) == 0) xsum[b * (KS / 16) + (cc >> 1)] = half;
+      }
     }
   }
 }
 
-
-template <int NB, typename XT>
+template <int T, int NB, bool SUMS, typename XT>
 __device__ void quantise_slice_t(const QmvArgs& a, int btile, int kb0, int w, int KS, int8_t* xq, float* xs,
                                  float* xsum) {
   constexpr int CH = sizeof(XT) == 4 ? 5 : 10;
   const int per_row = w * 32;  // 8-value chunks per activation row
   const int total = NB * per_row;
   for (int base = 0; base < total; base += CH * QMV_CTHREADS)
-    quantise_round<NB, XT, CH>(a, btile, kb0, KS, per_row, total, base, xq, xs, xsum);
+    quantise_round<T, NB, SUMS, XT, CH>(a, btile, kb0, KS, per_row, total, base, xq, xs, xsum);
 }
 
-template <int NB>
+template <int T, int NB, bool SUMS>
 __device__ __forceinline__ void quantise_slice(const QmvArgs& a, int btile, int kb0, int w, int KS, int8_t* xq,
                                                float* xs, float* xsum) {
-  if (a.x_dtype == DT_F16) quantise_slice_t<NB, __half>(a, btile, kb0, w, KS, xq, xs, xsum);
-  else if (a.x_dtype == DT_BF16) quantise_slice_t<NB, __nv_bfloat16>(a, btile, kb0, w, KS, xq, xs, xsum);
-  else quantise_slice_t<NB, float>(a, btile, kb0, w, KS, xq, xs, xsum);
+  if (a.x_dtype == DT_F16) quantise_slice_t<T, NB, SUMS, __half>(a, btile, kb0, w, KS, xq, xs, xsum);
+  else if (a.x_dtype == DT_BF16) quantise_slice_t<T, NB, SUMS, __nv_bfloat16>(a, btile, kb0, w, KS, xq, xs, xsum);
+  else quantise_slice_t<T, NB, SUMS, float>(a, btile, kb0, w, KS, xq, xs, xsum);
 }
 
 // ---------------------------------------------------------------------------
@@ -406,6 +402,7 @@ __device__ void combine_piece(const QmvArgs& a, int btile, int slice, int C, int
 template <int T, int NB>
 __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   using F = Fast<T>;
+  using MV = MvDecode<T>;
   using G = QmvGeom<T>;
   constexpr int UNIT = F::UNIT;
   constexpr int UPS = 4 / NB;            // units per set
@@ -540,7 +537,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   // Everything above reads only weights and tables; from here on the kernel
   // reads activations / scratch that an earlier kernel in the stream writes.
   pdl_wait();
-  quantise_slice<NB>(a, btile, kb0, w, KS, xq_s, xs_s, xsum_s);
+  quantise_slice<T, NB, F::HAS_BIAS>(a, btile, kb0, w, KS, xq_s, xs_s, xsum_s);
   named_sync_consumers();
 
   const int g = lane >> 2, tq = lane & 3;
@@ -625,10 +622,15 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
             }
           } else {
             uint32_t a0, a1, a2, a3;
-            F::entry(b0, c32, tq, tab, a0, a2);
-            F::entry(b1, c32, tq, tab, a1, a3);
-            if (j & 1) mma_s8(Cb, a0, a1, a2, a3, bx0, bx1);
-            else mma_s8(Cc, a0, a1, a2, a3, bx0, bx1);
+            MV::entry(b0, c32, tq, tab, a0, a2);
+            MV::entry(b1, c32, tq, tab, a1, a3);
+            if constexpr (MV::UNSIGNED) {
+              if (j & 1) mma_u8s8(Cb, a0, a1, a2, a3, bx0, bx1);
+              else mma_u8s8(Cc, a0, a1, a2, a3, bx0, bx1);
+            } else {
+              if (j & 1) mma_s8(Cb, a0, a1, a2, a3, bx0, bx1);
+              else mma_s8(Cc, a0, a1, a2, a3, bx0, bx1);
+            }
           }
         }
         if constexpr (MMAS > 1) {
