@@ -7,13 +7,16 @@ larger than the 126 MB L2, so no step reuses another's weights from L2).
 
   value       whole-job QMV throughput in packed-weight GB/s: packed bytes of
               the sweep x steps / device time of the timed region (CUDA graph
-              replays of the step, CUDA events, max over ranks).
+              replays of the step, CUDA events, max over ranks).  One step is
+              33 launches of the QMV kernel, nothing else.
   e2e         the same metric through the public Python API with host
               buffers: every step copies each projection's activation from
               pinned host memory and reads the result back.
-  roofline    the QMV kernel: algorithmic bytes (packed + 2K + 4N per call)
-              / CUDA-event duration per launch (cold L2: a 256 MB write
-              between launches), summed over the sweep, vs measured HBM peak.
+  roofline    the QMV kernel inside the timed region: algorithmic bytes of a
+              step (packed + 2K + 4N per call) / the step's CUDA-event time,
+              vs the measured HBM copy bandwidth.
+  qmv_sweep   per configuration: a CUDA graph of 24 launches over a ring of
+              distinct weight copies (working set > 2x L2), CUDA events.
   qmm_prefill config 3 at M=512 (tcgen05 QMM) in TFLOP/s vs measured bf16 peak.
   cpu_baseline the reference's CPU path (gguf-py dequantize, which
               mlx_gsq/quant/reference.py:10-18 calls, + numpy matvec) on a
@@ -75,10 +78,14 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "25",
                  "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0:  # sampling has started before timing does
+                time.sleep(0.01)
+            self.lines.clear()
         except OSError:
             self.proc = None
         return self
@@ -161,7 +168,7 @@ def run_reference(args, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=15.0)
@@ -249,28 +256,9 @@ def main():
     ms_per_step = ms / args.steps
     value = step_bytes * args.steps / (ms / 1e3) / 1e9
 
-    # ---- per-kernel roofline: cold-L2 CUDA-event duration of every launch ----
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    per = []
-    reps = 5
-    for c in cfgs:
-        ts = []
-        for _ in range(reps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            quantized_matvec(c["x"], c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
-                             out_dtype=torch.float32)
-            e1.record()
-            torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1))
-        t_ms = float(np.median(ts))
-        per.append({"type": c["q"], "N": c["n"], "K": c["k"], "us": round(t_ms * 1e3, 2),
-                    "GBs": round(c["alg"] / (t_ms / 1e3) / 1e9, 1),
-                    "frac": round(c["alg"] / (t_ms / 1e3) / 1e9 / pk["hbm"], 3)})
-    alg_total = sum(c["alg"] for c in cfgs)
-    t_total = sum(p["us"] for p in per) * 1e-6
-    achieved = alg_total / t_total / 1e9
+    # ---- roofline of the QMV kernel over the timed region ----
+    alg_step = sum(c["alg"] for c in cfgs)
+    achieved = alg_step / (ms_per_step / 1e3) / 1e9
     traffic = None
     tpath = os.path.join(REPO, "profiles", "qmv_traffic.json")
     if os.path.exists(tpath):
@@ -279,10 +267,48 @@ def main():
         except (OSError, ValueError):
             traffic = None
     roofline = {"bound": "hbm", "kernel": "gsq::qmv_kernel", "achieved": round(achieved, 1), "peak": pk["hbm"],
-                "unit": "GB/s", "frac": round(achieved / pk["hbm"], 4), "peak_source": pk["src"] + " (burst)",
+                "unit": "GB/s", "frac": round(achieved / pk["hbm"], 4), "peak_source": pk["src"] + " (copy bandwidth)",
                 "traffic": traffic,
-                "achieved_definition": "sum over the 33 sweep launches of (packed + 2K + 4N) bytes / sum of "
-                                       "cold-L2 CUDA-event launch durations"}
+                "achieved_definition": "algorithmic bytes of one step (33 launches: packed + 2K + 4N each) / "
+                                       "CUDA-event time of one step in the timed region"}
+
+    # ---- per configuration: graph of 24 launches over a ring of copies ----
+    per = []
+    if world == 1:
+        l2 = 126 << 20
+        for c in cfgs:
+            nbytes = c["packed"].numel()
+            ncopy = max(8, min(24, -(-2 * l2 // nbytes)))
+            ring = [c["packed"]] + [c["packed"].clone() for _ in range(ncopy - 1)]
+            reps = 24
+            for i in range(2):
+                quantized_matvec(c["x"], ring[i % ncopy], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
+                                 out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            st = torch.cuda.Stream(device=dev)
+            st.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(st):
+                with torch.cuda.graph(g, stream=st):
+                    for i in range(reps):
+                        quantized_matvec(c["x"], ring[i % ncopy], qtype=c["q"], out_features=c["rows"],
+                                         in_features=c["k"], out_dtype=torch.float32)
+            torch.cuda.current_stream(dev).wait_stream(st)
+            for _ in range(2):
+                g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            t_us = e0.elapsed_time(e1) * 1e3 / (5 * reps)
+            per.append({"type": c["q"], "N": c["n"], "K": c["k"], "us": round(t_us, 2),
+                        "GBs": round(c["alg"] / (t_us / 1e6) / 1e9, 1),
+                        "frac": round(c["alg"] / (t_us / 1e6) / 1e9 / pk["hbm"], 3)})
+            del g, ring
+            torch.cuda.empty_cache()
 
     # ---- e2e through the public API with host buffers ----
     host_x = [c["x"].cpu().pin_memory() for c in cfgs]
@@ -335,16 +361,25 @@ def main():
                 x = torch.randn(512, k, device=dev, dtype=torch.bfloat16)
                 for _ in range(2):
                     quantized_matmul(x, w, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
-                ts = []
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                st = torch.cuda.Stream(device=dev)
+                st.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(st):
+                    with torch.cuda.graph(g, stream=st):
+                        for _ in range(8):
+                            quantized_matmul(x, w, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
+                torch.cuda.current_stream(dev).wait_stream(st)
+                g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
                 for _ in range(3):
-                    flush.zero_()
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record()
-                    quantized_matmul(x, w, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
-                    e1.record()
-                    torch.cuda.synchronize()
-                    ts.append(e0.elapsed_time(e1))
-                t_ms = float(np.median(ts))
+                    g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                t_ms = e0.elapsed_time(e1) / 24
+                del g
                 fl = 2.0 * 512 * n * k
                 flops_total += fl
                 t_qmm += t_ms / 1e3
@@ -354,7 +389,8 @@ def main():
         tf = flops_total / t_qmm / 1e12
         qmm = {"M": 512, "tflops": round(tf, 1), "peak": pk["bf16"], "frac": round(tf / pk["bf16"], 4),
                "prefill_tok_s_per_projection_set": None, "per_shape": qres,
-               "note": "includes the bf16->fp16 activation pre-pass; weights decoded once per 128x128 tile"}
+               "note": "includes the bf16->fp16 activation pre-pass; weights decoded once per 128x128 tile; "
+                       "CUDA graph of 8 launches, CUDA events"}
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
@@ -367,7 +403,9 @@ def main():
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s (packed weight bytes, QMV batch 1)",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-            "dtype": "int8 tensor-core dot of decoded packed weights (fp16 x, fp32 accumulate/out)",
+            "dtype": "int8",
+            "dtype_note": "decoded packed entries (s8/u8) x two int8 activation levels on the tensor cores, "
+                          "s32 accumulate, fp32 scales and output; fp16 activations in",
             "data": "synthetic",
             "config": {"workload": "config-2 QMV sweep: 11 types x {5120->5120, 5120->17408, 17408->5120}, batch 1",
                        "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (886 MB per step)",
