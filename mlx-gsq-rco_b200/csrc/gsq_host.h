@@ -39,6 +39,7 @@ struct QmvPlan {
   int ctas;          // persistent CTAs per K-slice (grid.x)
   int aligned;       // 1: CTAs own whole tiles (no partial sums, no tickets)
   int ns;            // ring stages (2..4)
+  int cb, rowb, stage;  // ring geometry: blocks per stage, staged row stride, stage bytes
   size_t smem;       // dynamic shared memory bytes
   size_t off_full, off_piece;  // scratch layout (bytes)
   size_t workspace;  // scratch bytes (tickets + partial sums), 0 when no tile is split

@@ -69,23 +69,25 @@ struct QmvArgs {
   int* err;
   int64_t N, K, row_bytes, packed_bytes, tiles;
   int rows, x_dtype, y_dtype, kb, bps, slices, aligned, ns;
+  int cb, rowb, stage;  // ring geometry: blocks per stage, staged row stride, stage bytes
 };
+
+// Staged row stride for cb blocks: the copied bytes plus head/tail 16-byte
+// rounding, padded to an odd number of 16-byte units so that the 8 rows a
+// warp reads at once (rows g = 0..7) start in 8 different 16-byte bank groups.
+__host__ __device__ constexpr int qmv_rowb(int cb, int bb) {
+  return (((cb * bb + 30) + 15) / 16) % 2 ? ((cb * bb + 30) + 15) / 16 * 16 : ((cb * bb + 30) + 15) / 16 * 16 + 16;
+}
 
 template <int T>
 struct QmvGeom {
   static constexpr int BB = block_bytes(T);
-  static constexpr int CB = BB <= 84 ? 16 : 8;                       // blocks per stage (~0.8-1.7 KB a row)
-  // Staged row stride: the copied bytes plus head/tail 16-byte rounding,
-  // padded to an odd number of 16-byte units so that the 8 rows a warp reads
-  // at once (rows g = 0..7) start in 8 different 16-byte bank groups.
-  static constexpr int ROWB0 = ((CB * BB + 30) + 15) / 16 * 16;
-  static constexpr int ROWB = (ROWB0 / 16) % 2 ? ROWB0 : ROWB0 + 16;
-  static constexpr int STAGE = 16 * ROWB;
   static constexpr int TAB = (Fast<T>::TAB_BYTES + 127) / 128 * 128;
   static constexpr int FIXED = 128 /*align*/ + TAB + 256 /*mbarriers*/ + QMV_RED_BYTES;
-  // Two stages plus the activations of one block must fit; the ring depth
-  // (2..4 stages) and the K-slice width are chosen per call.
-  static_assert(FIXED + 2 * STAGE + 2 * QMV_XBYTES_PER_BLOCK <= QMV_CTA_SMEM, "ring must hold two stages");
+  // Stages of 8 blocks: two of them plus the activations of one block always
+  // fit; the plan may choose wider stages (16 or 32 blocks) per call.
+  static_assert(FIXED + 2 * 16 * qmv_rowb(8, BB) + 2 * QMV_XBYTES_PER_BLOCK <= QMV_CTA_SMEM,
+                "ring must hold two stages");
 };
 
 __device__ __forceinline__ void named_sync_consumers() {
@@ -423,9 +425,10 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   uint64_t* rfree = segb + QMV_RED_BUFS;                        // [RB] segment row sums read
   float* red = reinterpret_cast<float*>(smem + G::TAB + 256);
   uint8_t* ring = smem + G::TAB + 256 + QMV_RED_BYTES;
+  const int CB = a.cb, ROWB = a.rowb, STAGE = a.stage;
   const int KS = a.bps * QK;
-  int8_t* xq_s = reinterpret_cast<int8_t*>(ring + NS * G::STAGE);
-  float* xs_s = reinterpret_cast<float*>(ring + NS * G::STAGE + NB * 2 * KS);
+  int8_t* xq_s = reinterpret_cast<int8_t*>(ring + NS * STAGE);
+  float* xs_s = reinterpret_cast<float*>(ring + NS * STAGE + NB * 2 * KS);
   float* xsum_s = xs_s + NB * (KS / 32);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -461,7 +464,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     bool dead = false;
     while (!cur.done()) {
       if (i >= NS && !dead && !mbar_wait_bounded(&empty[s], ph ^ 1u, a.err)) dead = true;
-      const int nblk = cur.chunk(G::CB);
+      const int nblk = cur.chunk(CB);
       uint32_t bytes = 0;
       if (lane < 16 && !dead) {
         const int64_t r = cur.tile * 16 + lane;
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
           const int64_t off_al = off & ~int64_t(15);
           int64_t end_al = (end + 15) & ~int64_t(15);
           if (end_al > a.packed_bytes) end_al = end & ~int64_t(15);
-          uint8_t* dst = ring + s * G::STAGE + lane * G::ROWB;
+          uint8_t* dst = ring + s * STAGE + lane * ROWB;
           if (end_al > off_al) {
             bytes = (uint32_t)(end_al - off_al);
             fence_proxy_async_smem();
@@ -554,8 +557,8 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   // rows), so the staged position of a block needs only 32-bit arithmetic.
   const uint32_t rb16 = (uint32_t)a.row_bytes & 15u;
   const uint32_t h0 = (rb16 * (uint32_t)g) & 15u, h1 = (rb16 * (uint32_t)(g + 8)) & 15u;
-  const uint8_t* lane_st0 = ring + g * G::ROWB;
-  const uint8_t* lane_st1 = ring + (g + 8) * G::ROWB;
+  const uint8_t* lane_st0 = ring + g * ROWB;
+  const uint8_t* lane_st1 = ring + (g + 8) * ROWB;
 
   float acc0 = 0.f, acc1 = 0.f;
   QmvCursor cur(ub, ue, w);
@@ -565,11 +568,11 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   bool dead = false;
   while (!cur.done()) {
     if (!dead && !mbar_wait_bounded(&full[s], ph, a.err)) dead = true;
-    const int nblk = cur.chunk(G::CB);
+    const int nblk = cur.chunk(CB);
     const int64_t tile = cur.tile;
     const uint32_t kb16 = ((uint32_t)(kb0 + cur.blk) * (uint32_t)G::BB) & 15u;
-    const uint8_t* r0p = lane_st0 + s * G::STAGE + ((h0 + kb16) & 15u);
-    const uint8_t* r1p = lane_st1 + s * G::STAGE + ((h1 + kb16) & 15u);
+    const uint8_t* r0p = lane_st0 + s * STAGE + ((h0 + kb16) & 15u);
+    const uint8_t* r1p = lane_st1 + s * STAGE + ((h1 + kb16) & 15u);
     for (int bi = warp; bi < nblk; bi += QMV_CWARPS) {
       const uint8_t* b0 = r0p + bi * G::BB;
       const uint8_t* b1 = r1p + bi * G::BB;
@@ -743,7 +746,7 @@ static int qmv_sm_count() {
 #define GSQ_QMV_GEOM_CASE(TT)                                                           \
   case TT:                                                                              \
     fixed = QmvGeom<TT>::FIXED;                                                         \
-    stage = QmvGeom<TT>::STAGE;                                                         \
+    bb = QmvGeom<TT>::BB;                                                               \
     occ = nb == 1 ? qmv_occupancy<TT, 1>() : qmv_occupancy<TT, 2>();                    \
     break;
 
@@ -755,20 +758,33 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
   p.nb = rows == 1 ? 1 : 2;
   p.btiles = (rows + p.nb - 1) / p.nb;
   p.tiles = (N + 15) / 16;
-  size_t fixed = 0, stage = 0;
-  int occ = 1;
+  size_t fixed = 0;
+  int occ = 1, bb = 0;
   const int nb = p.nb;
   switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMV_GEOM_CASE) default: break; }
   // Shared memory per CTA = fixed part + ring (2..4 stages) + the activations
-  // of one K-slice.  Use as few slices as fit next to a two-stage ring, then
-  // as many stages as fit next to the slice.
+  // of one K-slice.  Wider stages (more blocks per consumer warp between
+  // ring synchronisations) are taken when the activations of a whole row
+  // still fit next to two of them; otherwise stages of 8 blocks, and as few
+  // K-slices as fit.
   const size_t avail = QMV_CTA_SMEM - fixed;
   auto xbytes = [&](int bps) { return align256((size_t)nb * bps * QMV_XBYTES_PER_BLOCK); };
+  const int cb_max = bb <= 84 ? 32 : 16;
+  p.cb = 8;
+  for (int cb = cb_max; cb > 8; cb /= 2) {
+    if (cb > 2 * kb) continue;  // wider than two tile rows: no gain
+    if (xbytes(kb) + 2 * (size_t)(16 * qmv_rowb(cb, bb)) <= avail) { p.cb = cb; break; }
+  }
+  const size_t stage = 16 * (size_t)qmv_rowb(p.cb, bb);
   p.slices = 1;
   while (p.slices < kb && xbytes((kb + p.slices - 1) / p.slices) + 2 * stage > avail) p.slices++;
   p.bps = (kb + p.slices - 1) / p.slices;
   p.slices = (kb + p.bps - 1) / p.bps;
   p.ns = (int)std::min<size_t>(QMV_NS_MAX, (avail - xbytes(p.bps)) / stage);
+  if (p.ns < 2) {  // cannot happen for 8-block stages (static_assert); refuse rather than run a 1-stage ring
+    p.ctas = 0;
+    return p;
+  }
   const int w_min = kb - (p.slices - 1) * p.bps;  // the last slice is the narrowest
   // CTAs per slice: fill every resident slot once.
   const int64_t slots = std::max<int64_t>(1, (int64_t)occ * qmv_sm_count() / p.btiles);
@@ -785,6 +801,8 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
   }
   p.ctas = (int)ctas;
   p.smem = fixed + (size_t)p.ns * stage + xbytes(p.bps);
+  p.rowb = qmv_rowb(p.cb, bb);
+  p.stage = (int)stage;
   const bool split = !(p.slices == 1 && (p.aligned || p.tiles % p.ctas == 0));
   if (split && p.aligned) {
     p.ctas = 0;  // not plannable: slices need tickets (K beyond the activation budget with > 1M rows)
@@ -856,6 +874,9 @@ cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, in
   a.slices = p.slices;
   a.aligned = p.aligned;
   a.ns = p.ns;
+  a.cb = p.cb;
+  a.rowb = p.rowb;
+  a.stage = p.stage;
   return qmv_launch(t, a, p, st);
 }
 
