@@ -123,9 +123,8 @@ int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_
 }
 
 size_t gsq_qmm_workspace_size(int qtype, int64_t N, int64_t K, int64_t M, int x_dtype) {
-  (void)qtype; (void)N;
-  if (M <= 0 || K <= 0) return 0;
-  return qmm_x16_bytes(x_dtype, M, K);
+  if (!supported(qtype) || M <= 0 || N <= 0 || K <= 0 || K % QK) return 0;
+  return qmm_workspace_bytes(qtype, N, K, M, x_dtype);
 }
 
 int gsq_qmm(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
@@ -137,12 +136,13 @@ int gsq_qmm(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_
   if (!x || !y) return fail(GSQ_ERR_ARG, "null x or y");
   if (!dtype_ok(x_dtype)) return fail(GSQ_ERR_ARG, "unsupported x dtype");
   if (!aligned(x, 16) || !aligned(y, 4)) return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned");
-  const size_t need = qmm_x16_bytes(x_dtype, M, K);
-  if (need > 0 && (!workspace || workspace_bytes < need || !aligned(workspace, 16)))
-    return fail(GSQ_ERR_WORKSPACE, "gsq_qmm needs %zu workspace bytes, got %zu", need, workspace_bytes);
+  const size_t need = qmm_workspace_bytes(qtype, N, K, M, x_dtype);
+  if (need > 0 && (!workspace || workspace_bytes < need || !aligned(workspace, 256)))
+    return fail(GSQ_ERR_WORKSPACE, "gsq_qmm needs %zu workspace bytes (256-byte aligned), got %zu", need,
+                workspace_bytes);
   const char* why = "launch";
-  cudaError_t e = qmm_launch(qtype, x, x_dtype, packed, N, K, M, y, static_cast<__half*>(workspace),
-                             device_error_word(), (cudaStream_t)stream, &why);
+  cudaError_t e = qmm_launch(qtype, x, x_dtype, packed, N, K, M, y, workspace, device_error_word(),
+                             (cudaStream_t)stream, &why);
   return e == cudaSuccess ? GSQ_OK : cuda_fail(e, why);
 }
 

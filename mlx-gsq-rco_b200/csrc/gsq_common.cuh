@@ -187,6 +187,16 @@ __device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v
   return r;
 }
 
+// Per-thread 16-byte async copy global -> shared (L2 evict-first), tracked by
+// commit groups; dst and src must be 16-byte aligned.
+__device__ __forceinline__ void cp_async16_stream(void* dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "l"(policy) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // One-dimensional bulk async copy global -> shared, completing on an mbarrier.
 // dst, src and bytes must all be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -40,6 +40,7 @@ struct QmvPlan {
   int aligned;       // 1: CTAs own whole tiles (no partial sums, no tickets)
   int ns;            // ring stages (2..4)
   int cb, rowb, stage;  // ring geometry: blocks per stage, staged row stride, stage bytes
+  int pre;           // stages issued before the activations are quantised
   size_t smem;       // dynamic shared memory bytes
   size_t off_full, off_piece;  // scratch layout (bytes)
   size_t workspace;  // scratch bytes (tickets + partial sums), 0 when no tile is split
@@ -55,9 +56,21 @@ cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, in
 cudaError_t dequant_launch(int t, const uint8_t* packed, int64_t nblocks, float* out, cudaStream_t st);
 cudaError_t embed_launch(int t, const int32_t* ids, int64_t n, const uint8_t* packed, int64_t vocab, int64_t dim,
                          void* out, int dtype, int* err, cudaStream_t st);
+// Launch plan of one QMM call: token tile T = bn x nacc, grid = row tiles x
+// token groups x K splits, and the scratch layout.
+struct QmmPlan {
+  int bn, nacc;              // MMA N per accumulator (<= 256), accumulators per CTA (1 or 2)
+  int ksplit, kbs;           // K splits, 256-blocks per split
+  int64_t row_tiles, token_groups;
+  size_t off_part, off_x16;  // scratch layout: tickets at 0, partial tiles, fp16 activations
+  size_t workspace;          // scratch bytes
+};
+
+QmmPlan qmm_plan(int t, int64_t N, int64_t K, int64_t M, int x_dtype);
+size_t qmm_workspace_bytes(int t, int64_t N, int64_t K, int64_t M, int x_dtype);
+// ws: the plan's scratch, zero-filled once by the caller.
 cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-                       float* y, __half* x16, int* err, cudaStream_t st, const char** why);
-size_t qmm_x16_bytes(int x_dtype, int64_t M, int64_t K);
+                       float* y, void* ws, int* err, cudaStream_t st, const char** why);
 
 // Records `msg` as this thread's gsq_last_error() text and returns `code`.
 int set_last_error(int code, const char* msg);

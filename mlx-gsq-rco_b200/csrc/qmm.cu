@@ -4,8 +4,13 @@
 // template _source :252-325, decode bodies :38-143, entry quantized_matmul
 // :559-594): Y[m, n] = sum_k X[m, k] * deq(W)[n, k], fp32 accumulation.
 //
-// Output tile = 128 weight rows (MMA M) x BN tokens (MMA N), K stepped 64 at
-// a time.  Warp roles in a 352-thread CTA:
+// Output tile = 128 weight rows (MMA M) x T tokens, K stepped 64 at a time;
+// T = nacc x BN with one or two fp32 accumulators of BN <= 256 columns in
+// TMEM (two when M > 256: every decoded weight tile then feeds 512 tokens).
+// When there are too few row tiles to fill the GPU, K is split over several
+// CTAs; each writes its partial tile to scratch and the last one to finish
+// (acquire-release ticket) sums them in split order and writes Y, so the
+// result stays deterministic.  Warp roles in a 352-thread CTA:
 //   warp 0      TMA tensor-map loads of the fp16 activation tile (128B swizzle);
 //   warp 1      allocates TMEM and issues tcgen05.mma (kind::f16, fp32 accum
 //               in TMEM) from one elected lane, committing to mbarriers;
@@ -32,6 +37,11 @@ constexpr int QMM_BK = 64;
 constexpr int QMM_DEC_WARPS = 8;                 // two per TMEM sub-partition
 constexpr int QMM_DEC0 = 3;                       // first decoder warp
 constexpr int QMM_THREADS = 32 * (QMM_DEC0 + QMM_DEC_WARPS);
+// Scratch: a fixed region of ticket counters (left zero-filled by every
+// call), then the partial tiles of split-K plans, then the fp16 activations.
+constexpr int QMM_TICKETS = 16384;
+constexpr int QMM_KSPLIT_MAX = 4;
+constexpr size_t QMM_TICKET_BYTES = QMM_TICKETS * sizeof(unsigned);
 
 template <int T>
 struct QmmGeom {
@@ -43,32 +53,43 @@ struct QmmGeom {
 
 constexpr size_t QMM_SMEM_LIMIT = 227 * 1024;
 
-// Pipeline shape for a token tile of bn: PST packed stages (3, or 2 when
-// space is short) and as many A/B stages (<= 4) as fit.
+// Pipeline shape for an activation stage of `bstage` bytes (T tokens x 64 k
+// fp16): PST packed stages (3, or 2 when space is short) and as many A/B
+// stages (<= 4) as fit.
 template <int T>
 struct QmmPipe {
   static constexpr size_t fixed(int pst) { return 1024 + (size_t)pst * QmmGeom<T>::PSTAGE + QmmGeom<T>::TAB + 256; }
-  static constexpr int stages_for(int bn, int pst) {
-    const size_t per = (size_t)QMM_BM * 128 + (size_t)bn * 128;
+  static constexpr int stages_for(size_t bstage, int pst) {
+    const size_t per = (size_t)QMM_BM * 128 + bstage;
     const size_t n = fixed(pst) < QMM_SMEM_LIMIT ? (QMM_SMEM_LIMIT - fixed(pst)) / per : 0;
     return n >= 4 ? 4 : (int)n;
   }
-  static constexpr int pst(int bn) { return stages_for(bn, 3) >= 3 ? 3 : 2; }
-  static constexpr int ns(int bn) { return stages_for(bn, pst(bn)); }
-  static constexpr size_t smem(int bn) {
-    return fixed(pst(bn)) + (size_t)ns(bn) * ((size_t)QMM_BM * 128 + (size_t)bn * 128);
+  static constexpr int pst(size_t bstage) { return stages_for(bstage, 3) >= 3 ? 3 : 2; }
+  static constexpr int ns(size_t bstage) { return stages_for(bstage, pst(bstage)); }
+  static constexpr size_t smem(size_t bstage) {
+    return fixed(pst(bstage)) + (size_t)ns(bstage) * ((size_t)QMM_BM * 128 + bstage);
   }
+  // 512 tokens (the widest tile) must still leave two stages.
+  static_assert(stages_for((size_t)512 * 128, 2) >= 2, "QMM ring must hold two stages at 512 tokens");
 };
 
 struct QmmArgs {
   const uint8_t* packed;
   int64_t N, K, M, row_bytes, packed_bytes;
   float* y;
-  int bn;
+  float* part;        // [row tiles x token groups][ksplit][T][128] partial tiles (ksplit > 1)
+  unsigned* tickets;  // [row tiles x token groups] (ksplit > 1)
+  int bn, nacc;       // MMA N per accumulator, accumulators per CTA
+  int ksplit, kbs;    // K splits, 256-blocks per split
   int* err;
 };
 
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31) == 0; }
+
+// Barrier 2: the decoder warps only.
+__device__ __forceinline__ void named_sync_decoders() {
+  asm volatile("bar.sync 2, %0;" ::"n"(32 * QMM_DEC_WARPS) : "memory");
+}
 
 // tcgen05 wrappers ------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
@@ -136,38 +157,36 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
   using G = QmmGeom<T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((0u - smem_u32(smem_raw)) & 1023u);  // 1024-aligned, shared provenance kept
-  const int bn = a.bn;
-  const int NS = QmmPipe<T>::ns(bn);
-  const int PST = QmmPipe<T>::pst(bn);
+  const int bn = a.bn, nacc = a.nacc, ttok = a.bn * a.nacc;
+  const size_t bbytes = (size_t)ttok * 128;                   // one activation stage: T tokens x 64 k fp16
+  const int NS = QmmPipe<T>::ns(bbytes);
+  const int PST = QmmPipe<T>::pst(bbytes);
   uint8_t* astage = smem;                                     // NS x 16 KB
-  uint8_t* bstage = astage + (size_t)NS * QMM_BM * 128;       // NS x bn*128
-  uint8_t* pstage = bstage + (size_t)NS * bn * 128;           // PST x PSTAGE
+  uint8_t* bstage = astage + (size_t)NS * QMM_BM * 128;       // NS x T*128
+  uint8_t* pstage = bstage + (size_t)NS * bbytes;             // PST x PSTAGE
   uint8_t* tab = pstage + (size_t)PST * G::PSTAGE;            // decode tables
   uint64_t* bars = reinterpret_cast<uint64_t*>(tab + G::TAB);
   uint64_t* full_a = bars;          // [NS]  count 8 (decoder warps)
   uint64_t* full_b = bars + 4;      // [NS]  count 1 (TMA)
   uint64_t* empty = bars + 8;       // [NS]  count 1 (tcgen05.commit)
-  uint64_t* pfull = bars + 12;      // [PST] count 1
-  uint64_t* pempty = bars + 16;     // [PST] count 8
   uint64_t* accf = bars + 20;       // [1]   count 1
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+  unsigned* last_flag = reinterpret_cast<unsigned*>(bars + 22);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n0 = (int64_t)blockIdx.x * QMM_BM;
-  const int m0 = blockIdx.y * bn;
-  const int nks = (int)(a.K / QMM_BK);
-  const int nkb = (int)(a.K / QK);
-  const uint32_t tcols = bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : 256;
+  const int m0 = blockIdx.y * ttok;
+  const int split = blockIdx.z;
+  const int kb0 = split * a.kbs;                                  // this CTA's 256-blocks
+  const int nkb = min(a.kbs, (int)(a.K / QK) - kb0);
+  const int nks = nkb * (QK / QMM_BK);
+  const uint32_t tcols = ttok <= 32 ? 32 : ttok <= 64 ? 64 : ttok <= 128 ? 128 : ttok <= 256 ? 256 : 512;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; s++) {
       mbar_init(&full_a[s], QMM_DEC_WARPS);
       mbar_init(&full_b[s], 1);
       mbar_init(&empty[s], 1);
-    }
-    for (int s = 0; s < PST; s++) {
-      mbar_init(&pfull[s], 1);
-      mbar_init(&pempty[s], QMM_DEC_WARPS);
     }
     mbar_init(accf, 1);
     fence_mbar_init();
@@ -188,43 +207,16 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
       if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
       if (!ok) break;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full_b[s], (uint32_t)bn * 128u);
-        tma_load_2d(bstage + (size_t)s * bn * 128, &xmap, ks * QMM_BK, m0, &full_b[s]);
+        mbar_arrive_expect_tx(&full_b[s], (uint32_t)bbytes);
+        for (int j = 0; j < nacc; j++)
+          tma_load_2d(bstage + (size_t)s * bbytes + (size_t)j * bn * 128, &xmap, kb0 * QK + ks * QMM_BK, m0 + j * bn,
+                      &full_b[s]);
       }
       __syncwarp();
       if (++s == NS) { s = 0; n++; }
     }
   } else if (warp == 2) {
-    // ---------------- packed weight blocks ----------------
-    const uintptr_t pbase = reinterpret_cast<uintptr_t>(a.packed);
-    const uint64_t policy = l2_policy_evict_first();
-    int ps = 0, pn = 0;
-    for (int kb = 0; kb < nkb && ok; kb++, (++ps == PST ? (ps = 0, pn++) : 0)) {
-      if (pn > 0) ok = mbar_wait_bounded(&pempty[ps], (uint32_t)((pn - 1) & 1), a.err);
-      if (!ok) break;
-      uint32_t bytes = 0;
-      for (int i = 0; i < 4; i++) {
-        const int r = lane + 32 * i;
-        const int64_t row = n0 + r;
-        if (row >= a.N) continue;
-        const int64_t off = row * a.row_bytes + (int64_t)kb * G::BB;
-        const int64_t end = off + G::BB;
-        const int64_t off_al = off & ~int64_t(15);
-        int64_t end_al = (end + 15) & ~int64_t(15);
-        if (end_al > a.packed_bytes) end_al = end & ~int64_t(15);
-        uint8_t* dst = pstage + (size_t)ps * G::PSTAGE + r * G::PROWB;
-        if (end_al > off_al) {
-          fence_proxy_async_smem();
-          bulk_g2s_stream(dst, reinterpret_cast<const void*>(pbase + off_al), (uint32_t)(end_al - off_al),
-                          &pfull[ps], policy);
-          bytes += (uint32_t)(end_al - off_al);
-        }
-        for (int64_t t = max(end_al, off_al); t < end; t++) dst[t - off_al] = a.packed[t];
-      }
-      const uint32_t total = __reduce_add_sync(0xffffffffu, bytes);
-      __syncwarp();
-      if (lane == 0) mbar_arrive_expect_tx(&pfull[ps], total);
-    }
+    // (idle: the decoder warps fetch their own packed rows)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     const uint32_t idesc = f16_idesc(bn);
@@ -236,11 +228,13 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
       tc_fence_after();
       if (lane == 0) {
         const uint32_t aaddr = smem_u32(astage + (size_t)s * QMM_BM * 128);
-        const uint32_t baddr = smem_u32(bstage + (size_t)s * bn * 128);
+        const uint32_t baddr = smem_u32(bstage + (size_t)s * bbytes);
+        for (int j = 0; j < nacc; j++) {
 #pragma unroll
-        for (int kk = 0; kk < QMM_BK / 16; kk++)
-          tc_mma_f16(tmem_d, sw128_desc(aaddr + kk * 32), sw128_desc(baddr + kk * 32), idesc,
-                     (ks | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < QMM_BK / 16; kk++)
+            tc_mma_f16(tmem_d + (uint32_t)(j * bn), sw128_desc(aaddr + kk * 32),
+                       sw128_desc(baddr + (uint32_t)(j * bn * 128) + kk * 32), idesc, (ks | kk) != 0 ? 1u : 0u);
+        }
         tc_commit(&empty[s]);
       }
       __syncwarp();
@@ -249,22 +243,50 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
     __syncwarp();
   } else {
     // ---------------- decoders + epilogue ----------------
-    // Two warps per TMEM sub-partition: `half` 0 decodes k 0..31 of each
-    // 64-wide step, `half` 1 decodes k 32..63; in the epilogue they split the
-    // BN token columns.
+    // Decoding: warp dw owns tile rows 16dw .. 16dw+15; lanes 2i and 2i+1
+    // share row 16dw+i, `half` 0 decoding k 0..31 and `half` 1 k 32..63 of
+    // every 64-wide step.  Each warp fetches its own rows' packed blocks with
+    // per-thread 16-byte async copies into a PST-deep ring (every slot but
+    // the one being decoded is in flight), so no producer or barrier sits
+    // between HBM and the decoders.  In the epilogue the TMEM sub-partition
+    // decides the rows.
     using F = Fast<T>;
-    const int dw = warp - QMM_DEC0, half = dw >> 2, sub = warp & 3;
-    const int r = 32 * sub + lane;  // tile row == TMEM lane
+    const int dw = warp - QMM_DEC0;
+    const int half = lane & 1;
+    const int r = 16 * dw + (lane >> 1);  // tile row decoded by this lane
     const int64_t row = n0 + r;
     const bool live = row < a.N;
     const int64_t roff = row * a.row_bytes;
     const __half2 off2 = __float2half2_rn(1152.f);
-    int ps = 0, pn = 0;  // packed stage / use count
-    int s = 0, n = 0;    // A/B stage / use count
-    for (int kb = 0; kb < nkb && ok; kb++, (++ps == PST ? (ps = 0, pn++) : 0)) {
-      ok = mbar_wait_bounded(&pfull[ps], (uint32_t)(pn & 1), a.err);
-      if (!ok) break;
-      const uint8_t* blk = pstage + (size_t)ps * G::PSTAGE + r * G::PROWB + (int)((roff + (int64_t)kb * G::BB) & 15);
+    const uintptr_t pbase = reinterpret_cast<uintptr_t>(a.packed);
+    const uint64_t policy = l2_policy_evict_first();
+    uint8_t* pslot = pstage + r * G::PROWB;
+    // Copies block kb of this row into ring slot ps (this lane's alternate
+    // 16-byte chunks); always commits a group so group counts stay uniform.
+    auto fetch = [&](int kb, int ps) {
+      if (live && kb < nkb) {
+        const int64_t off = roff + (int64_t)(kb0 + kb) * G::BB;
+        const int64_t end = off + G::BB;
+        const int64_t off_al = off & ~int64_t(15);
+        int64_t end_al = (end + 15) & ~int64_t(15);
+        if (end_al > a.packed_bytes) end_al = end & ~int64_t(15);
+        uint8_t* dst = pslot + (size_t)ps * G::PSTAGE;
+        const int nch = (int)((end_al - off_al) >> 4);
+        for (int c = half; c < nch; c += 2)
+          cp_async16_stream(dst + 16 * c, reinterpret_cast<const void*>(pbase + off_al + 16 * c), policy);
+        // Tail beyond the last 16-byte boundary of the buffer: plain loads.
+        if (half == 0)
+          for (int64_t t = max(end_al, off_al); t < end; t++) dst[t - off_al] = a.packed[t];
+      }
+      cp_async_commit();
+    };
+    for (int j = 0; j < PST; j++) fetch(j, j);
+    int ps = 0;        // packed ring slot
+    int s = 0, n = 0;  // A/B stage / use count
+    for (int kb = 0; kb < nkb && ok; kb++) {
+      if (PST == 3) cp_async_wait<2>(); else cp_async_wait<1>();  // block kb landed
+      __syncwarp();  // both lanes' chunks of the row are visible
+      const uint8_t* blk = pslot + (size_t)ps * G::PSTAGE + (int)((roff + (int64_t)(kb0 + kb) * G::BB) & 15);
       for (int q = 0; q < 4 && ok; q++, (++s == NS ? (s = 0, n++) : 0)) {
         if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
         if (!ok) break;
@@ -322,25 +344,79 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
         __syncwarp();
         if (lane == 0) mbar_arrive(&full_a[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&pempty[ps]);
+      __syncwarp();  // the ring slot is no longer read: refill it
+      fetch(kb + PST, ps);
+      if (++ps == PST) ps = 0;
     }
-    // epilogue: this warp's TMEM lanes, half of the BN columns
+    cp_async_wait<0>();
+    // Epilogue rows: TMEM sub-partition (warp & 3) x lane; the two warps of a
+    // sub-partition take half of the T columns each.
+    const int sub = warp & 3, ehalf = dw >> 2;
+    const int er = 32 * sub + lane;
+    const int64_t erow = n0 + er;
+    const bool elive = erow < a.N;
+    // epilogue: this warp's TMEM lanes, half of the T columns
     pdl_launch_dependents();
     pdl_wait();  // global writes only after the preceding kernel completed
     if (ok) ok = mbar_wait_bounded(accf, 0u, a.err);
     tc_fence_after();
-    if (ok) {
-      const uint32_t lane_base = (uint32_t)(32 * sub) << 16;
-      const int cols = bn / 2;
-      for (int j0 = half * cols; j0 < (half + 1) * cols; j0 += 16) {
-        uint32_t vv[16];
-        tmem_ld16(tmem_d + lane_base + (uint32_t)j0, vv);
-        if (live) {
+    const uint32_t lane_base = (uint32_t)(32 * sub) << 16;
+    const int cols = ttok / 2;
+    const int64_t tile = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+    if (a.ksplit == 1) {
+      if (ok) {
+        for (int j0 = ehalf * cols; j0 < (ehalf + 1) * cols; j0 += 16) {
+          uint32_t vv[16];
+          tmem_ld16(tmem_d + lane_base + (uint32_t)j0, vv);
+          if (elive) {
+#pragma unroll
+            for (int jj = 0; jj < 16; jj++) {
+              const int64_t m = (int64_t)m0 + j0 + jj;
+              if (m < a.M) a.y[m * a.N + erow] = __uint_as_float(vv[jj]);
+            }
+          }
+        }
+      }
+    } else {
+      // Partial tile of this split -> scratch [tile][split][T][128] (rows
+      // contiguous: coalesced), then a ticket; the last split to arrive sums
+      // all splits in order.
+      float* mine = a.part + ((tile * a.ksplit + split) * ttok) * QMM_BM;
+      if (ok) {
+        for (int j0 = ehalf * cols; j0 < (ehalf + 1) * cols; j0 += 16) {
+          uint32_t vv[16];
+          tmem_ld16(tmem_d + lane_base + (uint32_t)j0, vv);
+#pragma unroll
+          for (int jj = 0; jj < 16; jj++) mine[(int64_t)(j0 + jj) * QMM_BM + er] = __uint_as_float(vv[jj]);
+        }
+      }
+      named_sync_decoders();
+      if (warp == QMM_DEC0 && lane == 0) {
+        const unsigned prev = atom_add_acq_rel_gpu(a.tickets + tile, 1u);
+        *last_flag = (prev + 1u == (unsigned)a.ksplit) ? 1u : 0u;
+        if (prev + 1u == (unsigned)a.ksplit) a.tickets[tile] = 0u;
+      }
+      named_sync_decoders();
+      if (*last_flag && elive && ok) {
+        __threadfence();
+        // 16 columns x all splits (<= QMM_KSPLIT_MAX) of loads in flight per
+        // batch; sums in split order.
+        const float* base = a.part + (tile * a.ksplit * ttok) * QMM_BM;
+        for (int j0 = ehalf * cols; j0 < (ehalf + 1) * cols && m0 + j0 < a.M; j0 += 16) {
+          float v[QMM_KSPLIT_MAX][16];
+#pragma unroll
+          for (int z = 0; z < QMM_KSPLIT_MAX; z++) {
+#pragma unroll
+            for (int jj = 0; jj < 16; jj++)
+              v[z][jj] = z < a.ksplit ? __ldcg(base + ((int64_t)z * ttok + j0 + jj) * QMM_BM + er) : 0.f;
+          }
 #pragma unroll
           for (int jj = 0; jj < 16; jj++) {
+            float acc = v[0][jj];
+#pragma unroll
+            for (int z = 1; z < QMM_KSPLIT_MAX; z++) acc += v[z][jj];  // zeros beyond ksplit
             const int64_t m = (int64_t)m0 + j0 + jj;
-            if (m < a.M) a.y[m * a.N + row] = __uint_as_float(vv[jj]);
+            if (m < a.M) a.y[m * a.N + erow] = acc;
           }
         }
       }
@@ -378,27 +454,69 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// Token tile: the whole M when it fits one MMA (N <= 256, multiple of 32 so
-// the two epilogue warps take 16-column TMEM loads), else 256.
-int qmm_pick_bn(int64_t M) {
-  if (M <= 32) return 32;
-  if (M <= 256) return (int)((M + 31) / 32 * 32);
-  return 256;
+// Launch plan: token tile T (one accumulator of round32(M) tokens up to 256,
+// else two accumulators of up to 256 tokens each), row tiles x token groups,
+// and a K split when that grid would leave most SMs idle.
+static int qmm_sm_count() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+      sms = n;
+    else {
+      cudaGetLastError();
+      sms = 148;
+    }
+  }
+  return sms;
 }
 
-size_t qmm_x16_bytes(int x_dtype, int64_t M, int64_t K) {
-  return x_dtype == DT_F16 ? 0 : (size_t)(((M * K * 2) + 255) / 256 * 256);
+static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+QmmPlan qmm_plan(int t, int64_t N, int64_t K, int64_t M, int x_dtype) {
+  (void)t;
+  QmmPlan p = {};
+  if (M <= 256) {
+    p.nacc = 1;
+    p.bn = (int)std::max<int64_t>(32, (M + 31) / 32 * 32);
+  } else {
+    p.nacc = 2;
+    const int64_t groups = (M + 511) / 512;
+    const int64_t per = (M + groups - 1) / groups;            // tokens per group, <= 512
+    p.bn = (int)std::min<int64_t>(256, ((per + 1) / 2 + 31) / 32 * 32);
+  }
+  const int64_t ttok = (int64_t)p.bn * p.nacc;
+  p.row_tiles = (N + QMM_BM - 1) / QMM_BM;
+  p.token_groups = (M + ttok - 1) / ttok;
+  const int64_t ctas = p.row_tiles * p.token_groups;
+  const int nkb = (int)(K / QK);
+  const int sms = qmm_sm_count();
+  p.ksplit = 1;
+  if (ctas * 4 < (int64_t)sms * 3 && ctas <= QMM_TICKETS)
+    p.ksplit = (int)std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(nkb, QMM_KSPLIT_MAX), sms / ctas));
+  p.kbs = (nkb + p.ksplit - 1) / p.ksplit;
+  p.ksplit = (nkb + p.kbs - 1) / p.kbs;
+  // Nothing but tickets is ever written to [0, QMM_TICKET_BYTES), whatever
+  // the shape, so a workspace zero-filled once keeps zero tickets.
+  size_t off = QMM_TICKET_BYTES;
+  if (p.ksplit > 1) {
+    p.off_part = off;
+    off += align256((size_t)ctas * p.ksplit * ttok * QMM_BM * sizeof(float));
+  }
+  p.off_x16 = off;
+  if (x_dtype != DT_F16) off += align256((size_t)M * K * 2);
+  p.workspace = off > QMM_TICKET_BYTES ? off : 0;
+  return p;
 }
 
-#define GSQ_QMM_SMEM_CASE(TT) case TT: return QmmPipe<TT>::smem(bn);
-size_t qmm_smem(int t, int bn) {
-  switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMM_SMEM_CASE) }
-  return 0;
+size_t qmm_workspace_bytes(int t, int64_t N, int64_t K, int64_t M, int x_dtype) {
+  return qmm_plan(t, N, K, M, x_dtype).workspace;
 }
 
 template <int T>
-static cudaError_t qmm_launch_t(const QmmArgs& a, const CUtensorMap& map, cudaStream_t st) {
-  const size_t smem = QmmPipe<T>::smem(a.bn);
+static cudaError_t qmm_launch_t(const QmmArgs& a, const QmmPlan& p, const CUtensorMap& map, cudaStream_t st) {
+  const size_t smem = QmmPipe<T>::smem((size_t)a.bn * a.nacc * 128);
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -407,15 +525,19 @@ static cudaError_t qmm_launch_t(const QmmArgs& a, const CUtensorMap& map, cudaSt
     if (e != cudaSuccess) return e;
     configured[dev] = (int)smem;
   }
-  dim3 grid((unsigned)((a.N + QMM_BM - 1) / QMM_BM), (unsigned)((a.M + a.bn - 1) / a.bn));
+  dim3 grid((unsigned)p.row_tiles, (unsigned)p.token_groups, (unsigned)p.ksplit);
   return launch_pdl(qmm_kernel<T>, grid, dim3(QMM_THREADS), smem, st, a, map);
 }
 
-#define GSQ_QMM_LAUNCH_CASE(TT) case TT: return qmm_launch_t<TT>(a, map, st);
+#define GSQ_QMM_LAUNCH_CASE(TT) case TT: return qmm_launch_t<TT>(a, p, map, st);
 
-// x16 must hold M*K fp16 values (16-byte aligned); it may alias x when x is fp16.
+// ws holds the plan's scratch (zero-filled once by the caller; the ticket
+// region is left zero-filled by every call).
 cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-                       float* y, __half* x16, int* err, cudaStream_t st, const char** why) {
+                       float* y, void* ws, int* err, cudaStream_t st, const char** why) {
+  const QmmPlan p = qmm_plan(t, N, K, M, x_dtype);
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  __half* x16 = reinterpret_cast<__half*>(wsb + p.off_x16);
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) { *why = "cuTensorMapEncodeTiled unavailable"; return cudaErrorNotSupported; }
   if (x_dtype != DT_F16) {
@@ -431,7 +553,10 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
   a.packed = packed; a.N = N; a.K = K; a.M = M;
   a.row_bytes = (K / QK) * block_bytes(t);
   a.packed_bytes = N * a.row_bytes;
-  a.y = y; a.bn = qmm_pick_bn(M); a.err = err;
+  a.y = y; a.err = err;
+  a.bn = p.bn; a.nacc = p.nacc; a.ksplit = p.ksplit; a.kbs = p.kbs;
+  a.tickets = p.ksplit > 1 ? reinterpret_cast<unsigned*>(wsb) : nullptr;
+  a.part = p.ksplit > 1 ? reinterpret_cast<float*>(wsb + p.off_part) : nullptr;
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};

@@ -70,6 +70,7 @@ struct QmvArgs {
   int64_t N, K, row_bytes, packed_bytes, tiles;
   int rows, x_dtype, y_dtype, kb, bps, slices, aligned, ns;
   int cb, rowb, stage;  // ring geometry: blocks per stage, staged row stride, stage bytes
+  int pre;              // stages issued before the activations are quantised (<= ns)
 };
 
 // Staged row stride for cb blocks: the copied bytes plus head/tail 16-byte
@@ -423,6 +424,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   uint64_t* empty = full + QMV_NS_MAX;                          // [NS] stage released by all consumers
   uint64_t* segb = empty + QMV_NS_MAX;                          // [RB] segment row sums posted by all consumers
   uint64_t* rfree = segb + QMV_RED_BUFS;                        // [RB] segment row sums read
+  uint64_t* xready = rfree + QMV_RED_BUFS;                      // activations quantised
   float* red = reinterpret_cast<float*>(smem + G::TAB + 256);
   uint8_t* ring = smem + G::TAB + 256 + QMV_RED_BYTES;
   const int CB = a.cb, ROWB = a.rowb, STAGE = a.stage;
@@ -449,6 +451,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
       mbar_init(&segb[s], QMV_CWARPS);
       mbar_init(&rfree[s], 1);
     }
+    mbar_init(xready, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -463,6 +466,10 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     uint32_t ph = 0;
     bool dead = false;
     while (!cur.done()) {
+      // The first `pre` stages go out at once (before the previous kernel
+      // has finished: weights only); further stages wait until the
+      // activations are in, so their loads do not queue behind weights.
+      if (i == a.pre && i < NS && !dead && !mbar_wait_bounded(xready, 0u, a.err)) dead = true;
       if (i >= NS && !dead && !mbar_wait_bounded(&empty[s], ph ^ 1u, a.err)) dead = true;
       const int nblk = cur.chunk(CB);
       uint32_t bytes = 0;
@@ -542,6 +549,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   pdl_wait();
   quantise_slice<T, NB, F::HAS_BIAS>(a, btile, kb0, w, KS, xq_s, xs_s, xsum_s);
   named_sync_consumers();
+  if (threadIdx.x == 0) mbar_arrive(xready);
 
   const int g = lane >> 2, tq = lane & 3;
   // Activation-operand identity of this lane (column g of the MMA) and its
@@ -803,6 +811,7 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
   p.smem = fixed + (size_t)p.ns * stage + xbytes(p.bps);
   p.rowb = qmv_rowb(p.cb, bb);
   p.stage = (int)stage;
+  p.pre = p.ns;
   const bool split = !(p.slices == 1 && (p.aligned || p.tiles % p.ctas == 0));
   if (split && p.aligned) {
     p.ctas = 0;  // not plannable: slices need tickets (K beyond the activation budget with > 1M rows)
@@ -877,6 +886,7 @@ cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, in
   a.cb = p.cb;
   a.rowb = p.rowb;
   a.stage = p.stage;
+  a.pre = p.pre;
   return qmv_launch(t, a, p, st);
 }
 

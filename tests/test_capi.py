@@ -72,5 +72,6 @@ def test_workspace_sizes_are_plain_host_math():
     for q in SUPPORTED_QUANT_TYPES:
         t = type_id(q)
         assert lib.gsq_qmv_workspace_size(t, 17408, 5120, 1) >= 0
-        assert lib.gsq_qmm_workspace_size(t, 17408, 5120, 512, 2) == 512 * 5120 * 2
+        # a fixed 64 KiB ticket region, then (bf16 input) an fp16 copy of x
+        assert lib.gsq_qmm_workspace_size(t, 17408, 5120, 512, 2) == 65536 + 512 * 5120 * 2
         assert lib.gsq_qmm_workspace_size(t, 17408, 5120, 512, 1) == 0

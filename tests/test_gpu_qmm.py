@@ -9,7 +9,7 @@ import torch
 
 from gpu_util import REL_L2, cuda, dense_gpu, random_packed_gpu, rel_l2
 from gsq_b200.quant.layouts import SUPPORTED_QUANT_TYPES
-from gsq_b200.quant.synthetic import random_activations, random_matrix
+from gsq_b200.quant.synthetic import random_activations, random_matrix, random_matrix_torch
 from gsq_b200.runtime.kernels import quantized_matmul
 
 pytestmark = pytest.mark.gpu
@@ -62,3 +62,14 @@ def test_qmm_config3(qtype, nk, m):
     y = quantized_matmul(x, packed, qtype=qtype, out_features=n, in_features=k, out_dtype=torch.float32)
     exp = x.double() @ dense_gpu(packed, qtype, n, k).T
     assert rel_l2(y.cpu(), exp.cpu()) <= REL_L2
+
+
+def test_qmm_split_k_deterministic():
+    """Shapes with few row tiles split K over several CTAs; the partial tiles
+    are summed in split order, so repeated calls agree bit for bit."""
+    w = random_matrix_torch("IQ4_XS", 640, 17408, seed=5)
+    x = torch.randn(512, 17408, device="cuda", dtype=torch.bfloat16)
+    a = quantized_matmul(x, w, qtype="IQ4_XS", out_features=640, in_features=17408, out_dtype=torch.float32)
+    b = quantized_matmul(x, w, qtype="IQ4_XS", out_features=640, in_features=17408, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
