@@ -346,18 +346,45 @@ template <> struct Fast<T_IQ1_M> {
 // power of two, the matvec feeds it unshifted to the u8 x s8 tensor-core MMA
 // and folds the power of two into the scale of that 32-wide activation group
 // (xgroup_scale(g), g = group index along K).  Entries stay below 256.
+//
+// IQ3_XXS reads its entries from a pre-signed table (grid word x 4-bit sign
+// group, 16 KB, gen_tables.py) instead of expanding sign masks: the same
+// number of shared loads, no mask arithmetic and no second (masked) MMA.
+// (The same scheme for IQ3_S and IQ2_XXS needs 32 KB tables; the shared
+// memory they take from the stage ring costs more than the masks save.)
 template <int T>
 struct MvDecode {
   static constexpr bool UNSIGNED = false;
+  static constexpr bool SPLIT = Fast<T>::SPLIT;
+  static constexpr int TAB_BYTES = Fast<T>::TAB_BYTES;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { Fast<T>::load_tables(tab, tid, nthr); }
   __device__ static float xgroup_scale(int) { return 1.f; }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
     Fast<T>::entry(b, c32, tq, tab, lo, hi);
   }
 };
 
+static __device__ __align__(16) const int8_t kIq3xxsSigned[256 * 16 * 4] = GSQ_INIT_IQ3XXS_SIGNED;
+
+template <>
+struct MvDecode<T_IQ3_XXS> {
+  static constexpr bool UNSIGNED = false, SPLIT = false;
+  static constexpr int TAB_BYTES = 256 * 16 * 4;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kIq3xxsSigned, TAB_BYTES, tid, nthr); }
+  __device__ static float xgroup_scale(int) { return 1.f; }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const uint32_t idx = ld16a2(b + 2 + 8 * c32 + 2 * tq);
+    const uint32_t s8 = ksign((ld32a2(b + 66 + 4 * c32) >> (7 * tq)) & 127u);
+    lo = lds32(tab + 4 * (((idx & 255u) << 4) | (s8 & 15u)));
+    hi = lds32(tab + 4 * (((idx >> 8) << 4) | (s8 >> 4)));
+  }
+};
+
 template <>
 struct MvDecode<T_Q4_K> {  // odd 32-groups are the high nibbles: 16 q <= 240
-  static constexpr bool UNSIGNED = true;
+  static constexpr bool UNSIGNED = true, SPLIT = false;
+  static constexpr int TAB_BYTES = 0;
+  __device__ static void load_tables(uint8_t*, int, int) {}
   __device__ static float xgroup_scale(int g) { return (g & 1) ? 0.0625f : 1.f; }
   __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t*, uint32_t& lo, uint32_t& hi) {
     const uint2 w = ld64a8(b + 16 + (c32 >> 1) * 32 + 8 * tq);
@@ -369,7 +396,9 @@ struct MvDecode<T_Q4_K> {  // odd 32-groups are the high nibbles: 16 q <= 240
 
 template <>
 struct MvDecode<T_Q2_K> {  // 32-group g reads bit plane g & 3: 4^p q <= 192
-  static constexpr bool UNSIGNED = true;
+  static constexpr bool UNSIGNED = true, SPLIT = false;
+  static constexpr int TAB_BYTES = 0;
+  __device__ static void load_tables(uint8_t*, int, int) {}
   __device__ static float xgroup_scale(int g) {
     return (g & 3) == 0 ? 1.f : (g & 3) == 1 ? 0.25f : (g & 3) == 2 ? 0.0625f : 0.015625f;
   }

@@ -83,7 +83,7 @@ __host__ __device__ constexpr int qmv_rowb(int cb, int bb) {
 template <int T>
 struct QmvGeom {
   static constexpr int BB = block_bytes(T);
-  static constexpr int TAB = (Fast<T>::TAB_BYTES + 127) / 128 * 128;
+  static constexpr int TAB = (MvDecode<T>::TAB_BYTES + 127) / 128 * 128;
   static constexpr int FIXED = 128 /*align*/ + TAB + 256 /*mbarriers*/ + QMV_RED_BYTES;
   // Stages of 8 blocks: two of them plus the activations of one block always
   // fit; the plan may choose wider stages (16 or 32 blocks) per call.
@@ -543,7 +543,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   }
 
   // -------------------------------------------------------------- consumers
-  F::load_tables(tab, threadIdx.x, QMV_CTHREADS);
+  MV::load_tables(tab, threadIdx.x, QMV_CTHREADS);
   // Everything above reads only weights and tables; from here on the kernel
   // reads activations / scratch that an earlier kernel in the stream writes.
   pdl_wait();
@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
           const int c32 = set * MMAS + j;
           const bool on = (j == jsel);
           const uint32_t bx0 = on ? xw0 : 0u, bx1 = on ? xw1 : 0u;
-          if constexpr (F::SPLIT) {
+          if constexpr (MV::SPLIT) {
             uint32_t a0, a1, a2, a3, m0, m1, m2, m3;
             F::entry_split(b0, c32, tq, tab, a0, a2, m0, m2);
             F::entry_split(b1, c32, tq, tab, a1, a3, m1, m3);
@@ -648,7 +648,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
 #pragma unroll
           for (int q = 0; q < 4; q++) Cc[q] += Cb[q];
         }
-        if constexpr (F::SPLIT) {
+        if constexpr (MV::SPLIT) {
 #pragma unroll
           for (int q = 0; q < 4; q++) Cc[q] -= 2 * (Nn[q] + Nb[q]);
         }
