@@ -173,10 +173,14 @@ __device__ __forceinline__ void quantise_round(const QmvArgs& a, int btile, int 
     // hi, byte 0 is lo + 128, and hi + lo/256 = rint(256 u)/256.  The scale
     // and its reciprocal need only agree to a few ulps: the levels are
     // reconstructed with xs, never with inv.
+    // Rounding: adding 1.5 * 2^23 leaves the float grid at spacing 1, so the
+    // fma rounds 256 u + 128 once, to nearest even, and its bit pattern is
+    // 0x4B400000 + t: bytes 0 and 1 are those of t (|t| < 2^15).  This
+    // replaces a float-to-int conversion per value.
     const float inv = am > 0.f ? __fdividef(127.f * 256.f, am) : 0.f;
     uint32_t t[8];
 #pragma unroll
-    for (int j = 0; j < 8; j++) t[j] = (uint32_t)__float2int_rn(fmaf(v[j], inv, 128.f));
+    for (int j = 0; j < 8; j++) t[j] = __float_as_uint(fmaf(v[j], inv, 12582912.f + 128.f));
     uint32_t hw[2], lw[2];
 #pragma unroll
     for (int q = 0; q < 2; q++) {
