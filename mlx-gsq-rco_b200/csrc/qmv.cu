@@ -35,8 +35,9 @@
 //    start before griddepcontrol.wait, overlapping the previous kernel; the
 //    activations are read after it.
 #include <algorithm>
+#include <type_traits>
 
-#include "gsq_fast.cuh"
+#include "gsq_mv.cuh"
 #include "gsq_host.h"
 
 namespace gsq {
@@ -83,13 +84,22 @@ __host__ __device__ constexpr int qmv_rowb(int cb, int bb) {
 template <int T>
 struct QmvGeom {
   static constexpr int BB = block_bytes(T);
-  static constexpr int TAB = (MvDecode<T>::TAB_BYTES + 127) / 128 * 128;
-  static constexpr int FIXED = 128 /*align*/ + TAB + 256 /*mbarriers*/ + QMV_RED_BYTES;
+  static constexpr int TAB = (Mv<T>::TAB_BYTES + 127) / 128 * 128;
+  static constexpr int FIXED = 128 /*align*/ + TAB + 256 /*mbarriers*/ + QK /*zeros*/ + QMV_RED_BYTES;
   // Stages of 8 blocks: two of them plus the activations of one block always
   // fit; the plan may choose wider stages (16 or 32 blocks) per call.
   static_assert(FIXED + 2 * 16 * qmv_rowb(8, BB) + 2 * QMV_XBYTES_PER_BLOCK <= QMV_CTA_SMEM,
                 "ring must hold two stages");
 };
+
+// Calls f(std::integral_constant<int, i>) for i = I..N-1 (compile-time loop).
+template <int I, int N, typename Fn>
+__device__ __forceinline__ void static_for(Fn&& f) {
+  if constexpr (I < N) {
+    f(std::integral_constant<int, I>{});
+    static_for<I + 1, N>(f);
+  }
+}
 
 __device__ __forceinline__ void named_sync_consumers() {
   asm volatile("bar.sync 1, %0;" ::"n"(QMV_CTHREADS) : "memory");
@@ -408,16 +418,14 @@ __device__ void combine_piece(const QmvArgs& a, int btile, int slice, int C, int
 
 template <int T, int NB>
 __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
-  using F = Fast<T>;
-  using MV = MvDecode<T>;
+  using MV = Mv<T>;
   using G = QmvGeom<T>;
-  constexpr int UNIT = F::UNIT;
-  constexpr int UPS = 4 / NB;            // units per set
-  constexpr int KSET = UNIT * UPS;       // k per set
-  constexpr int MMAS = KSET / 32;        // MMAs per set
-  constexpr int SETS = QK / KSET;        // sets per block
+  constexpr int UNIT = MV::UNIT;
+  constexpr int UPS = 4 / NB;            // unit slots (lanes of a quad per activation row)
+  constexpr int SETS = QK / (UNIT * UPS);  // units per slot and block
+  constexpr int MMAS = UNIT / (8 * NB);  // MMAs per set
   static_assert(MMAS >= 1, "set must cover at least one MMA");
-  static_assert(F::BLOCKED || UNIT == 32, "identity mapping needs 32-wide units");
+  static_assert(!MV::IDENT || UNIT == 32, "identity mapping needs 32-wide units");
   const int NS = a.ns, RB = a.ns + 1;
 
   // Shared memory: tables | mbarriers | row-sum buffers | ring | activations.
@@ -429,8 +437,11 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   uint64_t* segb = empty + QMV_NS_MAX;                          // [RB] segment row sums posted by all consumers
   uint64_t* rfree = segb + QMV_RED_BUFS;                        // [RB] segment row sums read
   uint64_t* xready = rfree + QMV_RED_BUFS;                      // activations quantised
-  float* red = reinterpret_cast<float*>(smem + G::TAB + 256);
-  uint8_t* ring = smem + G::TAB + 256 + QMV_RED_BYTES;
+  // B operand of the columns a lane does not feed: one block of zero
+  // activations (offsets within a block stay below QK).
+  int8_t* zeros = reinterpret_cast<int8_t*>(smem + G::TAB + 256);
+  float* red = reinterpret_cast<float*>(smem + G::TAB + 256 + QK);
+  uint8_t* ring = smem + G::TAB + 256 + QK + QMV_RED_BYTES;
   const int CB = a.cb, ROWB = a.rowb, STAGE = a.stage;
   const int KS = a.bps * QK;
   int8_t* xq_s = reinterpret_cast<int8_t*>(ring + NS * STAGE);
@@ -548,22 +559,35 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
 
   // -------------------------------------------------------------- consumers
   MV::load_tables(tab, threadIdx.x, QMV_CTHREADS);
+  if (threadIdx.x < QK / 4) reinterpret_cast<uint32_t*>(zeros)[threadIdx.x] = 0u;
   // Everything above reads only weights and tables; from here on the kernel
   // reads activations / scratch that an earlier kernel in the stream writes.
   pdl_wait();
-  quantise_slice<T, NB, F::HAS_BIAS>(a, btile, kb0, w, KS, xq_s, xs_s, xsum_s);
+  quantise_slice<T, NB, MV::BIAS>(a, btile, kb0, w, KS, xq_s, xs_s, xsum_s);
   named_sync_consumers();
   if (threadIdx.x == 0) mbar_arrive(xready);
 
   const int g = lane >> 2, tq = lane & 3;
-  // Activation-operand identity of this lane (column g of the MMA) and its
-  // epilogue identity (sub-block s_ep of each set, activation row b_ep).
+  // A operand: unit slot q and first entry e0 of this lane.  B operand:
+  // column g = (unit slot s_col, activation row b_col, level), live in the
+  // k rows of the lanes that feed slot s_col -- this lane's own k rows when
+  // s_col == q; otherwise it reads zeros.  Epilogue: slot q, activation row e0.
+  const int q = tq / NB, e0 = tq % NB;
   const int pcol = g >> 1, level = g & 1;
   const int s_col = pcol / NB, b_col = pcol % NB;
-  const int s_ep = tq / NB, b_ep = tq % NB;
-  const int8_t* xrow = xq_s + (b_col * 2 + level) * KS;
-  const float* xs_row = xs_s + b_ep * (KS / 32);
-  const float* xsum_row = xsum_s + b_ep * (KS / 16);
+  const bool xlive = s_col == q;
+  const int8_t* xbase = xq_s + (b_col * 2 + level) * KS + (MV::IDENT ? 32 * q + 4 * e0 : UNIT * q + 8 * e0);
+  const float* xs_row = xs_s + e0 * (KS / 32);
+  const float* xsum_row = xsum_s + e0 * (KS / 16);
+  // Per-entry path (formats without a lane-unit view): the four lanes of a
+  // quad feed consecutive entries of one 32-weight chunk; column g is live in
+  // the one MMA of a set whose unit slot is s_col, and lane (g, tq) scales
+  // unit slot q of every set.
+  using FO = Fast<T>;
+  using MD = MvDecode<T>;
+  constexpr int KSET = UNIT * UPS;  // k per set
+  const int8_t* xrow_o = xq_s + (b_col * 2 + level) * KS;
+  const int s_ep = q;
 
   // Row starts keep their offset modulo 16 from tile to tile (a tile is 16
   // rows), so the staged position of a block needs only 32-bit arithmetic.
@@ -589,86 +613,128 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
       const uint8_t* b0 = r0p + bi * G::BB;
       const uint8_t* b1 = r1p + bi * G::BB;
       const int kk = (cur.blk + bi) * QK;  // within the slice
-      const int8_t* xb = xrow + kk;
-      const float* xsb = xs_row + (kk >> 5);
-      const float* xub = xsum_row + (kk >> 4);
+      if constexpr (MV::LANE_UNITS) {
+        const int8_t* xl = xlive ? xbase + kk : zeros;
+        const auto row0 = MV::template row<NB>(b0, q);
+        const auto row1 = MV::template row<NB>(b1, q);
+        float A0 = 0.f, A1 = 0.f, M0 = 0.f, M1 = 0.f;
+        static_for<0, SETS>([&](auto s_) {
+          constexpr int S = decltype(s_)::value;
+          const int u = UPS * S + q;  // this lane's unit
+          int C[4] = {0, 0, 0, 0}, N[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int set = 0; set < SETS; set++) {
-        const int kset = set * KSET;
-        // Activation words for the one MMA of this set where column g is live.
-        uint32_t xw0, xw1;
-        int jsel;
-        if constexpr (UNIT == 32) {
-          jsel = s_col;
-          if constexpr (F::BLOCKED) {
-            const uint2 v = *reinterpret_cast<const uint2*>(xb + kset + 32 * s_col + 8 * tq);
-            xw0 = v.x; xw1 = v.y;
-          } else {
-            xw0 = *reinterpret_cast<const uint32_t*>(xb + kset + 32 * s_col + 4 * tq);
-            xw1 = *reinterpret_cast<const uint32_t*>(xb + kset + 32 * s_col + 16 + 4 * tq);
-          }
-        } else {
-          jsel = s_col >> 1;
-          const bool live = (s_col & 1) == (tq >> 1);
-          const uint2 v = *reinterpret_cast<const uint2*>(xb + kset + 32 * jsel + 8 * tq);
-          xw0 = live ? v.x : 0u;
-          xw1 = live ? v.y : 0u;
-        }
-        // Two independent accumulator chains (even / odd MMAs) halve the
-        // dependent tensor-core latency per set.  Sign-carrying formats run a
-        // second pair of chains on the negative-position magnitudes.
-        int Cc[4] = {0, 0, 0, 0}, Cb[4] = {0, 0, 0, 0};
-        int Nn[4] = {0, 0, 0, 0}, Nb[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int j = 0; j < MMAS; j++) {
-          const int c32 = set * MMAS + j;
-          const bool on = (j == jsel);
-          const uint32_t bx0 = on ? xw0 : 0u, bx1 = on ? xw1 : 0u;
-          if constexpr (MV::SPLIT) {
+          for (int j = 0; j < MMAS; j++) {
+            const int e = e0 + NB * j;
+            uint32_t bx0, bx1;
+            if constexpr (MV::IDENT) {
+              bx0 = *reinterpret_cast<const uint32_t*>(xl + 32 * UPS * S + 4 * NB * j);
+              bx1 = *reinterpret_cast<const uint32_t*>(xl + 32 * UPS * S + 16 + 4 * NB * j);
+            } else {
+              const uint2 v = *reinterpret_cast<const uint2*>(xl + UNIT * UPS * S + 8 * NB * j);
+              bx0 = v.x;
+              bx1 = v.y;
+            }
             uint32_t a0, a1, a2, a3, m0, m1, m2, m3;
-            F::entry_split(b0, c32, tq, tab, a0, a2, m0, m2);
-            F::entry_split(b1, c32, tq, tab, a1, a3, m1, m3);
-            if (j & 1) {
-              mma_s8(Cb, a0, a1, a2, a3, bx0, bx1);
-              mma_s8(Nb, a0 & m0, a1 & m1, a2 & m2, a3 & m3, bx0, bx1);
+            MV::template entry<S, NB>(b0, row0, u, e, tab, a0, a2, m0, m2);
+            MV::template entry<S, NB>(b1, row1, u, e, tab, a1, a3, m1, m3);
+            if constexpr (MV::UNSIGNED) mma_u8s8(C, a0, a1, a2, a3, bx0, bx1);
+            else mma_s8(C, a0, a1, a2, a3, bx0, bx1);
+            if constexpr (MV::SPLIT) mma_s8(N, a0 & m0, a1 & m1, a2 & m2, a3 & m3, bx0, bx1);
+          }
+          const int ku = kk + UNIT * u;  // within the slice
+          const float xs = xs_row[ku >> 5];
+          float xsum = 0.f;
+          if constexpr (MV::BIAS) {
+            xsum = xsum_row[ku >> 4];
+            if constexpr (UNIT == 32) xsum += xsum_row[(ku >> 4) + 1];
+          }
+          MV::template unit<S, NB>(b0, row0, u, C[0] * 256 + C[1], N[0] * 256 + N[1], xs, xsum, A0, M0);
+          MV::template unit<S, NB>(b1, row1, u, C[2] * 256 + C[3], N[2] * 256 + N[3], xs, xsum, A1, M1);
+        });
+        acc0 += MV::finish(b0, row0, A0, M0);
+        acc1 += MV::finish(b1, row1, A1, M1);
+      } else {
+        const int8_t* xb = xrow_o + kk;
+        const float* xsb = xs_row + (kk >> 5);
+        const float* xub = xsum_row + (kk >> 4);
+#pragma unroll
+        for (int set = 0; set < SETS; set++) {
+          const int kset = set * KSET;
+          // Activation words for the one MMA of this set where column g is live.
+          uint32_t xw0, xw1;
+          int jsel;
+          if constexpr (UNIT == 32) {
+            jsel = s_col;
+            if constexpr (FO::BLOCKED) {
+              const uint2 v = *reinterpret_cast<const uint2*>(xb + kset + 32 * s_col + 8 * tq);
+              xw0 = v.x; xw1 = v.y;
             } else {
-              mma_s8(Cc, a0, a1, a2, a3, bx0, bx1);
-              mma_s8(Nn, a0 & m0, a1 & m1, a2 & m2, a3 & m3, bx0, bx1);
+              xw0 = *reinterpret_cast<const uint32_t*>(xb + kset + 32 * s_col + 4 * tq);
+              xw1 = *reinterpret_cast<const uint32_t*>(xb + kset + 32 * s_col + 16 + 4 * tq);
             }
           } else {
-            uint32_t a0, a1, a2, a3;
-            MV::entry(b0, c32, tq, tab, a0, a2);
-            MV::entry(b1, c32, tq, tab, a1, a3);
-            if constexpr (MV::UNSIGNED) {
-              if (j & 1) mma_u8s8(Cb, a0, a1, a2, a3, bx0, bx1);
-              else mma_u8s8(Cc, a0, a1, a2, a3, bx0, bx1);
+            jsel = s_col >> 1;
+            const bool live = (s_col & 1) == (tq >> 1);
+            const uint2 v = *reinterpret_cast<const uint2*>(xb + kset + 32 * jsel + 8 * tq);
+            xw0 = live ? v.x : 0u;
+            xw1 = live ? v.y : 0u;
+          }
+          // Two independent accumulator chains (even / odd MMAs) halve the
+          // dependent tensor-core latency per set.  Sign-carrying formats run a
+          // second pair of chains on the negative-position magnitudes.
+          int Cc[4] = {0, 0, 0, 0}, Cb[4] = {0, 0, 0, 0};
+          int Nn[4] = {0, 0, 0, 0}, Nb[4] = {0, 0, 0, 0};
+#pragma unroll
+          for (int j = 0; j < MMAS; j++) {
+            const int c32 = set * MMAS + j;
+            const bool on = (j == jsel);
+            const uint32_t bx0 = on ? xw0 : 0u, bx1 = on ? xw1 : 0u;
+            if constexpr (MD::SPLIT) {
+              uint32_t a0, a1, a2, a3, m0, m1, m2, m3;
+              FO::entry_split(b0, c32, tq, tab, a0, a2, m0, m2);
+              FO::entry_split(b1, c32, tq, tab, a1, a3, m1, m3);
+              if (j & 1) {
+                mma_s8(Cb, a0, a1, a2, a3, bx0, bx1);
+                mma_s8(Nb, a0 & m0, a1 & m1, a2 & m2, a3 & m3, bx0, bx1);
+              } else {
+                mma_s8(Cc, a0, a1, a2, a3, bx0, bx1);
+                mma_s8(Nn, a0 & m0, a1 & m1, a2 & m2, a3 & m3, bx0, bx1);
+              }
             } else {
-              if (j & 1) mma_s8(Cb, a0, a1, a2, a3, bx0, bx1);
-              else mma_s8(Cc, a0, a1, a2, a3, bx0, bx1);
+              uint32_t a0, a1, a2, a3;
+              MD::entry(b0, c32, tq, tab, a0, a2);
+              MD::entry(b1, c32, tq, tab, a1, a3);
+              if constexpr (MD::UNSIGNED) {
+                if (j & 1) mma_u8s8(Cb, a0, a1, a2, a3, bx0, bx1);
+                else mma_u8s8(Cc, a0, a1, a2, a3, bx0, bx1);
+              } else {
+                if (j & 1) mma_s8(Cb, a0, a1, a2, a3, bx0, bx1);
+                else mma_s8(Cc, a0, a1, a2, a3, bx0, bx1);
+              }
             }
           }
-        }
-        if constexpr (MMAS > 1) {
+          if constexpr (MMAS > 1) {
 #pragma unroll
-          for (int q = 0; q < 4; q++) Cc[q] += Cb[q];
-        }
-        if constexpr (MV::SPLIT) {
+            for (int i = 0; i < 4; i++) Cc[i] += Cb[i];
+          }
+          if constexpr (MD::SPLIT) {
 #pragma unroll
-          for (int q = 0; q < 4; q++) Cc[q] -= 2 * (Nn[q] + Nb[q]);
-        }
-        const int unit = set * UPS + s_ep;
-        const int ku = unit * UNIT;  // within the block
-        const float xsv = xsb[ku >> 5];
-        float S0, B0, S1, B1;
-        F::affine(b0, unit, S0, B0);
-        F::affine(b1, unit, S1, B1);
-        acc0 = fmaf(S0, (float)(Cc[0] * 256 + Cc[1]) * xsv, acc0);
-        acc1 = fmaf(S1, (float)(Cc[2] * 256 + Cc[3]) * xsv, acc1);
-        if constexpr (F::HAS_BIAS) {
-          float xu = xub[ku >> 4];
-          if constexpr (UNIT == 32) xu += xub[(ku >> 4) + 1];
-          acc0 = fmaf(B0, xu, acc0);
-          acc1 = fmaf(B1, xu, acc1);
+            for (int i = 0; i < 4; i++) Cc[i] -= 2 * (Nn[i] + Nb[i]);
+          }
+          const int unit = set * UPS + s_ep;
+          const int ku = unit * UNIT;  // within the block
+          const float xsv = xsb[ku >> 5];
+          float S0, B0, S1, B1;
+          FO::affine(b0, unit, S0, B0);
+          FO::affine(b1, unit, S1, B1);
+          acc0 = fmaf(S0, (float)(Cc[0] * 256 + Cc[1]) * xsv, acc0);
+          acc1 = fmaf(S1, (float)(Cc[2] * 256 + Cc[3]) * xsv, acc1);
+          if constexpr (FO::HAS_BIAS) {
+            float xu = xub[ku >> 4];
+            if constexpr (UNIT == 32) xu += xub[(ku >> 4) + 1];
+            acc0 = fmaf(B0, xu, acc0);
+            acc1 = fmaf(B1, xu, acc1);
+          }
         }
       }
     }
@@ -689,8 +755,8 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
       if (seg_no >= RB && !dead && !mbar_wait_bounded(&rfree[rbuf], rph ^ 1u, a.err)) dead = true;
       float* rb = red + (rbuf * QMV_CWARPS + warp) * 32;
       if (tq < NB) {
-        rb[b_ep * 16 + g] = acc0;
-        rb[b_ep * 16 + g + 8] = acc1;
+        rb[e0 * 16 + g] = acc0;
+        rb[e0 * 16 + g + 8] = acc1;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&segb[rbuf]);
