@@ -72,6 +72,7 @@ struct QmvArgs {
   int rows, x_dtype, y_dtype, kb, bps, slices, aligned, ns;
   int cb, rowb, stage;  // ring geometry: blocks per stage, staged row stride, stage bytes
   int pre;              // stages issued before the activations are quantised (<= ns)
+  int xbulk;            // one 16-bit activation row, copied into shared memory in bulk
 };
 
 // Staged row stride for cb blocks: the copied bytes plus head/tail 16-byte
@@ -157,10 +158,11 @@ __device__ __forceinline__ void quantise_round(const QmvArgs& a, int btile, int 
     const int c = base + threadIdx.x + i * QMV_CTHREADS;
     const int b = c >= per_row ? 1 : 0;  // NB <= 2
     const int row = btile * NB + b;
-    if (c < total && row < a.rows)
+    if (c < total && row < a.rows) {
       load8<XT>(a.x, (int64_t)row * a.K + (int64_t)kb0 * QK + (c - b * per_row) * 8, raw[i]);
-    else
+    } else {
       raw[i][0] = raw[i][1] = make_uint4(0, 0, 0, 0);
+    }
   }
 #pragma unroll
   for (int i = 0; i < CH; i++) {
@@ -213,12 +215,105 @@ __device__ __forceinline__ void quantise_round(const QmvArgs& a, int btile, int 
   }
 }
 
+// Staged row (bulk path): each consumer thread quantises whole 32-groups of
+// the 16-bit row that the bulk copy left at xq -- every value of a group in
+// one thread, so no shuffles, about half the instructions per value of the
+// per-chunk form.  All threads read their raw words (up to QMV_XSTAGE_G groups)
+// before the first level is written over the staged row.
+constexpr int QMV_XSTAGE_G = 3;
+
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+template <typename XT> __device__ __forceinline__ float amax32(const uint4 (&r)[4]);
+template <> __device__ __forceinline__ float amax32<__half>(const uint4 (&r)[4]) {
+  __half2 m = __habs2(*reinterpret_cast<const __half2*>(&r[0].x));
+#pragma unroll
+  for (int i = 1; i < 16; i++) {
+    const uint32_t u = word_of(r[i >> 2], i & 3);
+    m = __hmax2(m, __habs2(*reinterpret_cast<const __half2*>(&u)));
+  }
+  const float2 f = __half22float2(m);
+  return fmaxf(f.x, f.y);
+}
+template <> __device__ __forceinline__ float amax32<__nv_bfloat16>(const uint4 (&r)[4]) {
+  uint32_t m = 0;  // |bf16| orders as its 15 low bits
+#pragma unroll
+  for (int i = 0; i < 16; i++) {
+    const uint32_t u = word_of(r[i >> 2], i & 3);
+    m = max(m, max(u & 0x7FFFu, (u >> 16) & 0x7FFFu));
+  }
+  return __uint_as_float(m << 16);
+}
+template <typename XT> __device__ __forceinline__ float2 pair32(const uint4 (&r)[4], int j);  // values 2j, 2j+1
+template <> __device__ __forceinline__ float2 pair32<__half>(const uint4 (&r)[4], int j) {
+  const uint32_t u = word_of(r[j >> 2], j & 3);
+  return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+template <> __device__ __forceinline__ float2 pair32<__nv_bfloat16>(const uint4 (&r)[4], int j) {
+  const uint32_t u = word_of(r[j >> 2], j & 3);
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+
+template <int T, bool SUMS, typename XT>
+__device__ void quantise_staged(int groups, int KS, int8_t* xq, float* xs, float* xsum) {
+  uint4 raw[QMV_XSTAGE_G][4];
+#pragma unroll
+  for (int i = 0; i < QMV_XSTAGE_G; i++) {
+    const int gg = threadIdx.x + i * QMV_CTHREADS;
+    const uint4* p = reinterpret_cast<const uint4*>(xq + 64 * gg);
+#pragma unroll
+    for (int w2 = 0; w2 < 4; w2++) raw[i][w2] = gg < groups ? p[w2] : make_uint4(0, 0, 0, 0);
+  }
+  named_sync_consumers();
+#pragma unroll
+  for (int i = 0; i < QMV_XSTAGE_G; i++) {
+    const int gg = threadIdx.x + i * QMV_CTHREADS;
+    if (gg >= groups) break;
+    const float am = amax32<XT>(raw[i]);
+    // Levels and rounding as in quantise_round.
+    const float inv = am > 0.f ? __fdividef(127.f * 256.f, am) : 0.f;
+    uint32_t hw[8], lw[8];
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const float2 p0 = pair32<XT>(raw[i], 2 * q), p1 = pair32<XT>(raw[i], 2 * q + 1);
+      if constexpr (SUMS) {
+        if (q < 4) s0 += (p0.x + p0.y) + (p1.x + p1.y);
+        else s1 += (p0.x + p0.y) + (p1.x + p1.y);
+      }
+      const uint32_t t0 = __float_as_uint(fmaf(p0.x, inv, 12582912.f + 128.f));
+      const uint32_t t1 = __float_as_uint(fmaf(p0.y, inv, 12582912.f + 128.f));
+      const uint32_t t2 = __float_as_uint(fmaf(p1.x, inv, 12582912.f + 128.f));
+      const uint32_t t3 = __float_as_uint(fmaf(p1.y, inv, 12582912.f + 128.f));
+      const uint32_t z01 = __byte_perm(t0, t1, 0x5140);
+      const uint32_t z23 = __byte_perm(t2, t3, 0x5140);
+      lw[q] = __byte_perm(z01, z23, 0x5410) ^ 0x80808080u;
+      hw[q] = __byte_perm(z01, z23, 0x7632);
+    }
+    uint4* qh = reinterpret_cast<uint4*>(xq + gg * 32);
+    uint4* ql = reinterpret_cast<uint4*>(xq + KS + gg * 32);
+    qh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    qh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    ql[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    ql[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+    xs[gg] = am * (1.f / (127.f * 256.f)) * MvDecode<T>::xgroup_scale(gg);
+    if constexpr (SUMS) *reinterpret_cast<float2*>(xsum + 2 * gg) = make_float2(s0, s1);
+  }
+}
+
 template <int T, int NB, bool SUMS, typename XT>
 __device__ void quantise_slice_t(const QmvArgs& a, int btile, int kb0, int w, int KS, int8_t* xq, float* xs,
                                  float* xsum) {
   constexpr int CH = sizeof(XT) == 4 ? 5 : 10;
   const int per_row = w * 32;  // 8-value chunks per activation row
   const int total = NB * per_row;
+  if constexpr (NB == 1 && sizeof(XT) == 2) {
+    if (a.xbulk) {  // the plan guarantees w * 8 <= QMV_XSTAGE_G * QMV_CTHREADS
+      quantise_staged<T, SUMS, XT>(w * (QK / 32), KS, xq, xs, xsum);
+      return;
+    }
+  }
   for (int base = 0; base < total; base += CH * QMV_CTHREADS)
     quantise_round<T, NB, SUMS, XT, CH>(a, btile, kb0, KS, per_row, total, base, xq, xs, xsum);
 }
@@ -437,6 +532,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   uint64_t* segb = empty + QMV_NS_MAX;                          // [RB] segment row sums posted by all consumers
   uint64_t* rfree = segb + QMV_RED_BUFS;                        // [RB] segment row sums read
   uint64_t* xready = rfree + QMV_RED_BUFS;                      // activations quantised
+  uint64_t* xcopy = xready + 1;                                  // bulk copy of the activations landed
   // B operand of the columns a lane does not feed: one block of zero
   // activations (offsets within a block stay below QK).
   int8_t* zeros = reinterpret_cast<int8_t*>(smem + G::TAB + 256);
@@ -467,6 +563,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
       mbar_init(&rfree[s], 1);
     }
     mbar_init(xready, 1);
+    mbar_init(xcopy, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -563,6 +660,18 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   // Everything above reads only weights and tables; from here on the kernel
   // reads activations / scratch that an earlier kernel in the stream writes.
   pdl_wait();
+  if (a.xbulk) {
+    // One bulk copy brings the slice of the activation row (16-bit values)
+    // into the level area; per-thread loads of the same bytes from every CTA
+    // at once queue on each SM's outstanding-miss limit.
+    if (threadIdx.x == 0) {
+      const uint32_t bytes = (uint32_t)w * QK * 2u;
+      mbar_arrive_expect_tx(xcopy, bytes);
+      bulk_g2s(xq_s, reinterpret_cast<const uint8_t*>(a.x) + ((int64_t)btile * a.K + (int64_t)kb0 * QK) * 2, bytes,
+               xcopy);
+    }
+    mbar_wait_bounded(xcopy, 0u, a.err);
+  }
   quantise_slice<T, NB, MV::BIAS>(a, btile, kb0, w, KS, xq_s, xs_s, xsum_s);
   named_sync_consumers();
   if (threadIdx.x == 0) mbar_arrive(xready);
@@ -957,6 +1066,12 @@ cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, in
   a.rowb = p.rowb;
   a.stage = p.stage;
   a.pre = p.pre;
+  // Bulk activation copy: one 16-bit row, 16-byte aligned, at most
+  // QMV_XSTAGE_G 32-groups per consumer thread.
+  a.xbulk = (rows == 1 && p.nb == 1 && (x_dtype == DT_F16 || x_dtype == DT_BF16) &&
+             (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && p.bps * (QK / 32) <= QMV_XSTAGE_G * QMV_CTHREADS)
+                ? 1
+                : 0;
   return qmv_launch(t, a, p, st);
 }
 
