@@ -103,6 +103,19 @@ template <> struct Fast<T_Q2_K> {
     S = h2f_bits(ld16a2(b + 80)) * (float)(sc & 15u);
     B = -h2f_bits(ld16a2(b + 82)) * (float)(sc >> 4);
   }
+  // Integer unit scale k and min m: S_u = D * k, B_u = DM * m (kscale, dscale);
+  // KINT: k times any dot product the matvec forms fits int32 (entries <= 192
+  // as fed: 16 * 192 * 2^15 * 15 < 2^31).
+  static constexpr bool KINT = true;
+  __device__ static void kscale(const uint8_t* b, int u, int& k, int& m) {
+    const uint32_t sc = b[u];
+    k = (int)(sc & 15u);
+    m = (int)(sc >> 4);
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    D = h2f_bits(ld16a2(b + 80));
+    DM = -h2f_bits(ld16a2(b + 82));
+  }
 };
 
 template <> struct Fast<T_Q4_K> {
@@ -129,6 +142,19 @@ template <> struct Fast<T_Q4_K> {
     S = h2f_bits(dm & 0xFFFFu) * (float)sc;
     B = -h2f_bits(dm >> 16) * (float)mn;
   }
+  static constexpr bool KINT = false;  // 32 * 240 * 2^15 * 63 > 2^31
+  __device__ static void kscale(const uint8_t* b, int g, int& k, int& m) {
+    const uint32_t q0 = ld32a4(b + 4), q1 = ld32a4(b + 8), q2 = ld32a4(b + 12);
+    const int sh = 8 * (g & 3);
+    const bool hi = g >= 4;
+    k = (int)(hi ? ((q2 >> sh) & 15u) | ((q0 >> (sh + 2)) & 48u) : (q0 >> sh) & 63u);
+    m = (int)(hi ? ((q2 >> (sh + 4)) & 15u) | ((q1 >> (sh + 2)) & 48u) : (q1 >> sh) & 63u);
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    const uint32_t dm = ld32a4(b);
+    D = h2f_bits(dm & 0xFFFFu);
+    DM = -h2f_bits(dm >> 16);
+  }
 };
 
 template <> struct Fast<T_Q6_K> {
@@ -147,6 +173,15 @@ template <> struct Fast<T_Q6_K> {
   __device__ static void affine(const uint8_t* b, int u, float& S, float& B) {
     S = h2f_bits(ld16a2(b + 208)) * (float)(int8_t)b[192 + u];
     B = -32.0f * S;
+  }
+  static constexpr bool KINT = false;  // 16 * 63 * 2^15 * 128 > 2^31
+  __device__ static void kscale(const uint8_t* b, int u, int& k, int& m) {
+    k = (int)(int8_t)b[192 + u];
+    m = k;
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    D = h2f_bits(ld16a2(b + 208));
+    DM = -32.0f * D;
   }
 };
 
@@ -180,6 +215,17 @@ template <> struct Fast<T_IQ4_XS> {
     S = h2f_bits(ld16a2(b)) * (float)((int)(l | (h << 4)) - 32);
     B = 0.f;
   }
+  static constexpr bool KINT = false;  // 32 * 127 * 2^15 * 32 > 2^31
+  __device__ static void kscale(const uint8_t* b, int g, int& k, int& m) {
+    const uint32_t l = (b[4 + (g >> 1)] >> (4 * (g & 1))) & 15u;
+    const uint32_t h = (ld16a2(b + 2) >> (2 * g)) & 3u;
+    k = (int)(l | (h << 4)) - 32;
+    m = 0;
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    D = h2f_bits(ld16a2(b));
+    DM = 0.f;
+  }
 };
 
 // --- IQ lookup types ------------------------------------------------------------
@@ -206,6 +252,15 @@ template <> struct Fast<T_IQ2_XXS> {
     S = h2f_bits(ld16a2(b)) * (0.5f + (float)(aux >> 28)) * 0.25f;
     B = 0.f;
   }
+  static constexpr bool KINT = true;  // 32 * 43 * 2^15 * 31 < 2^31
+  __device__ static void kscale(const uint8_t* b, int g, int& k, int& m) {
+    k = 2 * (int)(ld32a2(b + 2 + 8 * g + 4) >> 28) + 1;
+    m = 0;
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    D = h2f_bits(ld16a2(b)) * 0.125f;
+    DM = 0.f;
+  }
 };
 
 template <> struct Fast<T_IQ2_XS> {
@@ -228,6 +283,15 @@ template <> struct Fast<T_IQ2_XS> {
     const uint32_t sc = (b[66 + (s >> 1)] >> (4 * (s & 1))) & 15u;
     S = h2f_bits(ld16a2(b)) * (0.5f + (float)sc) * 0.25f;
     B = 0.f;
+  }
+  static constexpr bool KINT = true;  // 16 * 43 * 2^15 * 31 < 2^31
+  __device__ static void kscale(const uint8_t* b, int s, int& k, int& m) {
+    k = 2 * (int)((b[66 + (s >> 1)] >> (4 * (s & 1))) & 15u) + 1;
+    m = 0;
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    D = h2f_bits(ld16a2(b)) * 0.125f;
+    DM = 0.f;
   }
 };
 
@@ -253,6 +317,15 @@ template <> struct Fast<T_IQ2_S> {
     S = h2f_bits(ld16a2(b)) * (0.5f + (float)sc) * 0.25f;
     B = 0.f;
   }
+  static constexpr bool KINT = true;  // 16 * 43 * 2^15 * 31 < 2^31
+  __device__ static void kscale(const uint8_t* b, int s, int& k, int& m) {
+    k = 2 * (int)((b[74 + (s >> 1)] >> (4 * (s & 1))) & 15u) + 1;
+    m = 0;
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    D = h2f_bits(ld16a2(b)) * 0.125f;
+    DM = 0.f;
+  }
 };
 
 template <> struct Fast<T_IQ3_XXS> {
@@ -276,6 +349,15 @@ template <> struct Fast<T_IQ3_XXS> {
     const uint32_t aux = ld32a2(b + 66 + 4 * g);
     S = h2f_bits(ld16a2(b)) * (0.5f + (float)(aux >> 28)) * 0.5f;
     B = 0.f;
+  }
+  static constexpr bool KINT = true;  // 32 * 62 * 2^15 * 31 < 2^31 (grid values <= 62)
+  __device__ static void kscale(const uint8_t* b, int g, int& k, int& m) {
+    k = 2 * (int)(ld32a2(b + 66 + 4 * g) >> 28) + 1;
+    m = 0;
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    D = h2f_bits(ld16a2(b)) * 0.25f;
+    DM = 0.f;
   }
 };
 
@@ -301,6 +383,15 @@ template <> struct Fast<T_IQ3_S> {
     S = h2f_bits(ld16a2(b)) * (float)(1u + 2u * sc);
     B = 0.f;
   }
+  static constexpr bool KINT = true;  // 32 * 15 * 2^15 * 31 < 2^31
+  __device__ static void kscale(const uint8_t* b, int g, int& k, int& m) {
+    k = 1 + 2 * (int)((b[106 + (g >> 1)] >> (4 * (g & 1))) & 15u);
+    m = 0;
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    D = h2f_bits(ld16a2(b));
+    DM = 0.f;
+  }
 };
 
 template <> struct Fast<T_IQ1_S> {
@@ -317,6 +408,15 @@ template <> struct Fast<T_IQ1_S> {
     const uint32_t qh = ld16a2(b + 34 + 2 * g);
     S = h2f_bits(ld16a2(b)) * (float)(2u * ((qh >> 12) & 7u) + 1u) * 0.125f;
     B = 0.f;
+  }
+  static constexpr bool KINT = true;  // 32 * 9 * 2^15 * 15 < 2^31
+  __device__ static void kscale(const uint8_t* b, int g, int& k, int& m) {
+    k = 2 * (int)((ld16a2(b + 34 + 2 * g) >> 12) & 7u) + 1;
+    m = 0;
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    D = h2f_bits(ld16a2(b)) * 0.125f;
+    DM = 0.f;
   }
 };
 
@@ -338,6 +438,19 @@ template <> struct Fast<T_IQ1_M> {
     const uint32_t sc = (ws >> (3 * (s & 3))) & 7u;
     S = h2f_bits(dbits) * (float)(2u * sc + 1u) * 0.125f;
     B = 0.f;
+  }
+  static constexpr bool KINT = true;  // 16 * 9 * 2^15 * 15 < 2^31
+  __device__ static void kscale(const uint8_t* b, int s, int& k, int& m) {
+    const uint32_t ws = ld16a2(b + 48 + 2 * (s >> 2));
+    k = 2 * (int)((ws >> (3 * (s & 3))) & 7u) + 1;
+    m = 0;
+  }
+  __device__ static void dscale(const uint8_t* b, float& D, float& DM) {
+    const uint2 w = ld64a8(b + 48);
+    const uint32_t w0 = w.x & 0xFFFFu, w1 = w.x >> 16, w2 = w.y & 0xFFFFu, w3 = w.y >> 16;
+    const uint32_t dbits = ((w0 & 0xF000u) >> 12) | ((w1 & 0xF000u) >> 8) | ((w2 & 0xF000u) >> 4) | (w3 & 0xF000u);
+    D = h2f_bits(dbits) * 0.125f;
+    DM = 0.f;
   }
 };
 

@@ -81,14 +81,19 @@ struct Mv {
   template <int S, int NB>
   __device__ static void unit(const uint8_t* b, const Row<NB>&, int u, int C, int N, float xs, float xsum, float& A,
                               float& M) {
-    float sc, bias;
-    F::affine(b, u, sc, bias);
+    int k, m;
+    F::kscale(b, u, k, m);
     const int c = SPLIT ? C - 2 * N : C;
-    A = fmaf(sc * xs, (float)c, A);
-    if constexpr (BIAS) M = fmaf(bias, xsum, M);
+    if constexpr (F::KINT) A = fmaf(xs, (float)(k * c), A);
+    else A = fmaf(xs * (float)k, (float)c, A);
+    if constexpr (BIAS) M = fmaf((float)m, xsum, M);
   }
   template <int NB>
-  __device__ static float finish(const uint8_t*, const Row<NB>&, float A, float M) { return A + M; }
+  __device__ static float finish(const uint8_t* b, const Row<NB>&, float A, float M) {
+    float D, DM;
+    F::dscale(b, D, DM);
+    return BIAS ? fmaf(D, A, DM * M) : D * A;
+  }
 };
 
 // IQ2_XXS: units of 32 weights, 8 bytes each at 2 + 8u: four grid indices

@@ -766,6 +766,8 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
         const int8_t* xb = xrow_o + kk;
         const float* xsb = xs_row + (kk >> 5);
         const float* xub = xsum_row + (kk >> 4);
+        // Block accumulators in units of the block scales (dscale).
+        float A0 = 0.f, A1 = 0.f, M0 = 0.f, M1 = 0.f;
 #pragma unroll
         for (int set = 0; set < SETS; set++) {
           const int kset = set * KSET;
@@ -833,17 +835,32 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
           const int unit = set * UPS + s_ep;
           const int ku = unit * UNIT;  // within the block
           const float xsv = xsb[ku >> 5];
-          float S0, B0, S1, B1;
-          FO::affine(b0, unit, S0, B0);
-          FO::affine(b1, unit, S1, B1);
-          acc0 = fmaf(S0, (float)(Cc[0] * 256 + Cc[1]) * xsv, acc0);
-          acc1 = fmaf(S1, (float)(Cc[2] * 256 + Cc[3]) * xsv, acc1);
+          int k0, m0, k1, m1;
+          FO::kscale(b0, unit, k0, m0);
+          FO::kscale(b1, unit, k1, m1);
+          const int c0 = Cc[0] * 256 + Cc[1], c1 = Cc[2] * 256 + Cc[3];
+          if constexpr (FO::KINT) {
+            A0 = fmaf(xsv, (float)(k0 * c0), A0);
+            A1 = fmaf(xsv, (float)(k1 * c1), A1);
+          } else {
+            A0 = fmaf(xsv * (float)k0, (float)c0, A0);
+            A1 = fmaf(xsv * (float)k1, (float)c1, A1);
+          }
           if constexpr (FO::HAS_BIAS) {
             float xu = xub[ku >> 4];
             if constexpr (UNIT == 32) xu += xub[(ku >> 4) + 1];
-            acc0 = fmaf(B0, xu, acc0);
-            acc1 = fmaf(B1, xu, acc1);
+            M0 = fmaf((float)m0, xu, M0);
+            M1 = fmaf((float)m1, xu, M1);
           }
+        }
+        float D0, DM0, D1, DM1;
+        FO::dscale(b0, D0, DM0);
+        FO::dscale(b1, D1, DM1);
+        acc0 = fmaf(D0, A0, acc0);
+        acc1 = fmaf(D1, A1, acc1);
+        if constexpr (FO::HAS_BIAS) {
+          acc0 = fmaf(DM0, M0, acc0);
+          acc1 = fmaf(DM1, M1, acc1);
         }
       }
     }
