@@ -194,6 +194,7 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
+        from gsq_b200.parallel import GatherRegion, quantized_matvec_gather
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     pk = peaks()
 
@@ -207,19 +208,25 @@ def main():
             shard = full[rank * rows * rb:(rank + 1) * rows * rb].clone()
             del full
             x = torch.randn(1, k, device=dev, dtype=torch.float16, generator=torch.Generator(device=dev).manual_seed(ti))
-            y = torch.empty(1, rows, device=dev, dtype=torch.float32)
-            yfull = torch.empty(world, rows, device=dev, dtype=torch.float32)
-            cfgs.append(dict(q=q, n=n, k=k, rows=rows, packed=shard, x=x, y=y, yfull=yfull,
+            # Ranks > 1: the gathered output of every configuration lives in
+            # its own region (the gather is fused into the matvec kernel).
+            region = GatherRegion(1, n) if world > 1 else None
+            cfgs.append(dict(q=q, n=n, k=k, rows=rows, packed=shard, x=x, region=region,
                              bytes=packed_bytes(q, n, k), alg=packed_bytes(q, rows, k) + 2 * k + 4 * rows))
     step_bytes = sum(c["bytes"] for c in cfgs)
     torch.cuda.synchronize()
 
+    def matvec(c, x):
+        """One projection: y, or (ranks > 1) every rank's rows gathered in c's region."""
+        if world > 1:
+            return quantized_matvec_gather(x, c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
+                                           region=c["region"], row0=rank * c["rows"])
+        return quantized_matvec(x, c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
+                                out_dtype=torch.float32)
+
     def step():
         for c in cfgs:
-            out = quantized_matvec(c["x"], c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
-                                   out_dtype=torch.float32)
-            if world > 1:
-                dist.all_gather_into_tensor(c["yfull"], out)
+            matvec(c, c["x"])
 
     # warm up eagerly (allocates workspaces, sets kernel attributes), then capture
     for _ in range(2):
@@ -316,13 +323,7 @@ def main():
     d2h = sum(c["rows"] * world * 4 for c in cfgs)
     for _ in range(2):
         for c, hx in zip(cfgs, host_x):
-            xd = hx.to(dev, non_blocking=True)
-            out = quantized_matvec(xd, c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
-                                   out_dtype=torch.float32)
-            if world > 1:
-                dist.all_gather_into_tensor(c["yfull"], out)
-                out = c["yfull"]
-            out.cpu()
+            matvec(c, hx.to(dev, non_blocking=True)).cpu()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -332,13 +333,7 @@ def main():
     t0.record()
     for _ in range(e2e_steps):
         for c, hx in zip(cfgs, host_x):
-            xd = hx.to(dev, non_blocking=True)
-            out = quantized_matvec(xd, c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
-                                   out_dtype=torch.float32)
-            if world > 1:
-                dist.all_gather_into_tensor(c["yfull"], out)
-                out = c["yfull"]
-            out.cpu()
+            matvec(c, hx.to(dev, non_blocking=True)).cpu()
     t1.record()
     torch.cuda.synchronize()
     e2e_ms = t0.elapsed_time(t1)
@@ -409,7 +404,8 @@ def main():
             "data": "synthetic",
             "config": {"workload": "config-2 QMV sweep: 11 types x {5120->5120, 5120->17408, 17408->5120}, batch 1",
                        "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (886 MB per step)",
-                       "parallelism": f"tp{world} (output rows, NCCL all-gather)" if world > 1 else "single GPU",
+                       "parallelism": (f"tp{world} (output rows; the gather is fused into the matvec: NVLink "
+                                       f"stores into every rank's output, flag exchange)") if world > 1 else "single GPU",
                        "timing": "CUDA graph of one step, replayed; CUDA events"},
             "roofline": roofline, "qmv_sweep": per, "qmm_prefill": qmm, "cpu_baseline": cpu, "e2e": e2e,
             "clocks": clocks.summary(), "gpu_launches": args.steps * len(cfgs),
@@ -417,6 +413,8 @@ def main():
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
+        for c in cfgs:
+            c["region"].close()
         dist.barrier()
         dist.destroy_process_group()
 

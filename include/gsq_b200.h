@@ -114,6 +114,36 @@ GSQ_API int gsq_embed(int qtype, const int32_t* ids, int64_t T, const uint8_t* p
 GSQ_API int gsq_qmv_noalloc(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
                             int64_t rows, void* y, int y_dtype, gsq_stream_t stream);
 
+/* ---- Row-parallel decode with the gather fused into the matvec ----------
+ * No reference counterpart: the reference runs on one device (its only
+ * trace of parallelism is mlx-lm's unexercised all_sum hook,
+ * mlx_gsq/models/qwen35.py:104-105).  Each rank of a row split holds one
+ * gather region per projection call site: 256 bytes of control words, the
+ * gathered output (fp32 rows x ntot, at byte 256), then an inbox the peers
+ * write.  Regions are exchanged between the ranks' processes with CUDA IPC
+ * handles. */
+GSQ_API size_t gsq_gather_region_bytes(int64_t rows, int64_t ntot);
+/* Device allocation of `bytes` (>= 256), zero-filled; 256-byte aligned. */
+GSQ_API int gsq_gather_region_alloc(size_t bytes, void** region);
+GSQ_API int gsq_gather_region_free(void* region);
+/* 64-byte CUDA IPC handle of a region, and its mapping in another process. */
+GSQ_API int gsq_ipc_export(void* region, uint8_t handle[64]);
+GSQ_API int gsq_ipc_import(const uint8_t handle[64], void** peer);
+GSQ_API int gsq_ipc_close(void* peer);
+
+/* gsq_qmv for rank `rank` of `world` (2..8) holding output rows
+ * [row0, row0 + N) of ntot: the kernel sends its rows into every rank's
+ * region (regions[i] = rank i's region, mapped in this process) over NVLink
+ * and ends with the exchange of the rows through the regions' inboxes, so
+ * that once the call has completed on `stream` every rank's region holds all
+ * ntot rows of this call.  Every rank must make the same sequence of calls on a region; a
+ * region must serve one call site (its rows stay valid until that site runs
+ * again).  The flag wait is bounded: a rank that never arrives makes the
+ * others return with gsq_device_status() == 1.  Output is fp32. */
+GSQ_API int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
+                           int64_t rows, void* const* regions, int world, int rank, int64_t row0, int64_t ntot,
+                           void* workspace, size_t workspace_bytes, gsq_stream_t stream);
+
 /* Synchronises `stream`, then returns and clears the device error word the
  * kernels of the current device write (0 = none; 1 = a bounded wait expired;
  * 2 = an embedding id was out of range).  No reference counterpart: the

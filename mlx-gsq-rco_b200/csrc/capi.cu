@@ -122,6 +122,84 @@ int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_
   return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_qmv launch");
 }
 
+size_t gsq_gather_region_bytes(int64_t rows, int64_t ntot) {
+  if (rows <= 0 || ntot <= 0) return 0;
+  return qmv_gather_region_bytes(rows, ntot);
+}
+
+int gsq_gather_region_alloc(size_t bytes, void** region) {
+  if (!region || bytes < 256) return fail(GSQ_ERR_ARG, "region pointer missing or size below the 256-byte header");
+  *region = nullptr;
+  cudaError_t e = cudaMalloc(region, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "gsq_gather_region_alloc");
+  e = cudaMemset(*region, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(*region);
+    *region = nullptr;
+    return cuda_fail(e, "gsq_gather_region_alloc (zero fill)");
+  }
+  return GSQ_OK;
+}
+
+int gsq_gather_region_free(void* region) {
+  if (!region) return GSQ_OK;
+  cudaError_t e = cudaFree(region);
+  return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_gather_region_free");
+}
+
+int gsq_ipc_export(void* region, uint8_t handle[64]) {
+  if (!region || !handle) return fail(GSQ_ERR_ARG, "null region or handle");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, region);
+  if (e != cudaSuccess) return cuda_fail(e, "gsq_ipc_export");
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  memcpy(handle, &h, 64);
+  return GSQ_OK;
+}
+
+int gsq_ipc_import(const uint8_t handle[64], void** peer) {
+  if (!handle || !peer) return fail(GSQ_ERR_ARG, "null handle or output pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, 64);
+  *peer = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(peer, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_ipc_import");
+}
+
+int gsq_ipc_close(void* peer) {
+  if (!peer) return GSQ_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(peer);
+  return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_ipc_close");
+}
+
+int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
+                   int64_t rows, void* const* regions, int world, int rank, int64_t row0, int64_t ntot,
+                   void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
+  int rc = check_matrix(qtype, packed, N, K);
+  if (rc) return rc;
+  if (world < 2 || world > 8 || rank < 0 || rank >= world) return fail(GSQ_ERR_ARG, "world must be 2..8 and rank < world");
+  if (!regions) return fail(GSQ_ERR_ARG, "null region list");
+  for (int i = 0; i < world; i++)
+    if (!regions[i] || !aligned(regions[i], 256)) return fail(GSQ_ERR_ALIGN, "region %d missing or not 256-byte aligned", i);
+  if (rows <= 0 || rows > (1 << 20)) return fail(GSQ_ERR_SIZE, "invalid row count %lld", (long long)rows);
+  if (row0 < 0 || N <= 0 || row0 + N > ntot) return fail(GSQ_ERR_SIZE, "rows [%lld, %lld) outside the %lld gathered rows",
+                                                         (long long)row0, (long long)(row0 + N), (long long)ntot);
+  if (!x) return fail(GSQ_ERR_ARG, "null x");
+  if (!dtype_ok(x_dtype)) return fail(GSQ_ERR_ARG, "unsupported dtype");
+  if (!aligned(x, 16)) return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned");
+  const QmvPlan p = qmv_plan(qtype, N, K, (int)rows);
+  if (p.ctas <= 0)
+    return fail(GSQ_ERR_SIZE, "matrix too large for the matvec (N=%lld, K=%lld)", (long long)N, (long long)K);
+  if (p.workspace > 0 && (!workspace || workspace_bytes < p.workspace || !aligned(workspace, 256)))
+    return fail(GSQ_ERR_WORKSPACE, "gsq_qmv_gather needs %zu workspace bytes (256-byte aligned), got %zu",
+                p.workspace, workspace_bytes);
+  const QmvGather g = {regions, world, rank, row0, ntot};
+  uint8_t* own_y = static_cast<uint8_t*>(regions[rank]) + 256;
+  cudaError_t e = qmv_run(qtype, x, x_dtype, packed, N, K, (int)rows, own_y, DT_F32, workspace, p,
+                          device_error_word(), (cudaStream_t)stream, &g);
+  return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_qmv_gather launch");
+}
+
 size_t gsq_qmm_workspace_size(int qtype, int64_t N, int64_t K, int64_t M, int x_dtype) {
   if (!supported(qtype) || M <= 0 || N <= 0 || K <= 0 || K % QK) return 0;
   return qmm_workspace_bytes(qtype, N, K, M, x_dtype);

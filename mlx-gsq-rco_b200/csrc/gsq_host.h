@@ -50,8 +50,19 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows);
 
 // Runs QMV with `ws` as scratch (must hold plan.workspace bytes, zero-filled
 // tickets; left zero-filled on completion).
+// Fused row gather of a rank's output rows into every rank's region (see
+// gsq_qmv_gather); regions[i] is rank i's region, mapped in this process.
+struct QmvGather {
+  void* const* regions;
+  int world, rank;
+  int64_t row0, ntot;
+};
+
 cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int rows,
-                    void* y, int y_dtype, void* ws, const QmvPlan& p, int* err, cudaStream_t st);
+                    void* y, int y_dtype, void* ws, const QmvPlan& p, int* err, cudaStream_t st,
+                    const QmvGather* gather = nullptr);
+size_t qmv_gather_inbox_offset(int64_t rows, int64_t ntot);
+size_t qmv_gather_region_bytes(int64_t rows, int64_t ntot);
 
 cudaError_t dequant_launch(int t, const uint8_t* packed, int64_t nblocks, float* out, cudaStream_t st);
 cudaError_t embed_launch(int t, const int32_t* ids, int64_t n, const uint8_t* packed, int64_t vocab, int64_t dim,

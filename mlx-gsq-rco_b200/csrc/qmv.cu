@@ -57,6 +57,13 @@ constexpr int QMV_RED_BYTES = QMV_RED_BUFS * QMV_CWARPS * 32 * 4;
 // the partial sums of multi-slice plans.  Nothing else is ever written over
 // the fixed region, so one zero-filled workspace serves calls of any shape.
 constexpr int QMV_TICKET_SLOTS = 65536;
+// Gather regions (fused row gather): 64 words of which the last two are the
+// owner's CTA ticket and call count, then fp32 y [rows][ntot], then an
+// inbox of two [rows][ntot] arrays of {value, call count} 8-byte pairs that
+// the peers write (slot = call count & 1).
+constexpr int QMV_GATHER_MAX = 8;
+constexpr int QMV_GFLAG_TICKET = 62, QMV_GFLAG_COUNT = 63;
+constexpr size_t QMV_GATHER_HEADER = 64 * sizeof(unsigned);
 constexpr size_t QMV_TICKET_BYTES = QMV_TICKET_SLOTS * sizeof(unsigned);
 
 struct QmvArgs {
@@ -73,7 +80,98 @@ struct QmvArgs {
   int cb, rowb, stage;  // ring geometry: blocks per stage, staged row stride, stage bytes
   int pre;              // stages issued before the activations are quantised (<= ns)
   int xbulk;            // one 16-bit activation row, copied into shared memory in bulk
+  // Fused row gather (world > 1): output rows [row0, row0 + N) of ntot are
+  // stored into every rank's gather region (fp32, [rows][ntot]) over
+  // NVLink, and the regions' flag words synchronise the ranks at the end.
+  float* gy[QMV_GATHER_MAX];
+  unsigned* gflags[QMV_GATHER_MAX];
+  uint2* ginbox[QMV_GATHER_MAX];
+  int world, rank;
+  int64_t row0, ntot;
 };
+
+// 8-byte {value, call count} pairs: one single-copy-atomic access each.
+__device__ __forceinline__ void st_pair_sys(uint2* p, float v, unsigned ep) {
+  const unsigned long long w = ((unsigned long long)ep << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_pair_sys(const uint2* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+// Store one output value: y, or (gathering) this rank's own region and, as
+// a {value, call count} pair, every peer's inbox slot for call count ep.
+__device__ __forceinline__ void store_y(const QmvArgs& a, int batch, int64_t rr, float v, unsigned ep) {
+  if (a.world <= 1) {
+    store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, v);
+    return;
+  }
+  const int64_t off = (int64_t)batch * a.ntot + a.row0 + rr;
+  a.gy[a.rank][off] = v;
+  const int64_t slot = (int64_t)(ep & 1u) * a.rows * a.ntot;
+#pragma unroll
+  for (int p = 0; p < QMV_GATHER_MAX; p++)
+    if (p < a.world && p != a.rank) st_pair_sys(a.ginbox[p] + slot + off, v, ep);
+}
+
+// Call count of this call on the gather region (read after griddepcontrol.wait:
+// the previous call on the region may be the kernel just before).
+__device__ __forceinline__ unsigned gather_count(const QmvArgs& a) {
+  return a.world > 1 ? a.gflags[a.rank][QMV_GFLAG_COUNT] + 1u : 0u;
+}
+
+// End of a gathering call, run by the consumer and combiner threads of every
+// CTA after their last store.  Every output value already went to the
+// peers' inboxes as a {value, call count} pair when it was stored (8-byte
+// stores over NVLink, no fences: each pair carries its own readiness).
+// Here the CTA takes its share of the other ranks' values of this call from
+// its own inbox into y -- about one value per thread, spread over all CTAs --
+// waiting (bounded) until each pair's call count is this call's.  The kernel
+// completes only when every share is in, i.e. every rank's rows of this call
+// are in every rank's y.  The last CTA to finish (gpu-scope ticket) records
+// the call count.  The inbox slot alternates with the call count; a rank
+// cannot finish a call before every peer has computed its rows of that call,
+// and it sends the next call's rows only after this call's kernel completed,
+// so a peer is never two calls ahead in one slot.  Every rank must make the
+// same sequence of calls on a region.
+__device__ void gather_finish(const QmvArgs& a, unsigned ep) {
+  constexpr int NT = QMV_CTHREADS + 32;  // consumer and combiner threads
+  const int t = threadIdx.x < QMV_CTHREADS ? threadIdx.x : threadIdx.x - 32;  // skip the producer warp
+  const int64_t cta = (int64_t)blockIdx.x + (int64_t)gridDim.x * ((int64_t)blockIdx.y + (int64_t)gridDim.y * blockIdx.z);
+  const int64_t nthreads = (int64_t)gridDim.x * gridDim.y * gridDim.z * NT;
+  const int64_t total = (int64_t)a.rows * a.ntot;
+  const uint2* in = a.ginbox[a.rank] + (int64_t)(ep & 1u) * total;
+  float* y = a.gy[a.rank];
+  const long long t0 = clock64();
+  bool late = false;  // a timed-out thread still reaches the barrier below
+  for (int64_t i = cta * NT + t; i < total && !late; i += nthreads) {
+    const int64_t col = i % a.ntot;
+    if (col >= a.row0 && col < a.row0 + a.N) continue;  // this rank's own rows
+    unsigned long long w = ld_pair_sys(in + i);
+    while ((unsigned)(w >> 32) != ep) {
+      if (clock64() - t0 > (1ll << 31)) {
+        atomicExch(a.err, DEV_WAIT_TIMEOUT);
+        late = true;
+        break;
+      }
+      __nanosleep(32);
+      w = ld_pair_sys(in + i);
+    }
+    if (!late) y[i] = __uint_as_float((unsigned)w);
+  }
+  asm volatile("bar.sync 2, %0;" ::"n"(NT) : "memory");
+  if (threadIdx.x == 0) {
+    unsigned* own = a.gflags[a.rank];
+    __threadfence();
+    const unsigned ctas = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(own + QMV_GFLAG_TICKET, 1u) == ctas - 1u) {
+      own[QMV_GFLAG_TICKET] = 0u;
+      own[QMV_GFLAG_COUNT] = ep;
+    }
+  }
+}
 
 // Staged row stride for cb blocks: the copied bytes plus head/tail 16-byte
 // rounding, padded to an odd number of 16-byte units so that the 8 rows a
@@ -427,7 +525,8 @@ __device__ void publish_piece(const QmvArgs& a, int btile, int C, int c, float v
 }
 
 template <int NB>
-__device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t U, int w, int64_t tile, float v) {
+__device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t U, int w, int64_t tile, float v,
+                              unsigned ep) {
   const int lane = threadIdx.x & 31;
   if (lane >= NB * 16) return;
   const int64_t c0 = ((tile * w + 1) * C - 1) / U;  // first CTA touching the tile
@@ -453,7 +552,7 @@ __device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t
   const int b = lane >> 4, r = lane & 15;
   const int batch = btile * NB + b;
   const int64_t rr = tile * 16 + r;
-  if (batch < a.rows && rr < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, sum);
+  if (batch < a.rows && rr < a.N) store_y(a, batch, rr, sum, ep);
 }
 
 // Global combination of one piece of a tile shared with other CTAs (other
@@ -463,7 +562,7 @@ __device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t
 // is this piece's row sum (lane = b*16 + r).
 template <int NB>
 __device__ void combine_piece(const QmvArgs& a, int btile, int slice, int C, int c, int w, int64_t tile,
-                              int64_t first_tile, int seg_len, float v) {
+                              int64_t first_tile, int seg_len, float v, unsigned ep) {
   const int lane = threadIdx.x & 31;
   float* pp;
   if (seg_len == w)
@@ -506,7 +605,7 @@ __device__ void combine_piece(const QmvArgs& a, int btile, int slice, int C, int
     const int b = lane >> 4, r = lane & 15;
     const int batch = btile * NB + b;
     const int64_t rr = tile * 16 + r;
-    if (batch < a.rows && rr < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, sum);
+    if (batch < a.rows && rr < a.N) store_y(a, batch, rr, sum, ep);
   }
   if (lane == 0) *tk = 0u;
 }
@@ -623,6 +722,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     // takes over every piece that needs other CTAs' pieces, so that the
     // tensor-core warps never wait on global-memory round trips.
     pdl_wait();  // before any global write
+    const unsigned gep = gather_count(a);
     QmvCursor cur(ub, ue, w);
     const int64_t first_tile = cur.t0;
     int rbuf = 0;
@@ -643,14 +743,15 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&rfree[rbuf]);
         if (a.slices > 1)
-          combine_piece<NB>(a, btile, slice, C, c, w, tile, first_tile, seg_len, v);
+          combine_piece<NB>(a, btile, slice, C, c, w, tile, first_tile, seg_len, v, gep);
         else if (sb + seg_len < w)
           publish_piece<NB>(a, btile, C, c, v);  // later CTAs hold the rest of this tile
         else
-          gather_pieces<NB>(a, btile, C, c, U, w, tile, v);
+          gather_pieces<NB>(a, btile, C, c, U, w, tile, v, gep);
       }
       if (++rbuf == RB) { rbuf = 0; rph ^= 1u; }
     }
+    if (a.world > 1) gather_finish(a, gep);
     return;
   }
 
@@ -673,6 +774,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     mbar_wait_bounded(xcopy, 0u, a.err);
   }
   quantise_slice<T, NB, MV::BIAS>(a, btile, kb0, w, KS, xq_s, xs_s, xsum_s);
+  const unsigned gep = gather_count(a);
   named_sync_consumers();
   if (threadIdx.x == 0) mbar_arrive(xready);
 
@@ -900,7 +1002,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
         const int b = lane >> 4, r = lane & 15;
         const int batch = btile * NB + b;
         const int64_t rr = tile * 16 + r;
-        if (lane < NB * 16 && batch < a.rows && rr < a.N) store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, v);
+        if (lane < NB * 16 && batch < a.rows && rr < a.N) store_y(a, batch, rr, v, gep);
       }
       if (++rbuf == RB) { rbuf = 0; rph ^= 1u; }
       seg_no++;
@@ -908,6 +1010,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
       seg_len = 0;
     }
   }
+  if (a.world > 1) gather_finish(a, gep);
 }
 
 // --------------------------------------------------------------------------
@@ -1053,8 +1156,17 @@ static cudaError_t qmv_launch(int t, const QmvArgs& a, const QmvPlan& p, cudaStr
   return cudaErrorInvalidValue;
 }
 
+size_t qmv_gather_inbox_offset(int64_t rows, int64_t ntot) {
+  return (QMV_GATHER_HEADER + (size_t)rows * ntot * sizeof(float) + 15) / 16 * 16;
+}
+
+size_t qmv_gather_region_bytes(int64_t rows, int64_t ntot) {
+  return qmv_gather_inbox_offset(rows, ntot) + 2 * (size_t)rows * ntot * sizeof(uint2);
+}
+
 cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int rows,
-                    void* y, int y_dtype, void* ws, const QmvPlan& p, int* err, cudaStream_t st) {
+                    void* y, int y_dtype, void* ws, const QmvPlan& p, int* err, cudaStream_t st,
+                    const QmvGather* gather) {
   if (p.ctas <= 0) return cudaErrorInvalidValue;
   uint8_t* w = static_cast<uint8_t*>(ws);
   QmvArgs a;
@@ -1083,6 +1195,29 @@ cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, in
   a.rowb = p.rowb;
   a.stage = p.stage;
   a.pre = p.pre;
+  a.world = 0;
+  a.rank = 0;
+  a.row0 = 0;
+  a.ntot = N;
+  for (int i = 0; i < QMV_GATHER_MAX; i++) {
+    a.gy[i] = nullptr;
+    a.gflags[i] = nullptr;
+    a.ginbox[i] = nullptr;
+  }
+  if (gather && gather->world > 1) {
+    if (gather->world > QMV_GATHER_MAX || gather->rank < 0 || gather->rank >= gather->world)
+      return cudaErrorInvalidValue;
+    a.world = gather->world;
+    a.rank = gather->rank;
+    a.row0 = gather->row0;
+    a.ntot = gather->ntot;
+    for (int i = 0; i < gather->world; i++) {
+      uint8_t* r = static_cast<uint8_t*>(gather->regions[i]);
+      a.gflags[i] = reinterpret_cast<unsigned*>(r);
+      a.gy[i] = reinterpret_cast<float*>(r + QMV_GATHER_HEADER);
+      a.ginbox[i] = reinterpret_cast<uint2*>(r + qmv_gather_inbox_offset(rows, gather->ntot));
+    }
+  }
   // Bulk activation copy: one 16-bit row, 16-byte aligned, at most
   // QMV_XSTAGE_G 32-groups per consumer thread.
   a.xbulk = (rows == 1 && p.nb == 1 && (x_dtype == DT_F16 || x_dtype == DT_BF16) &&

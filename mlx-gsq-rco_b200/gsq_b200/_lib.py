@@ -39,6 +39,13 @@ SIGNATURES = {
     "gsq_embed": (_I, [_I, _P, _I64, _P, _I64, _I64, _P, _I, _P]),
     "gsq_device_status": (_I, [_P]),
     "gsq_qmv_noalloc": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, _P, _I, _P]),
+    "gsq_gather_region_bytes": (_SZ, [_I64, _I64]),
+    "gsq_gather_region_alloc": (_I, [_SZ, ctypes.POINTER(_P)]),
+    "gsq_gather_region_free": (_I, [_P]),
+    "gsq_ipc_export": (_I, [_P, ctypes.c_char_p]),
+    "gsq_ipc_import": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "gsq_ipc_close": (_I, [_P]),
+    "gsq_qmv_gather": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _I, _I, _I64, _I64, _P, _SZ, _P]),
 }
 
 _lib = None

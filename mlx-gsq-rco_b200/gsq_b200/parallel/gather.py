@@ -1,0 +1,115 @@
+"""Row-parallel decode with the gather fused into the matvec.
+
+``RowParallelLinear`` joins the ranks' output slices with an NCCL all-gather
+after the local kernel, one collective (about 10 us of latency) per
+projection.  For decode rows the matvec kernel can instead store each output
+row straight into every rank's copy of the output over NVLink and finish
+with a flag exchange (``gsq_qmv_gather`` in ``include/gsq_b200.h``): one
+kernel per projection, no collective launch.
+
+A :class:`GatherRegion` is the per-call-site buffer behind it: every rank
+allocates ``gsq_gather_region_bytes(rows, ntot)`` bytes (256 bytes of flag
+words, then fp32 ``rows x ntot``), exports a CUDA IPC handle, and maps its
+peers' regions.  Every rank must make the same sequence of calls on a
+region, and a region serves one call site: its rows stay valid until the
+same site runs again.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from .. import _lib
+from ..quant.layouts import type_id as _type_id
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ view of library-owned device memory."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...]):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class GatherRegion:
+    """One projection call site's gathered output on every rank of ``group``.
+
+    ``y`` is this rank's copy, a ``rows x ntot`` fp32 tensor (a view of the
+    region; ``gsq_qmv_gather`` fills all of it).
+    """
+
+    def __init__(self, rows: int, ntot: int, group=None, device: torch.device | None = None):
+        if not dist.is_initialized():
+            raise RuntimeError("GatherRegion needs an initialised process group")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 2 <= self.world <= 8:
+            raise ValueError("the fused gather supports 2 to 8 ranks")
+        self.rows, self.ntot = int(rows), int(ntot)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.load()
+        nbytes = lib.gsq_gather_region_bytes(self.rows, self.ntot)
+        if nbytes == 0:
+            raise ValueError("empty gather region")
+        with torch.cuda.device(self.device):
+            own = ctypes.c_void_p()
+            _lib.check(lib.gsq_gather_region_alloc(nbytes, ctypes.byref(own)))
+            self._own = own.value
+            handle = ctypes.create_string_buffer(64)
+            _lib.check(lib.gsq_ipc_export(own, handle))
+            handles: list = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle.raw), group=group)
+            ptrs, self._imported = [], []
+            for i, h in enumerate(handles):
+                if i == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                peer = ctypes.c_void_p()
+                _lib.check(lib.gsq_ipc_import(h, ctypes.byref(peer)))
+                ptrs.append(peer.value)
+                self._imported.append(peer.value)
+        self.regions = (ctypes.c_void_p * self.world)(*ptrs)
+        self.y = torch.as_tensor(_DeviceArray(self._own + 256, (self.rows, self.ntot)), device=self.device)
+
+    def close(self) -> None:
+        """Unmap the peers' regions and free this rank's (collective: every rank calls it)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no peer still writes into this rank's region
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            for p in self._imported:
+                _lib.check(lib.gsq_ipc_close(ctypes.c_void_p(p)))
+            dist.barrier(group=self.group)
+            _lib.check(lib.gsq_gather_region_free(ctypes.c_void_p(self._own)))
+        self._own, self._imported = None, []
+
+
+def quantized_matvec_gather(x: torch.Tensor, packed_shard: torch.Tensor, *, qtype: str, out_features: int,
+                            in_features: int, region: GatherRegion, row0: int) -> torch.Tensor:
+    """y = x @ deq(W).T for this rank's rows [row0, row0 + out_features) of a
+    row-split projection, gathered: returns the region's ``rows x ntot`` fp32
+    output, which holds every rank's rows once the call completes on the
+    current stream."""
+    tid = _type_id(qtype)
+    dev = _lib.require_cuda(x, packed_shard)
+    rows = x.numel() // in_features
+    if rows != region.rows:
+        raise ValueError(f"x has {rows} rows, the region {region.rows}")
+    flat = x.reshape(rows, in_features).contiguous()
+    if flat.data_ptr() % 16:
+        flat = flat.clone()
+    pk = packed_shard.reshape(-1).contiguous()
+    lib = _lib.load()
+    need = lib.gsq_qmv_workspace_size(tid, out_features, in_features, rows)
+    ws = _lib.workspaces.get(dev, need, "qmv")
+    code = lib.gsq_qmv_gather(tid, flat.data_ptr(), _lib.DTYPE_CODES[flat.dtype], pk.data_ptr(), out_features,
+                              in_features, rows, region.regions, region.world, region.rank, row0, region.ntot,
+                              ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                              _lib.stream_ptr(dev))
+    _lib.check(code)
+    return region.y

@@ -76,11 +76,15 @@ class RowParallelLinear(torch.nn.Module):
     """A packed projection split by output rows across the ranks of ``group``.
 
     ``forward(x)`` runs the local shard with the fused kernels (GSQLinear
-    dispatch: matvec for one row, tiled matmul otherwise) and all-gathers
-    the output slices, so every rank returns the full ``(..., out_features)``.
+    dispatch: matvec for few rows, tiled matmul otherwise) and joins the
+    output slices, so every rank returns the full ``(..., out_features)``.
+    Decode-sized inputs on CUDA (``fused_gather``) use the matvec with the
+    gather fused in (one kernel, NVLink stores into every rank's copy, see
+    ``gather.py``); other inputs use an NCCL all-gather after the kernel.
     """
 
-    def __init__(self, weight: PackedWeight, group=None, bias: torch.Tensor | None = None, local_fn=None):
+    def __init__(self, weight: PackedWeight, group=None, bias: torch.Tensor | None = None, local_fn=None,
+                 fused_gather: bool = True):
         super().__init__()
         from ..nn.linear import GSQLinear
         self.group = group
@@ -89,9 +93,34 @@ class RowParallelLinear(torch.nn.Module):
         self.world, self.rank = world, rank
         self.out_features, self.in_features = weight.logical_shape
         self.shard = shard_weight(weight, world, rank) if world > 1 else weight
+        self.row0 = shard_bounds(self.out_features, world, rank)[0] if world > 1 else 0
         self.bias = bias
         self.local = local_fn or GSQLinear(self.shard)
+        self.fused_gather = fused_gather and local_fn is None and 2 <= world <= 8
+        self._regions: dict[int, object] = {}
+
+    def _gathered_matvec(self, x: torch.Tensor) -> torch.Tensor:
+        from .gather import GatherRegion, quantized_matvec_gather
+        rows = x.numel() // self.in_features
+        region = self._regions.get(rows)
+        if region is None:
+            region = self._regions[rows] = GatherRegion(rows, self.out_features, self.group, x.device)
+        y = quantized_matvec_gather(x, self.shard.data, qtype=self.shard.quantization_type,
+                                    out_features=self.out_features // self.world, in_features=self.in_features,
+                                    region=region, row0=self.row0)
+        y = y.reshape(*x.shape[:-1], self.out_features)
+        return y if x.dtype == torch.float32 else y.to(x.dtype)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        y = gather_rows(self.local(x), self.group) if self.world > 1 else self.local(x)
+        from ..runtime.kernels.qmv import QMM_MIN_ROWS
+        if self.world > 1 and self.fused_gather and x.is_cuda and x.numel() // self.in_features < QMM_MIN_ROWS:
+            y = self._gathered_matvec(x)
+        else:
+            y = gather_rows(self.local(x), self.group) if self.world > 1 else self.local(x)
         return y if self.bias is None else y + self.bias
+
+    def close(self) -> None:
+        """Release the gather regions (collective: every rank calls it)."""
+        for r in self._regions.values():
+            r.close()
+        self._regions.clear()

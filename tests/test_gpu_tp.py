@@ -1,6 +1,8 @@
 """Output-row tensor parallelism on real GPUs: two NCCL ranks, each holding
 half of a packed projection's rows, must reproduce the single-GPU result
-(matvec and matmul paths).  Skipped with fewer than two GPUs."""
+(matvec with the gather fused in, matmul with an NCCL all-gather), also over
+repeated calls and CUDA-graph replays of the fused gather.  Skipped with
+fewer than two GPUs."""
 import os
 import socket
 
@@ -48,6 +50,48 @@ def _worker(rank, world, port, q):
                                            out_dtype=torch.float32)
                 err = float((y - ref).norm() / ref.norm())
                 ok = ok and y.shape == ref.shape and err <= 1e-3
+        # Matvec with the gather fused in: against the NCCL path and one GPU,
+        # repeated on two alternating regions (flag counts advance per call),
+        # then replayed from a CUDA graph.
+        from gsq_b200 import _lib
+        from gsq_b200.parallel import GatherRegion, quantized_matvec_gather, shard_packed
+        n, k = 2048, 5120
+        packed = random_matrix_torch("IQ2_XS", n, k, seed=5, device=dev)
+        shard = shard_packed(packed, "IQ2_XS", n, k, world, rank)
+        regions = [GatherRegion(1, n) for _ in range(2)]
+        xs = [torch.randn(1, k, device=dev, dtype=torch.float16, generator=torch.Generator(device=dev).manual_seed(i))
+              for i in range(2)]
+        refs = [quantized_matvec(x, packed, qtype="IQ2_XS", out_features=n, in_features=k, out_dtype=torch.float32)
+                for x in xs]
+        for it in range(20):
+            i = it % 2
+            y = quantized_matvec_gather(xs[i], shard, qtype="IQ2_XS", out_features=n // world, in_features=k,
+                                        region=regions[i], row0=rank * (n // world))
+            err = float((y - refs[i]).norm() / refs[i].norm())
+            ok = ok and err <= 1e-3
+        g = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream(device=dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                for i in range(2):
+                    quantized_matvec_gather(xs[i], shard, qtype="IQ2_XS", out_features=n // world, in_features=k,
+                                            region=regions[i], row0=rank * (n // world))
+        torch.cuda.current_stream(dev).wait_stream(st)
+        for _ in range(5):
+            regions[0].y.zero_()
+            regions[1].y.zero_()
+            torch.cuda.synchronize()
+            dist.barrier()
+            g.replay()
+            torch.cuda.synchronize()
+            for i in range(2):
+                ok = ok and float((regions[i].y - refs[i]).norm() / refs[i].norm()) <= 1e-3
+        ok = ok and _lib.load().gsq_device_status(None) == 0
+        del g
+        for r in regions:
+            r.close()
+        layer.close()
         torch.cuda.synchronize()
         q.put((rank, ok))
     finally:
