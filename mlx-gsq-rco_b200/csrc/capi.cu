@@ -98,7 +98,8 @@ static int check_matrix(int qtype, const uint8_t* packed, int64_t N, int64_t K) 
 
 size_t gsq_qmv_workspace_size(int qtype, int64_t N, int64_t K, int64_t rows) {
   if (!supported(qtype) || N <= 0 || K <= 0 || K % QK || rows <= 0) return 0;
-  return qmv_plan(qtype, N, K, (int)rows).workspace;
+  // Also enough for gsq_qmv_gather's one-row-per-tile plan of the same shape.
+  return std::max(qmv_plan(qtype, N, K, (int)rows).workspace, qmv_plan(qtype, N, K, (int)rows, true).workspace);
 }
 
 int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t rows,
@@ -187,7 +188,7 @@ int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed,
   if (!x) return fail(GSQ_ERR_ARG, "null x");
   if (!dtype_ok(x_dtype)) return fail(GSQ_ERR_ARG, "unsupported dtype");
   if (!aligned(x, 16)) return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned");
-  const QmvPlan p = qmv_plan(qtype, N, K, (int)rows);
+  const QmvPlan p = qmv_plan(qtype, N, K, (int)rows, true);
   if (p.ctas <= 0)
     return fail(GSQ_ERR_SIZE, "matrix too large for the matvec (N=%lld, K=%lld)", (long long)N, (long long)K);
   if (p.workspace > 0 && (!workspace || workspace_bytes < p.workspace || !aligned(workspace, 256)))

@@ -46,7 +46,9 @@ struct QmvPlan {
   size_t workspace;  // scratch bytes (tickets + partial sums), 0 when no tile is split
 };
 
-QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows);
+// one_row_tiles: one activation row per tile (the gathering kernel exists
+// only in that form).
+QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows, bool one_row_tiles = false);
 
 // Runs QMV with `ws` as scratch (must hold plan.workspace bytes, zero-filled
 // tickets; left zero-filled on completion).

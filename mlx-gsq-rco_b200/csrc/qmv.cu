@@ -66,6 +66,14 @@ constexpr int QMV_GFLAG_TICKET = 62, QMV_GFLAG_COUNT = 63;
 constexpr size_t QMV_GATHER_HEADER = 64 * sizeof(unsigned);
 constexpr size_t QMV_TICKET_BYTES = QMV_TICKET_SLOTS * sizeof(unsigned);
 
+// Non-negative division and remainder with a 32-bit path: the work-split
+// arithmetic fits 32 bits for every plannable shape, and a 64-bit division
+// is a long software sequence.
+__device__ __forceinline__ int64_t udiv(int64_t a, int64_t b) {
+  return ((uint64_t)a | (uint64_t)b) >> 32 ? a / b : (int64_t)((uint32_t)a / (uint32_t)b);
+}
+__device__ __forceinline__ int64_t umod(int64_t a, int64_t b) { return a - udiv(a, b) * b; }
+
 struct QmvArgs {
   const uint8_t* packed;
   const void* x;
@@ -103,8 +111,9 @@ __device__ __forceinline__ unsigned long long ld_pair_sys(const uint2* p) {
 
 // Store one output value: y, or (gathering) this rank's own region and, as
 // a {value, call count} pair, every peer's inbox slot for call count ep.
+template <bool GATHER>
 __device__ __forceinline__ void store_y(const QmvArgs& a, int batch, int64_t rr, float v, unsigned ep) {
-  if (a.world <= 1) {
+  if constexpr (!GATHER) {
     store_out(a.y, a.y_dtype, (int64_t)batch * a.N + rr, v);
     return;
   }
@@ -118,8 +127,10 @@ __device__ __forceinline__ void store_y(const QmvArgs& a, int batch, int64_t rr,
 
 // Call count of this call on the gather region (read after griddepcontrol.wait:
 // the previous call on the region may be the kernel just before).
+template <bool GATHER>
 __device__ __forceinline__ unsigned gather_count(const QmvArgs& a) {
-  return a.world > 1 ? a.gflags[a.rank][QMV_GFLAG_COUNT] + 1u : 0u;
+  if constexpr (GATHER) return a.gflags[a.rank][QMV_GFLAG_COUNT] + 1u;
+  return 0u;
 }
 
 // End of a gathering call, run by the consumer and combiner threads of every
@@ -147,7 +158,7 @@ __device__ void gather_finish(const QmvArgs& a, unsigned ep) {
   const long long t0 = clock64();
   bool late = false;  // a timed-out thread still reaches the barrier below
   for (int64_t i = cta * NT + t; i < total && !late; i += nthreads) {
-    const int64_t col = i % a.ntot;
+    const int64_t col = umod(i, a.ntot);
     if (col >= a.row0 && col < a.row0 + a.N) continue;  // this rank's own rows
     unsigned long long w = ld_pair_sys(in + i);
     while ((unsigned)(w >> 32) != ep) {
@@ -438,9 +449,9 @@ struct QmvCursor {
   int w, b0, e1;        // slice width, first block in t0, end block in t1
   int phase;            // 0 last shared tile, 1 first shared tile, 2 whole tiles, 3 done
   __device__ QmvCursor(int64_t u0, int64_t u1, int width) : w(width) {
-    t0 = u0 / width;
+    t0 = udiv(u0, width);
     b0 = (int)(u0 - t0 * width);
-    t1 = (u1 - 1) / width;
+    t1 = udiv(u1 - 1, width);
     e1 = (int)(u1 - t1 * width);
     phase = u1 > u0 ? 0 : 3;
     enter();
@@ -489,11 +500,11 @@ struct QmvCursor {
 __device__ __forceinline__ void cta_range(const QmvArgs& a, int64_t U, int w, int c, int C, int64_t& u0,
                                           int64_t& u1) {
   if (a.aligned) {
-    u0 = ((int64_t)c * a.tiles / C) * w;
-    u1 = ((int64_t)(c + 1) * a.tiles / C) * w;
+    u0 = udiv((int64_t)c * a.tiles, C) * w;
+    u1 = udiv((int64_t)(c + 1) * a.tiles, C) * w;
   } else {
-    u0 = (int64_t)c * U / C;
-    u1 = (int64_t)(c + 1) * U / C;
+    u0 = udiv((int64_t)c * U, C);
+    u1 = udiv((int64_t)(c + 1) * U, C);
   }
 }
 
@@ -524,12 +535,12 @@ __device__ void publish_piece(const QmvArgs& a, int btile, int C, int c, float v
   if (lane < NB * 16) st_relaxed_gpu(a.slots + ((int64_t)btile * C + c) * (NB * 16) + lane, piece_enc(v));
 }
 
-template <int NB>
+template <int NB, bool GATHER>
 __device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t U, int w, int64_t tile, float v,
                               unsigned ep) {
   const int lane = threadIdx.x & 31;
   if (lane >= NB * 16) return;
-  const int64_t c0 = ((tile * w + 1) * C - 1) / U;  // first CTA touching the tile
+  const int64_t c0 = udiv((tile * w + 1) * C - 1, U);  // first CTA touching the tile
   float sum = 0.f;
   for (int64_t c2 = c0; c2 < c; c2++) {
     uint32_t* p = a.slots + ((int64_t)btile * C + c2) * (NB * 16) + lane;
@@ -552,7 +563,7 @@ __device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t
   const int b = lane >> 4, r = lane & 15;
   const int batch = btile * NB + b;
   const int64_t rr = tile * 16 + r;
-  if (batch < a.rows && rr < a.N) store_y(a, batch, rr, sum, ep);
+  if (batch < a.rows && rr < a.N) store_y<GATHER>(a, batch, rr, sum, ep);
 }
 
 // Global combination of one piece of a tile shared with other CTAs (other
@@ -560,7 +571,7 @@ __device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t
 // a ticket, and if this was the last piece, sum all pieces of the tile in
 // slice order then CTA order and write y.  Executed by the combiner warp; v
 // is this piece's row sum (lane = b*16 + r).
-template <int NB>
+template <int NB, bool GATHER>
 __device__ void combine_piece(const QmvArgs& a, int btile, int slice, int C, int c, int w, int64_t tile,
                               int64_t first_tile, int seg_len, float v, unsigned ep) {
   const int lane = threadIdx.x & 31;
@@ -588,29 +599,32 @@ __device__ void combine_piece(const QmvArgs& a, int btile, int slice, int C, int
       const int w2 = min(a.bps, a.kb - s2 * a.bps);
       const int64_t U2 = a.tiles * w2;
       const int64_t ut0 = tile * w2, ut1 = ut0 + w2;
-      const int64_t c0 = ((ut0 + 1) * C - 1) / U2;
-      const int64_t c1 = (ut1 * C - 1) / U2;
+      const int64_t c0 = udiv((ut0 + 1) * C - 1, U2);
+      const int64_t c1 = udiv(ut1 * C - 1, U2);
       const int64_t base = (int64_t)btile * a.slices + s2;
       if (c0 == c1) {  // one CTA covered the whole slice of this tile
         sum += __ldcg(a.part_full + (base * a.tiles + tile) * (NB * 16) + lane);
         continue;
       }
       for (int64_t c2 = c0; c2 <= c1; c2++) {
-        const int64_t s0 = c2 * U2 / C, s1 = (c2 + 1) * U2 / C;
+        const int64_t s0 = udiv(c2 * U2, C), s1 = udiv((c2 + 1) * U2, C);
         if (s0 == s1 || s1 <= ut0 || s0 >= ut1) continue;  // empty or not covering this tile
-        const int sl = (s0 / w2 == tile) ? 0 : 1;
+        const int sl = (udiv(s0, w2) == tile) ? 0 : 1;
         sum += __ldcg(a.part_piece + ((base * C + c2) * 2 + sl) * (NB * 16) + lane);
       }
     }
     const int b = lane >> 4, r = lane & 15;
     const int batch = btile * NB + b;
     const int64_t rr = tile * 16 + r;
-    if (batch < a.rows && rr < a.N) store_y(a, batch, rr, sum, ep);
+    if (batch < a.rows && rr < a.N) store_y<GATHER>(a, batch, rr, sum, ep);
   }
   if (lane == 0) *tk = 0u;
 }
 
-template <int T, int NB>
+// GATHER: the row-parallel variant (gsq_qmv_gather), instantiated for
+// one-activation-row tiles only; the ordinary kernel carries none of its code
+// (its presence alone cost ~2 % in the single-GPU sweep).
+template <int T, int NB, bool GATHER>
 __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
   using MV = Mv<T>;
   using G = QmvGeom<T>;
@@ -722,7 +736,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     // takes over every piece that needs other CTAs' pieces, so that the
     // tensor-core warps never wait on global-memory round trips.
     pdl_wait();  // before any global write
-    const unsigned gep = gather_count(a);
+    const unsigned gep = gather_count<GATHER>(a);
     QmvCursor cur(ub, ue, w);
     const int64_t first_tile = cur.t0;
     int rbuf = 0;
@@ -743,15 +757,15 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&rfree[rbuf]);
         if (a.slices > 1)
-          combine_piece<NB>(a, btile, slice, C, c, w, tile, first_tile, seg_len, v, gep);
+          combine_piece<NB, GATHER>(a, btile, slice, C, c, w, tile, first_tile, seg_len, v, gep);
         else if (sb + seg_len < w)
           publish_piece<NB>(a, btile, C, c, v);  // later CTAs hold the rest of this tile
         else
-          gather_pieces<NB>(a, btile, C, c, U, w, tile, v, gep);
+          gather_pieces<NB, GATHER>(a, btile, C, c, U, w, tile, v, gep);
       }
       if (++rbuf == RB) { rbuf = 0; rph ^= 1u; }
     }
-    if (a.world > 1) gather_finish(a, gep);
+    if constexpr (GATHER) gather_finish(a, gep);
     return;
   }
 
@@ -774,7 +788,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
     mbar_wait_bounded(xcopy, 0u, a.err);
   }
   quantise_slice<T, NB, MV::BIAS>(a, btile, kb0, w, KS, xq_s, xs_s, xsum_s);
-  const unsigned gep = gather_count(a);
+  const unsigned gep = gather_count<GATHER>(a);
   named_sync_consumers();
   if (threadIdx.x == 0) mbar_arrive(xready);
 
@@ -1002,7 +1016,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
         const int b = lane >> 4, r = lane & 15;
         const int batch = btile * NB + b;
         const int64_t rr = tile * 16 + r;
-        if (lane < NB * 16 && batch < a.rows && rr < a.N) store_y(a, batch, rr, v, gep);
+        if (lane < NB * 16 && batch < a.rows && rr < a.N) store_y<GATHER>(a, batch, rr, v, gep);
       }
       if (++rbuf == RB) { rbuf = 0; rph ^= 1u; }
       seg_no++;
@@ -1010,7 +1024,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
       seg_len = 0;
     }
   }
-  if (a.world > 1) gather_finish(a, gep);
+  if constexpr (GATHER) gather_finish(a, gep);
 }
 
 // --------------------------------------------------------------------------
@@ -1024,9 +1038,9 @@ static int qmv_occupancy() {
   if (cached > 0) return cached;
   int occ = 0;
   const size_t smem = QMV_CTA_SMEM;
-  if (cudaFuncSetAttribute(qmv_kernel<T, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  if (cudaFuncSetAttribute(qmv_kernel<T, NB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
           cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, qmv_kernel<T, NB>, QMV_THREADS, smem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, qmv_kernel<T, NB, false>, QMV_THREADS, smem) != cudaSuccess ||
       occ <= 0) {
     cudaGetLastError();
     occ = (int)std::max<size_t>(1, std::min<size_t>(2, (228u * 1024u) / (smem + 1024)));
@@ -1059,10 +1073,10 @@ static int qmv_sm_count() {
 
 static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
-QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
+QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows, bool one_row_tiles) {
   QmvPlan p = {};
   const int kb = (int)(K / QK);
-  p.nb = rows == 1 ? 1 : 2;
+  p.nb = rows == 1 || one_row_tiles ? 1 : 2;
   p.btiles = (rows + p.nb - 1) / p.nb;
   p.tiles = (N + 15) / 16;
   size_t fixed = 0;
@@ -1132,9 +1146,9 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows) {
   return p;
 }
 
-template <int T, int NB>
+template <int T, int NB, bool GATHER>
 static cudaError_t qmv_launch_t(const QmvArgs& a, const QmvPlan& p, cudaStream_t st) {
-  auto kern = qmv_kernel<T, NB>;
+  auto kern = qmv_kernel<T, NB, GATHER>;
   static int configured[64] = {0};  // dynamic smem attribute already set, per device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1147,9 +1161,10 @@ static cudaError_t qmv_launch_t(const QmvArgs& a, const QmvPlan& p, cudaStream_t
   return launch_pdl(kern, dim3(p.ctas, p.slices, p.btiles), dim3(QMV_THREADS), p.smem, st, a);
 }
 
-#define GSQ_QMV_LAUNCH_CASE(TT) \
-  case TT:                      \
-    return p.nb == 1 ? qmv_launch_t<TT, 1>(a, p, st) : qmv_launch_t<TT, 2>(a, p, st);
+#define GSQ_QMV_LAUNCH_CASE(TT)                                                     \
+  case TT:                                                                          \
+    if (a.world > 1) return p.nb == 1 ? qmv_launch_t<TT, 1, true>(a, p, st) : cudaErrorInvalidValue; \
+    return p.nb == 1 ? qmv_launch_t<TT, 1, false>(a, p, st) : qmv_launch_t<TT, 2, false>(a, p, st);
 
 static cudaError_t qmv_launch(int t, const QmvArgs& a, const QmvPlan& p, cudaStream_t st) {
   switch (t) { GSQ_FOR_EACH_QTYPE(GSQ_QMV_LAUNCH_CASE) }
