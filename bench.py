@@ -165,6 +165,18 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def decode_tok_s(per):
+    """Batch-1 decode tokens/s of one FFN-shaped projection pair per type
+    (17408x5120 up + 5120x17408 down), from the per-configuration timings:
+    1 / (t_up + t_down).  A per-pair figure, not a model's tok/s."""
+    out = {}
+    for q in TYPES:
+        t = [r["us"] for r in per if r["type"] == q and (r["N"], r["K"]) in ((17408, 5120), (5120, 17408))]
+        if len(t) == 2:
+            out[q] = round(1e6 / sum(t), 1)
+    return out or None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -393,7 +405,9 @@ def main():
                 del w
         tf = flops_total / t_qmm / 1e12
         qmm = {"M": 512, "tflops": round(tf, 1), "peak": pk["bf16"], "frac": round(tf / pk["bf16"], 4),
-               "prefill_tok_s_per_projection_set": None, "per_shape": qres,
+               "prefill_tok_s_per_projection_pair": {
+                   q: round(512.0 / sum(r["us"] * 1e-6 for r in qres if r["type"] == q), 1) for q in QMM_TYPES},
+               "per_shape": qres,
                "note": "includes the bf16->fp16 activation pre-pass; weights decoded once per 128x128 tile; "
                        "CUDA graph of 8 launches, CUDA events"}
 
@@ -414,10 +428,11 @@ def main():
             "data": "synthetic",
             "config": {"workload": "config-2 QMV sweep: 11 types x {5120->5120, 5120->17408, 17408->5120}, batch 1",
                        "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (886 MB per step)",
-                       "parallelism": (f"tp{world} (output rows; the gather is fused into the matvec: NVLink "
-                                       f"stores into every rank's output, flag exchange)") if world > 1 else "single GPU",
+                       "parallelism": (f"tp{world} (output rows; the gather is fused into the matvec: each "
+                                       f"value goes to every rank's inbox over NVLink)") if world > 1 else "single GPU",
                        "timing": "CUDA graph of one step, replayed; CUDA events"},
             "roofline": roofline, "qmv_sweep": per, "qmm_prefill": qmm, "cpu_baseline": cpu, "e2e": e2e,
+            "decode_tok_s_per_projection_pair": decode_tok_s(per),
             "clocks": clocks.summary(), "gpu_launches": args.steps * len(cfgs),
         }
         print(json.dumps(line), flush=True)

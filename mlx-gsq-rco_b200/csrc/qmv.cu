@@ -1073,7 +1073,7 @@ static int qmv_sm_count() {
 
 static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
-QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows, bool one_row_tiles) {
+static QmvPlan qmv_plan_compute(int t, int64_t N, int64_t K, int rows, bool one_row_tiles) {
   QmvPlan p = {};
   const int kb = (int)(K / QK);
   p.nb = rows == 1 || one_row_tiles ? 1 : 2;
@@ -1143,6 +1143,28 @@ QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows, bool one_row_tiles) {
     p.off_full = p.off_piece = 0;
     p.workspace = 0;
   }
+  return p;
+}
+
+// The plan depends only on the shape (and the device model): the last few are
+// kept per host thread, so a call does not redo it (the workspace query and
+// the launch of one call both need it).
+QmvPlan qmv_plan(int t, int64_t N, int64_t K, int rows, bool one_row_tiles) {
+  struct Entry {
+    int t, rows, one;
+    int64_t N, K;
+    QmvPlan p;
+  };
+  static thread_local Entry cache[8];
+  static thread_local int filled = 0, next = 0;
+  for (int i = 0; i < filled; i++) {
+    const Entry& e = cache[i];
+    if (e.t == t && e.N == N && e.K == K && e.rows == rows && e.one == (int)one_row_tiles) return e.p;
+  }
+  const QmvPlan p = qmv_plan_compute(t, N, K, rows, one_row_tiles);
+  cache[next] = Entry{t, rows, (int)one_row_tiles, N, K, p};
+  next = (next + 1) % 8;
+  filled = std::min(filled + 1, 8);
   return p;
 }
 

@@ -17,6 +17,10 @@ from ...quant.layouts import QUANT_BLOCK_SIZES, GGMLQuantizationType
 from .qmm import QMM_MIN_ROWS, quantized_matmul
 
 
+# gsq_qmv_workspace_size per (type id, N, K, rows): a pure function of the shape.
+_WORKSPACE_BYTES: dict[tuple[int, int, int, int], int] = {}
+
+
 def _validate(x, packed, qtype, out_features, in_features):
     try:
         type_id = int(GGMLQuantizationType[qtype])
@@ -54,7 +58,10 @@ def quantized_matvec(x: torch.Tensor, packed: torch.Tensor, *, qtype: str, out_f
     pk = packed.reshape(-1).contiguous()
     y = torch.empty((rows, out_features), dtype=out_dtype, device=dev)
     lib = _lib.load()
-    need = lib.gsq_qmv_workspace_size(type_id, out_features, in_features, rows)
+    key = (type_id, out_features, in_features, rows)
+    need = _WORKSPACE_BYTES.get(key)
+    if need is None:
+        need = _WORKSPACE_BYTES[key] = lib.gsq_qmv_workspace_size(type_id, out_features, in_features, rows)
     ws = _lib.workspaces.get(dev, need, "qmv")
     code = lib.gsq_qmv(type_id, flat.data_ptr(), _lib.DTYPE_CODES[flat.dtype], pk.data_ptr(), out_features,
                        in_features, rows, y.data_ptr(), _lib.DTYPE_CODES[out_dtype],
