@@ -367,17 +367,30 @@ def main():
            "path": "pinned host x -> quantized_matvec (one ctypes C-ABI call per projection) -> y copied to "
                    "pinned host memory; one stream synchronisation per step"}
 
-    # ---- QMM prefill, config 3 at M=512 (single GPU) ----
+    # ---- QMM prefill, config 3 at M=512 (ranks > 1: each rank's row shard,
+    # then an NCCL all-gather of the (512, N/P) slices) ----
     qmm = None
-    if world == 1 and not args.no_qmm:
+    if not args.no_qmm:
         qres = []
         flops_total, t_qmm = 0.0, 0.0
         for q in QMM_TYPES:
             for (n, k) in QMM_SHAPES:
-                w = random_matrix_torch(q, n, k, seed=7, device=dev)
-                x = torch.randn(512, k, device=dev, dtype=torch.bfloat16)
+                rows = n // world
+                full = random_matrix_torch(q, n, k, seed=7, device=dev)
+                rb = (k // 256) * BLOCK_BYTES[q]
+                w = full[rank * rows * rb:(rank + 1) * rows * rb].clone()
+                del full
+                x = torch.randn(512, k, device=dev, dtype=torch.bfloat16,
+                                generator=torch.Generator(device=dev).manual_seed(11))
+                gathered = torch.empty(world, 512, rows, device=dev, dtype=torch.float32) if world > 1 else None
+
+                def prefill():
+                    y = quantized_matmul(x, w, qtype=q, out_features=rows, in_features=k, out_dtype=torch.float32)
+                    if world > 1:
+                        dist.all_gather_into_tensor(gathered, y)
+
                 for _ in range(2):
-                    quantized_matmul(x, w, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
+                    prefill()
                 torch.cuda.synchronize()
                 g = torch.cuda.CUDAGraph()
                 st = torch.cuda.Stream(device=dev)
@@ -385,10 +398,12 @@ def main():
                 with torch.cuda.stream(st):
                     with torch.cuda.graph(g, stream=st):
                         for _ in range(8):
-                            quantized_matmul(x, w, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
+                            prefill()
                 torch.cuda.current_stream(dev).wait_stream(st)
                 g.replay()
                 torch.cuda.synchronize()
+                if world > 1:
+                    dist.barrier()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
                 for _ in range(3):
@@ -396,6 +411,10 @@ def main():
                 e1.record()
                 torch.cuda.synchronize()
                 t_ms = e0.elapsed_time(e1) / 24
+                if world > 1:
+                    tt = torch.tensor([t_ms], device=dev)
+                    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                    t_ms = float(tt.item())
                 del g
                 fl = 2.0 * 512 * n * k
                 flops_total += fl
@@ -404,12 +423,15 @@ def main():
                              "TFLOPs": round(fl / (t_ms / 1e3) / 1e12, 1)})
                 del w
         tf = flops_total / t_qmm / 1e12
-        qmm = {"M": 512, "tflops": round(tf, 1), "peak": pk["bf16"], "frac": round(tf / pk["bf16"], 4),
+        qmm = {"M": 512, "tflops": round(tf, 1), "peak": round(pk["bf16"] * world, 1),
+               "frac": round(tf / (pk["bf16"] * world), 4),
                "prefill_tok_s_per_projection_pair": {
                    q: round(512.0 / sum(r["us"] * 1e-6 for r in qres if r["type"] == q), 1) for q in QMM_TYPES},
                "per_shape": qres,
                "note": "includes the bf16->fp16 activation pre-pass; weights decoded once per 128x128 tile; "
-                       "CUDA graph of 8 launches, CUDA events"}
+                       "CUDA graph of 8 launches, CUDA events" + (
+                           f"; {world} ranks: row shards plus an NCCL all-gather, max over ranks, "
+                           f"peak = {world} x the measured bf16 peak" if world > 1 else "")}
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
