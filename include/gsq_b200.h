@@ -131,7 +131,7 @@ GSQ_API int gsq_ipc_export(void* region, uint8_t handle[64]);
 GSQ_API int gsq_ipc_import(const uint8_t handle[64], void** peer);
 GSQ_API int gsq_ipc_close(void* peer);
 
-/* gsq_qmv for rank `rank` of `world` (2..8) holding output rows
+/* gsq_qmv for 1..7 activation rows on rank `rank` of `world` (2..8) holding output rows
  * [row0, row0 + N) of ntot: the kernel sends its rows into every rank's
  * region (regions[i] = rank i's region, mapped in this process) over NVLink
  * and ends with the exchange of the rows through the regions' inboxes, so
@@ -142,6 +142,17 @@ GSQ_API int gsq_ipc_close(void* peer);
  * others return with gsq_device_status() == 1.  Output is fp32. */
 GSQ_API int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
                            int64_t rows, void* const* regions, int world, int rank, int64_t row0, int64_t ntot,
+                           void* workspace, size_t workspace_bytes, gsq_stream_t stream);
+
+/* gsq_qmm for rank `rank` of `world` (2..8) holding output rows
+ * [row0, row0 + N) of ntot (prefill): every output tile is stored into every
+ * rank's region (fp32 M x ntot at byte 256) over NVLink as the epilogue
+ * writes it, and each rank counts the tiles its peers delivered, so that once
+ * the call has completed on `stream` every rank's region holds all ntot rows.
+ * Same region rules and bounded wait as gsq_qmv_gather (a region for M >= 8
+ * rows has no inbox: gsq_gather_region_bytes(M, ntot) bytes). */
+GSQ_API int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
+                           int64_t M, void* const* regions, int world, int rank, int64_t row0, int64_t ntot,
                            void* workspace, size_t workspace_bytes, gsq_stream_t stream);
 
 /* Synchronises `stream`, then returns and clears the device error word the

@@ -182,7 +182,8 @@ int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed,
   if (!regions) return fail(GSQ_ERR_ARG, "null region list");
   for (int i = 0; i < world; i++)
     if (!regions[i] || !aligned(regions[i], 256)) return fail(GSQ_ERR_ALIGN, "region %d missing or not 256-byte aligned", i);
-  if (rows <= 0 || rows > (1 << 20)) return fail(GSQ_ERR_SIZE, "invalid row count %lld", (long long)rows);
+  if (rows <= 0 || rows >= 8)
+    return fail(GSQ_ERR_SIZE, "gsq_qmv_gather takes 1..7 activation rows, got %lld", (long long)rows);
   if (row0 < 0 || N <= 0 || row0 + N > ntot) return fail(GSQ_ERR_SIZE, "rows [%lld, %lld) outside the %lld gathered rows",
                                                          (long long)row0, (long long)(row0 + N), (long long)ntot);
   if (!x) return fail(GSQ_ERR_ARG, "null x");
@@ -199,6 +200,35 @@ int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed,
   cudaError_t e = qmv_run(qtype, x, x_dtype, packed, N, K, (int)rows, own_y, DT_F32, workspace, p,
                           device_error_word(), (cudaStream_t)stream, &g);
   return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_qmv_gather launch");
+}
+
+int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
+                   void* const* regions, int world, int rank, int64_t row0, int64_t ntot, void* workspace,
+                   size_t workspace_bytes, gsq_stream_t stream) {
+  int rc = check_matrix(qtype, packed, N, K);
+  if (rc) return rc;
+  if (world < 2 || world > 8 || rank < 0 || rank >= world) return fail(GSQ_ERR_ARG, "world must be 2..8 and rank < world");
+  if (!regions) return fail(GSQ_ERR_ARG, "null region list");
+  for (int i = 0; i < world; i++)
+    if (!regions[i] || !aligned(regions[i], 256)) return fail(GSQ_ERR_ALIGN, "region %d missing or not 256-byte aligned", i);
+  if (M <= 0 || M > (1ll << 31)) return fail(GSQ_ERR_SIZE, "invalid row count %lld", (long long)M);
+  if (row0 < 0 || N <= 0 || row0 + N > ntot)
+    return fail(GSQ_ERR_SIZE, "rows [%lld, %lld) outside the %lld gathered rows", (long long)row0,
+                (long long)(row0 + N), (long long)ntot);
+  if (!x) return fail(GSQ_ERR_ARG, "null x");
+  if (!dtype_ok(x_dtype)) return fail(GSQ_ERR_ARG, "unsupported x dtype");
+  if (!aligned(x, 16)) return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned");
+  const size_t need = qmm_workspace_bytes(qtype, N, K, M, x_dtype);
+  if (need > 0 && (!workspace || workspace_bytes < need || !aligned(workspace, 256)))
+    return fail(GSQ_ERR_WORKSPACE, "gsq_qmm_gather needs %zu workspace bytes (256-byte aligned), got %zu", need,
+                workspace_bytes);
+  const QmmGather g = {regions, world, rank, row0, ntot};
+  float* own_y = reinterpret_cast<float*>(static_cast<uint8_t*>(regions[rank]) + 256);
+  const char* why = "";
+  cudaError_t e = qmm_launch(qtype, x, x_dtype, packed, N, K, M, own_y, workspace, device_error_word(),
+                             (cudaStream_t)stream, &why, &g);
+  if (e != cudaSuccess) return fail(GSQ_ERR_CUDA, "gsq_qmm_gather launch: %s (%s)", cudaGetErrorString(e), why);
+  return GSQ_OK;
 }
 
 size_t gsq_qmm_workspace_size(int qtype, int64_t N, int64_t K, int64_t M, int x_dtype) {

@@ -82,8 +82,17 @@ struct QmmPlan {
 QmmPlan qmm_plan(int t, int64_t N, int64_t K, int64_t M, int x_dtype);
 size_t qmm_workspace_bytes(int t, int64_t N, int64_t K, int64_t M, int x_dtype);
 // ws: the plan's scratch, zero-filled once by the caller.
+// Fused row gather of a rank's output rows into every rank's region (see
+// gsq_qmm_gather); regions[i] is rank i's region, mapped in this process.
+struct QmmGather {
+  void* const* regions;
+  int world, rank;
+  int64_t row0, ntot;
+};
+
 cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-                       float* y, void* ws, int* err, cudaStream_t st, const char** why);
+                       float* y, void* ws, int* err, cudaStream_t st, const char** why,
+                       const struct QmmGather* gather = nullptr);
 
 // Records `msg` as this thread's gsq_last_error() text and returns `code`.
 int set_last_error(int code, const char* msg);

@@ -73,6 +73,9 @@ struct QmmPipe {
   static_assert(stages_for((size_t)512 * 128, 2) >= 2, "QMM ring must hold two stages at 512 tokens");
 };
 
+constexpr int QMM_GATHER_MAX = 8;
+constexpr int QMM_GFLAG_TICKET = 62, QMM_GFLAG_COUNT = 63;  // owner's words of a gather region header
+
 struct QmmArgs {
   const uint8_t* packed;
   int64_t N, K, M, row_bytes, packed_bytes;
@@ -82,7 +85,66 @@ struct QmmArgs {
   int bn, nacc;       // MMA N per accumulator, accumulators per CTA
   int ksplit, kbs;    // K splits, 256-blocks per split
   int* err;
+  // Fused row gather (world > 1, gsq_qmm_gather): output rows
+  // [row0, row0 + N) of ntot go to every rank's region (fp32 [M][ntot] after
+  // a 256-byte header whose word p counts the tiles rank p has delivered).
+  float* gy[QMM_GATHER_MAX];
+  unsigned* gflags[QMM_GATHER_MAX];
+  int world, rank;
+  int64_t row0, ntot;
 };
+
+// One output value: y, or every rank's gather region (coalesced per warp:
+// 32 consecutive rows of one token).
+__device__ __forceinline__ void qmm_store(const QmmArgs& a, int64_t m, int64_t erow, float v) {
+  if (a.world <= 1) {
+    a.y[m * a.N + erow] = v;
+    return;
+  }
+  const int64_t off = m * a.ntot + a.row0 + erow;
+#pragma unroll
+  for (int p = 0; p < QMM_GATHER_MAX; p++)
+    if (p < a.world) a.gy[p][off] = v;
+}
+
+// End of a gathering call, one thread per CTA, after the decoder warps'
+// barrier.  A CTA that stored an output tile (every CTA without split-K, the
+// last split otherwise) adds 1 to this rank's word in every peer's region
+// (release, system scope; the storing threads fenced their peer stores at
+// system scope before the barrier).  The last CTA of the grid (gpu-scope
+// ticket) then waits, bounded, until every peer's word in the own region
+// reaches this call's total (calls x tiles per rank, acquire): when the
+// kernel completes, every rank's tiles of this call are in every region.
+// Every rank must make the same sequence of calls on a region.
+__device__ void qmm_gather_signal(const QmmArgs& a, bool stored) {
+  unsigned* own = a.gflags[a.rank];
+  if (stored) {
+    for (int p = 0; p < a.world; p++)
+      if (p != a.rank)
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.gflags[p] + a.rank) : "memory");
+  }
+  __threadfence();
+  const unsigned ctas = gridDim.x * gridDim.y * gridDim.z;
+  if (atomicAdd(own + QMM_GFLAG_TICKET, 1u) != ctas - 1u) return;
+  own[QMM_GFLAG_TICKET] = 0u;
+  const unsigned calls = own[QMM_GFLAG_COUNT] + 1u;
+  own[QMM_GFLAG_COUNT] = calls;
+  const unsigned expected = calls * (gridDim.x * gridDim.y);
+  const long long t0 = clock64();
+  for (int p = 0; p < a.world; p++) {
+    if (p == a.rank) continue;
+    for (;;) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + p) : "memory");
+      if ((int)(v - expected) >= 0) break;
+      if (clock64() - t0 > (1ll << 31)) {
+        atomicExch(a.err, DEV_WAIT_TIMEOUT);
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+}
 
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31) == 0; }
 
@@ -372,7 +434,7 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
 #pragma unroll
             for (int jj = 0; jj < 16; jj++) {
               const int64_t m = (int64_t)m0 + j0 + jj;
-              if (m < a.M) a.y[m * a.N + erow] = __uint_as_float(vv[jj]);
+              if (m < a.M) qmm_store(a, m, erow, __uint_as_float(vv[jj]));
             }
           }
         }
@@ -416,11 +478,17 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
 #pragma unroll
             for (int z = 1; z < QMM_KSPLIT_MAX; z++) acc += v[z][jj];  // zeros beyond ksplit
             const int64_t m = (int64_t)m0 + j0 + jj;
-            if (m < a.M) a.y[m * a.N + erow] = acc;
+            if (m < a.M) qmm_store(a, m, erow, acc);
           }
         }
       }
     }
+  }
+  if (a.world > 1 && warp >= QMM_DEC0) {
+    const bool stored = a.ksplit == 1 || *last_flag;
+    if (stored) __threadfence_system();  // this thread's stores into the peers' regions
+    named_sync_decoders();
+    if (warp == QMM_DEC0 && lane == 0) qmm_gather_signal(a, stored);
   }
   tc_fence_before();
   __syncthreads();
@@ -534,7 +602,7 @@ static cudaError_t qmm_launch_t(const QmmArgs& a, const QmmPlan& p, const CUtens
 // ws holds the plan's scratch (zero-filled once by the caller; the ticket
 // region is left zero-filled by every call).
 cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-                       float* y, void* ws, int* err, cudaStream_t st, const char** why) {
+                       float* y, void* ws, int* err, cudaStream_t st, const char** why, const QmmGather* gather) {
   const QmmPlan p = qmm_plan(t, N, K, M, x_dtype);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   __half* x16 = reinterpret_cast<__half*>(wsb + p.off_x16);
@@ -557,6 +625,29 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
   a.bn = p.bn; a.nacc = p.nacc; a.ksplit = p.ksplit; a.kbs = p.kbs;
   a.tickets = p.ksplit > 1 ? reinterpret_cast<unsigned*>(wsb) : nullptr;
   a.part = p.ksplit > 1 ? reinterpret_cast<float*>(wsb + p.off_part) : nullptr;
+  a.world = 0;
+  a.rank = 0;
+  a.row0 = 0;
+  a.ntot = N;
+  for (int i = 0; i < QMM_GATHER_MAX; i++) {
+    a.gy[i] = nullptr;
+    a.gflags[i] = nullptr;
+  }
+  if (gather && gather->world > 1) {
+    if (gather->world > QMM_GATHER_MAX || gather->rank < 0 || gather->rank >= gather->world) {
+      *why = "invalid gather world/rank";
+      return cudaErrorInvalidValue;
+    }
+    a.world = gather->world;
+    a.rank = gather->rank;
+    a.row0 = gather->row0;
+    a.ntot = gather->ntot;
+    for (int i = 0; i < gather->world; i++) {
+      uint8_t* r = static_cast<uint8_t*>(gather->regions[i]);
+      a.gflags[i] = reinterpret_cast<unsigned*>(r);
+      a.gy[i] = reinterpret_cast<float*>(r + 256);
+    }
+  }
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};

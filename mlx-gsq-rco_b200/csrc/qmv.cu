@@ -1197,8 +1197,11 @@ size_t qmv_gather_inbox_offset(int64_t rows, int64_t ntot) {
   return (QMV_GATHER_HEADER + (size_t)rows * ntot * sizeof(float) + 15) / 16 * 16;
 }
 
+// The inbox exists only for decode-sized regions (fewer than 8 rows: the
+// matvec's gather); a prefill region (the tiled matmul's gather) is header
+// and output only.
 size_t qmv_gather_region_bytes(int64_t rows, int64_t ntot) {
-  return qmv_gather_inbox_offset(rows, ntot) + 2 * (size_t)rows * ntot * sizeof(uint2);
+  return qmv_gather_inbox_offset(rows, ntot) + (rows < 8 ? 2 * (size_t)rows * ntot * sizeof(uint2) : 0);
 }
 
 cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int rows,

@@ -46,6 +46,7 @@ SIGNATURES = {
     "gsq_ipc_import": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
     "gsq_ipc_close": (_I, [_P]),
     "gsq_qmv_gather": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _I, _I, _I64, _I64, _P, _SZ, _P]),
+    "gsq_qmm_gather": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _I, _I, _I64, _I64, _P, _SZ, _P]),
 }
 
 _lib = None

@@ -1,18 +1,21 @@
-"""Row-parallel decode with the gather fused into the matvec.
+"""Row-parallel decode and prefill with the gather fused into the kernels.
 
-``RowParallelLinear`` joins the ranks' output slices with an NCCL all-gather
-after the local kernel, one collective (about 10 us of latency) per
-projection.  For decode rows the matvec kernel can instead store each output
-row straight into every rank's copy of the output over NVLink and finish
-with a flag exchange (``gsq_qmv_gather`` in ``include/gsq_b200.h``): one
-kernel per projection, no collective launch.
+``RowParallelLinear`` can join the ranks' output slices with an NCCL
+all-gather after the local kernel: one collective (about 10 us of latency at
+decode sizes) per projection.  Instead, the matvec kernel sends each output
+value straight into every rank's inbox over NVLink and each CTA collects its
+share of the peers' values (``gsq_qmv_gather`` in ``include/gsq_b200.h``):
+one kernel per projection, no collective launch.  The tiled matmul (prefill)
+does the same from its epilogue (``gsq_qmm_gather``): each output tile is
+stored into every rank's copy as it is written, and the ranks count each
+other's delivered tiles.
 
-A :class:`GatherRegion` is the per-call-site buffer behind it: every rank
-allocates ``gsq_gather_region_bytes(rows, ntot)`` bytes (256 bytes of flag
-words, then fp32 ``rows x ntot``), exports a CUDA IPC handle, and maps its
-peers' regions.  Every rank must make the same sequence of calls on a
-region, and a region serves one call site: its rows stay valid until the
-same site runs again.
+A :class:`GatherRegion` is the per-call-site buffer behind both: every rank
+allocates ``gsq_gather_region_bytes(rows, ntot)`` bytes (256 bytes of control
+words, then fp32 ``rows x ntot``, then for fewer than 8 rows the matvec's
+inbox), exports a CUDA IPC handle, and maps its peers' regions.  Every rank
+must make the same sequence of calls on a region, and a region serves one
+call site: its rows stay valid until the same site runs again.
 """
 from __future__ import annotations
 
@@ -109,6 +112,34 @@ def quantized_matvec_gather(x: torch.Tensor, packed_shard: torch.Tensor, *, qtyp
     ws = _lib.workspaces.get(dev, need, "qmv")
     code = lib.gsq_qmv_gather(tid, flat.data_ptr(), _lib.DTYPE_CODES[flat.dtype], pk.data_ptr(), out_features,
                               in_features, rows, region.regions, region.world, region.rank, row0, region.ntot,
+                              ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                              _lib.stream_ptr(dev))
+    _lib.check(code)
+    return region.y
+
+
+def quantized_matmul_gather(x: torch.Tensor, packed_shard: torch.Tensor, *, qtype: str, out_features: int,
+                            in_features: int, region: GatherRegion, row0: int) -> torch.Tensor:
+    """The tiled matmul (prefill) of this rank's rows [row0, row0 + out_features)
+    of a row-split projection with the gather fused into its epilogue
+    (``gsq_qmm_gather``): every output tile goes into every rank's region over
+    NVLink as it is written.  Returns the region's ``rows x ntot`` fp32
+    output, complete once the call finishes on the current stream."""
+    tid = _type_id(qtype)
+    dev = _lib.require_cuda(x, packed_shard)
+    rows = x.numel() // in_features
+    if rows != region.rows:
+        raise ValueError(f"x has {rows} rows, the region {region.rows}")
+    flat = x.reshape(rows, in_features).contiguous()
+    if flat.data_ptr() % 16:
+        flat = flat.clone()
+    pk = packed_shard.reshape(-1).contiguous()
+    lib = _lib.load()
+    xcode = _lib.DTYPE_CODES[flat.dtype]
+    need = lib.gsq_qmm_workspace_size(tid, out_features, in_features, rows, xcode)
+    ws = _lib.workspaces.get(dev, need, "qmm")
+    code = lib.gsq_qmm_gather(tid, flat.data_ptr(), xcode, pk.data_ptr(), out_features, in_features, rows,
+                              region.regions, region.world, region.rank, row0, region.ntot,
                               ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
                               _lib.stream_ptr(dev))
     _lib.check(code)
