@@ -92,3 +92,41 @@ def test_row_parallel_gloo(world):
         p.join(timeout=120)
     results = sorted(q.get(timeout=5) for _ in range(world))
     assert [r for r in results] == [(r, True) for r in range(world)]
+
+
+def _failing_worker(rank, world, port, result_q):
+    """Rank 1 fails before the step's gather; rank 0 must learn of it on the
+    host, from the collective's error, within the group's short timeout."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    try:
+        if rank == 1:
+            result_q.put((rank, "raised"))
+            raise SystemExit(0)  # leaves between steps: nothing of it in flight
+        t0 = time.time()
+        try:
+            gather_rows(torch.ones(2, 3))
+            result_q.put((rank, "no error"))
+        except RuntimeError:
+            result_q.put((rank, "error" if time.time() - t0 < 60 else "late"))
+    finally:
+        if rank == 0:
+            dist.destroy_process_group()
+
+
+def test_peer_failure_surfaces_on_host_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    results = sorted(q.get(timeout=5) for _ in range(2))
+    assert results == [(0, "error"), (1, "raised")]
