@@ -17,15 +17,21 @@ larger than the 126 MB L2, so no step reuses another's weights from L2).
               vs the measured HBM copy bandwidth.
   qmv_sweep   per configuration: a CUDA graph of 24 launches over a ring of
               distinct weight copies (working set > 2x L2), CUDA events.
-  qmm_prefill config 3 at M=512 (tcgen05 QMM) in TFLOP/s vs measured bf16 peak.
+  qmm_prefill config 3 at M=512 (tcgen05 QMM) in TFLOP/s vs measured bf16 peak;
+              on one GPU also M = 16, 182, 2048 against the max(FLOP, byte)
+              roofline (``by_M``).
+  model       config 4 on one GPU: the 27B Qwen3.5-hybrid decoder with
+              random-init packed weights; prefill (182 and 512 tokens) and
+              batch-1 decode tok/s (CUDA-graph replay per token).
   cpu_baseline the reference's CPU path (gguf-py dequantize, which
               mlx_gsq/quant/reference.py:10-18 calls, + numpy matvec) on a
               bounded sample of the same workload.
 
 --gpus N (torchrun): each projection is split by output rows over the N
-ranks and the partial outputs are all-gathered with NCCL (tensor parallel,
-strong scaling: total work fixed).  --impl reference runs the CPU reference
-path only (rank 0).
+ranks (tensor parallel, strong scaling: total work fixed); the row gather is
+fused into the kernels (the matvec sends every value to each peer's inbox
+over NVLink, the matmul stores its tiles into every rank's output).
+--impl reference runs the CPU reference path only (rank 0).
 """
 from __future__ import annotations
 
@@ -177,6 +183,123 @@ def decode_tok_s(per):
     return out or None
 
 
+def qmm_by_m(dev, pk, ms=(16, 182, 2048)):
+    """Config 3 at the other token counts, one GPU: for each M, one CUDA graph
+    runs the 8 projections (4 types x 2 shapes, 369 MB of distinct packed
+    weights, > 2x L2) back to back; replayed, CUDA events.  Reported against
+    the max(FLOP, byte) roofline: bound = max(2MNK / bf16 peak, bytes / HBM
+    peak) summed over the 8 projections, bytes = packed + 2MK (bf16 x) +
+    4MN (fp32 y)."""
+    import torch
+    from gsq_b200.quant.synthetic import random_matrix_torch
+    from gsq_b200.runtime.kernels import quantized_matmul
+
+    mats = [(q, n, k, random_matrix_torch(q, n, k, seed=7, device=dev)) for q in QMM_TYPES for (n, k) in QMM_SHAPES]
+    out = []
+    for m in ms:
+        xs = {k: torch.randn(m, k, device=dev, dtype=torch.bfloat16,
+                             generator=torch.Generator(device=dev).manual_seed(11)) for k in {5120, 17408}}
+
+        def run():
+            for q, n, k, w in mats:
+                quantized_matmul(xs[k], w, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
+
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream(device=dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                for _ in range(2):
+                    run()
+        torch.cuda.current_stream(dev).wait_stream(st)
+        g.replay()
+        torch.cuda.synchronize()
+        reps = 4
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / 1e3 / (2 * reps)  # seconds per pass over the 8 projections
+        del g
+        flops = sum(2.0 * m * n * k for _, n, k, _ in mats)
+        nbytes = sum(packed_bytes(q, n, k) + 2 * m * k + 4 * m * n for q, n, k, _ in mats)
+        bound = sum(max(2.0 * m * n * k / (pk["bf16"] * 1e12), (packed_bytes(q, n, k) + 2 * m * k + 4 * m * n)
+                        / (pk["hbm"] * 1e9)) for q, n, k, _ in mats)
+        out.append({"M": m, "us_per_pass": round(t * 1e6, 1), "tflops": round(flops / t / 1e12, 1),
+                    "gbs": round(nbytes / t / 1e9, 1), "roofline_frac": round(bound / t, 4),
+                    "bound": "hbm" if nbytes / (pk["hbm"] * 1e9) > flops / (pk["bf16"] * 1e12) else "tensor"})
+        del xs
+    del mats
+    torch.cuda.empty_cache()
+    return out
+
+
+def model_bench(dev, pk, prompt=182, decode_tokens=64, prefill_m=512):
+    """Config 4 (BASELINE): the Qwen3.5-hybrid 27B decoder (64 layers) with
+    random-init packed weights of the config's type mix, one GPU.  A
+    ``prompt``-token prefill, then ``decode_tokens`` greedy decode tokens at
+    batch 1, each a replay of the captured decode-step graph (embedding ->
+    64 layers -> LM head -> argmax); and a ``prefill_m``-token prefill.
+    CUDA events around each timed region; every decode token reads all
+    packed projections (12 GB, ~90x L2)."""
+    import torch
+    from gsq_b200.models import Qwen35Config, build_qwen35, random_weights
+
+    cfg = Qwen35Config()
+    w = random_weights(cfg, dev, seed=0)
+    model = build_qwen35(w, cfg, dev, max_len=prefill_m + decode_tokens + 16)
+    del w
+    torch.cuda.empty_cache()
+    gen = torch.Generator(device=dev).manual_seed(1)
+
+    def timed(fn, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    out = {"workload": "config 4: Qwen3.5-hybrid 27B (64 layers, 48 gated-DeltaNet + 16 GQA), random-init packed "
+                       "weights (embedding/LM head Q6_K, FFN gate/up IQ2_XS|IQ2_S, down Q4_K, attention IQ3_S|IQ4_XS)",
+           "packed_bytes_per_token": model.packed_bytes_per_token()}
+    for T in (prompt, prefill_m):
+        ids = torch.randint(0, cfg.vocab_size, (T,), device=dev, generator=gen, dtype=torch.int32)
+        model.prefill(ids)  # warm-up (workspaces, cuBLAS / attention plans)
+        torch.cuda.synchronize()
+        t = timed(lambda: model.prefill(ids), 3)
+        out[f"prefill_{T}_ms"] = round(t * 1e3, 2)
+        out[f"prefill_{T}_tok_s"] = round(T / t, 1)
+
+    ids = torch.randint(0, cfg.vocab_size, (prompt,), device=dev, generator=gen, dtype=torch.int32)
+    model.prefill(ids)
+    model.decode_step()
+    model.capture_decode()
+    model.replay_decode(3)  # warm-up replays
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    model.replay_decode(decode_tokens)
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / decode_tokens
+    gbs = out["packed_bytes_per_token"] / t / 1e9
+    out.update({"decode_tokens": decode_tokens, "decode_ms_per_token": round(t * 1e3, 3),
+                "decode_tok_s": round(1.0 / t, 1), "decode_packed_gbs": round(gbs, 1),
+                "decode_roofline_frac": round(gbs / pk["hbm"], 4),
+                "decode_note": "batch 1 after the prompt prefill; each token one CUDA-graph replay of the whole "
+                               "step; roofline = packed weight bytes per token / time vs measured HBM copy peak"})
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -186,6 +309,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-qmm", action="store_true")
+    ap.add_argument("--no-model", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -436,6 +560,10 @@ def main():
                            f"; {world} ranks: row shards, the gather fused into the matmul epilogue, max over ranks, "
                            f"peak = {world} x the measured bf16 peak" if world > 1 else "")}
 
+    if qmm is not None and world == 1:
+        qmm["by_M"] = qmm_by_m(dev, pk)
+    model = model_bench(dev, pk) if world == 1 and not args.no_model else None
+
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         gbs, spent, sample = cpu_reference_sample(args.cpu_budget)
@@ -457,7 +585,7 @@ def main():
                                        f"value goes to every rank's inbox over NVLink)") if world > 1 else "single GPU",
                        "timing": "CUDA graph of one step, replayed; CUDA events"},
             "roofline": roofline, "qmv_sweep": per, "qmm_prefill": qmm, "cpu_baseline": cpu, "e2e": e2e,
-            "decode_tok_s_per_projection_pair": decode_tok_s(per),
+            "decode_tok_s_per_projection_pair": decode_tok_s(per), "model": model,
             "clocks": clocks.summary(), "gpu_launches": args.steps * len(cfgs),
         }
         print(json.dumps(line), flush=True)

@@ -1,0 +1,4 @@
+"""Model harness over the packed-weight kernels (mirrors mlx_gsq/models)."""
+from .qwen35 import Qwen35, Qwen35Config, build_qwen35, default_type_mix, random_weights, tensor_shapes
+
+__all__ = ["Qwen35", "Qwen35Config", "build_qwen35", "default_type_mix", "random_weights", "tensor_shapes"]

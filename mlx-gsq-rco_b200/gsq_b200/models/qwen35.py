@@ -1,0 +1,440 @@
+"""Qwen3.5-hybrid decoder over packed GGUF weights (the model harness).
+
+The reference attaches packed weights to mlx_lm's Qwen3.5 model
+(``mlx_gsq/models/qwen35.py:11-152``): 64 decoder layers at hidden 5120,
+every 4th layer gated GQA attention (24 query heads, 4 key/value heads of
+256), the others gated-DeltaNet linear attention (16 key heads and 48 value
+heads of 128, value head h reading key head h % 16, ``qwen35.py:87-94``),
+SwiGLU FFN 17408, vocab 248320.  Here the same model runs on B200:
+
+  * every quantized projection is a packed-weight kernel call
+    (``quantized_matvec``: the fused dequant-matvec for fewer than 8 token
+    rows, the tcgen05 dequant-matmul above), with fp16 activations in and
+    fp32 out;
+  * the projections of a layer that read the same input and share a quant
+    type are joined row-wise at load time (ffn_gate|ffn_up,
+    attn_qkv|attn_gate, attn_q|attn_k|attn_v): a packed matrix is rows of
+    whole blocks, so the join is a byte concatenation and each layer makes
+    fewer, larger calls;
+  * the work between projections is in ``include/gsq_model.h``: residual
+    add + RMSNorm, SiLU-mul, the gated-DeltaNet block (conv, norms, gates,
+    recurrence, gated norm) and the single-token attention step; prefill
+    attention uses torch's scaled-dot-product attention;
+  * a decode step (embedding gather -> 64 layers -> LM head -> argmax ->
+    next id) reads its token and position from device buffers, so it is
+    captured once as a CUDA graph and replayed per token.
+
+GGUF tensor names and the A_log convention follow ``qwen35.py:104-152``
+(``ssm_a`` holds -exp(A_log), ``qwen35.py:43-45``).  mlx_lm's Qwen3.5 and
+gated-delta sources are not part of the reference repository; the formulas
+used are written in ``include/gsq_model.h``.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .. import _lib
+from ..runtime.kernels import packed_embedding, quantized_matvec
+from ..runtime.store import PackedWeight
+
+
+@dataclass(frozen=True)
+class Qwen35Config:
+    """Model dimensions (``qwen35.py:11-36``)."""
+    hidden_size: int = 5120
+    intermediate_size: int = 17408
+    num_hidden_layers: int = 64
+    num_attention_heads: int = 24
+    num_key_value_heads: int = 4
+    head_dim: int = 256
+    vocab_size: int = 248320
+    rms_norm_eps: float = 1e-6
+    linear_num_value_heads: int = 48
+    linear_num_key_heads: int = 16
+    linear_key_head_dim: int = 128
+    linear_value_head_dim: int = 128
+    linear_conv_kernel_dim: int = 4
+    full_attention_interval: int = 4
+    rope_theta: float = 10_000_000.0
+    partial_rotary_factor: float = 0.25
+
+    def is_linear(self, i: int) -> bool:
+        return (i + 1) % self.full_attention_interval != 0
+
+    @property
+    def rotary_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary_factor)
+
+    @property
+    def gdn_conv_dim(self) -> int:
+        return 2 * self.linear_num_key_heads * self.linear_key_head_dim + \
+            self.linear_num_value_heads * self.linear_value_head_dim
+
+    def check(self) -> None:
+        if self.linear_key_head_dim != 128 or self.linear_value_head_dim != 128 or self.head_dim != 256:
+            raise ValueError("the harness kernels need 128-wide linear-attention heads and 256-wide attention heads")
+        if self.linear_conv_kernel_dim != 4:
+            raise ValueError("the conv kernel width must be 4")
+        if self.linear_num_value_heads % self.linear_num_key_heads or \
+                self.num_attention_heads % self.num_key_value_heads:
+            raise ValueError("head counts must divide")
+
+
+def tensor_shapes(cfg: Qwen35Config) -> dict[str, tuple[int, ...]]:
+    """Logical shapes (out, in) of every GGUF tensor of the model, by name."""
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    nq, nkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+    nv, dv = cfg.linear_num_value_heads, cfg.linear_value_head_dim
+    s = {"token_embd.weight": (cfg.vocab_size, H), "output_norm.weight": (H,), "output.weight": (cfg.vocab_size, H)}
+    for i in range(cfg.num_hidden_layers):
+        p = f"blk.{i}."
+        s[p + "attn_norm.weight"] = (H,)
+        s[p + "post_attention_norm.weight"] = (H,)
+        s[p + "ffn_gate.weight"] = (I, H)
+        s[p + "ffn_up.weight"] = (I, H)
+        s[p + "ffn_down.weight"] = (H, I)
+        if cfg.is_linear(i):
+            s[p + "attn_qkv.weight"] = (cfg.gdn_conv_dim, H)
+            s[p + "attn_gate.weight"] = (nv * dv, H)
+            s[p + "ssm_out.weight"] = (H, nv * dv)
+            s[p + "ssm_alpha.weight"] = (nv, H)
+            s[p + "ssm_beta.weight"] = (nv, H)
+            s[p + "ssm_conv1d.weight"] = (cfg.gdn_conv_dim, cfg.linear_conv_kernel_dim)
+            s[p + "ssm_a"] = (nv,)
+            s[p + "ssm_dt.bias"] = (nv,)
+            s[p + "ssm_norm.weight"] = (dv,)
+        else:
+            s[p + "attn_q.weight"] = (2 * nq * hd, H)
+            s[p + "attn_k.weight"] = (nkv * hd, H)
+            s[p + "attn_v.weight"] = (nkv * hd, H)
+            s[p + "attn_output.weight"] = (H, nq * hd)
+            s[p + "attn_q_norm.weight"] = (hd,)
+            s[p + "attn_k_norm.weight"] = (hd,)
+    return s
+
+
+def default_type_mix(cfg: Qwen35Config) -> dict[str, str]:
+    """Quant type per packed tensor: embedding and LM head
+    Q6_K; FFN gate/up IQ2_XS on even layers, IQ2_S on odd ones; FFN down
+    Q4_K; attention and linear-attention projections IQ3_S on even layers,
+    IQ4_XS on odd ones.  ssm_alpha / ssm_beta, norms, conv taps and gates
+    stay plain (F32)."""
+    mix = {"token_embd.weight": "Q6_K", "output.weight": "Q6_K"}
+    for i in range(cfg.num_hidden_layers):
+        p = f"blk.{i}."
+        mix[p + "ffn_gate.weight"] = mix[p + "ffn_up.weight"] = "IQ2_XS" if i % 2 == 0 else "IQ2_S"
+        mix[p + "ffn_down.weight"] = "Q4_K"
+        att = "IQ3_S" if i % 2 == 0 else "IQ4_XS"
+        names = ("attn_qkv", "attn_gate", "ssm_out") if cfg.is_linear(i) else \
+            ("attn_q", "attn_k", "attn_v", "attn_output")
+        for n in names:
+            mix[p + n + ".weight"] = att
+    return mix
+
+
+def random_weights(cfg: Qwen35Config, device, seed: int = 0, type_mix: dict[str, str] | None = None) -> dict:
+    """Random-init weights of the model by GGUF name: packed tensors as
+    ``PackedWeight`` (the synthetic generator of the benchmarks: uniform
+    bytes, fp16 super-block scales in [1e-4, 4e-3]), plain tensors as fp32
+    CUDA tensors (norm weights near 1, conv taps, gates)."""
+    from ..quant.synthetic import random_matrix_torch
+    cfg.check()
+    mix = type_mix or default_type_mix(cfg)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    out = {}
+    for idx, (name, shape) in enumerate(tensor_shapes(cfg).items()):
+        if name in mix:
+            data = random_matrix_torch(mix[name], shape[0], shape[1], seed=seed * 100003 + idx, device=device)
+            out[name] = PackedWeight.from_packed(name, data, mix[name], shape, device=None)
+            continue
+
+        def rnd(scale, offset=0.0):
+            return torch.randn(shape, device=device, generator=gen) * scale + offset
+
+        if name.endswith("norm.weight"):
+            out[name] = rnd(0.05, 1.0)
+        elif name.endswith("ssm_conv1d.weight"):
+            out[name] = rnd(0.3)
+        elif name.endswith("ssm_alpha.weight") or name.endswith("ssm_beta.weight"):
+            out[name] = rnd(1.0 / math.sqrt(shape[1]))
+        elif name.endswith("ssm_a"):
+            out[name] = -torch.exp(torch.rand(shape, device=device, generator=gen) * 2.0)
+        elif name.endswith("ssm_dt.bias"):
+            out[name] = rnd(0.5)
+        else:
+            raise KeyError(name)
+    return out
+
+
+class _Packed:
+    """A packed projection: flat uint8 payload of n rows x k inputs."""
+
+    def __init__(self, parts: list[PackedWeight]):
+        q = {p.quantization_type for p in parts}
+        k = {p.logical_shape[1] for p in parts}
+        if len(q) != 1 or len(k) != 1:
+            raise ValueError("joined projections must share quant type and input width: "
+                             + ", ".join(p.name for p in parts))
+        self.qtype, self.k = q.pop(), k.pop()
+        self.n = sum(p.logical_shape[0] for p in parts)
+        self.data = parts[0].data if len(parts) == 1 else torch.cat([p.data.reshape(-1) for p in parts])
+        self.nbytes = self.data.numel()
+
+    def __call__(self, x16: torch.Tensor) -> torch.Tensor:
+        return quantized_matvec(x16, self.data, qtype=self.qtype, out_features=self.n, in_features=self.k,
+                                out_dtype=torch.float32)
+
+
+def _stream(dev):
+    return _lib.stream_ptr(dev)
+
+
+def rmsnorm(resid: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, eps: float,
+            out_dtype=torch.float16) -> torch.Tensor:
+    """resid += delta (in place, when given); returns rmsnorm(resid) * weight."""
+    rows, dim = resid.shape
+    out = torch.empty((rows, dim), dtype=out_dtype, device=resid.device)
+    _lib.check(_lib.load().gsq_rmsnorm(resid.data_ptr(), delta.data_ptr() if delta is not None else None, rows, dim,
+                                       weight.data_ptr(), eps, out.data_ptr(), _lib.DTYPE_CODES[out_dtype],
+                                       _stream(resid.device)))
+    return out
+
+
+def silu_mul(gu: torch.Tensor, out_dtype=torch.float16) -> torch.Tensor:
+    rows, n2 = gu.shape
+    out = torch.empty((rows, n2 // 2), dtype=out_dtype, device=gu.device)
+    _lib.check(_lib.load().gsq_silu_mul(gu.data_ptr(), rows, n2 // 2, out.data_ptr(), _lib.DTYPE_CODES[out_dtype],
+                                        _stream(gu.device)))
+    return out
+
+
+class Qwen35:
+    """The model on one GPU, built from GGUF-named weights (``build_qwen35``)."""
+
+    def __init__(self, weights: dict, cfg: Qwen35Config, device, max_len: int = 2304):
+        cfg.check()
+        self.cfg, self.dev, self.max_len = cfg, torch.device(device), max_len
+        self.eps = cfg.rms_norm_eps
+        w = weights
+        self.embed = w["token_embd.weight"]
+        self.out_norm = w["output_norm.weight"].float().contiguous()
+        self.lm_head = _Packed([w["output.weight"]])
+        nv = cfg.linear_num_value_heads
+        nkv, hd = cfg.num_key_value_heads, cfg.head_dim
+        self.layers = []
+        for i in range(cfg.num_hidden_layers):
+            p = f"blk.{i}."
+            L = {"linear": cfg.is_linear(i),
+                 "attn_norm": w[p + "attn_norm.weight"].float().contiguous(),
+                 "post_norm": w[p + "post_attention_norm.weight"].float().contiguous(),
+                 "gate_up": _Packed([w[p + "ffn_gate.weight"], w[p + "ffn_up.weight"]]),
+                 "down": _Packed([w[p + "ffn_down.weight"]])}
+            if L["linear"]:
+                L["qkvz"] = _Packed([w[p + "attn_qkv.weight"], w[p + "attn_gate.weight"]])
+                L["out"] = _Packed([w[p + "ssm_out.weight"]])
+                L["ab"] = torch.cat([w[p + "ssm_alpha.weight"], w[p + "ssm_beta.weight"]]).to(torch.float16)
+                L["conv_w"] = w[p + "ssm_conv1d.weight"].float().reshape(cfg.gdn_conv_dim, 4).contiguous()
+                L["A"] = w[p + "ssm_a"].float().contiguous()
+                L["dt_bias"] = w[p + "ssm_dt.bias"].float().contiguous()
+                L["norm"] = w[p + "ssm_norm.weight"].float().contiguous()
+                L["conv_state"] = torch.zeros(3, cfg.gdn_conv_dim, device=self.dev)
+                L["state"] = torch.zeros(nv, cfg.linear_value_head_dim, cfg.linear_key_head_dim, device=self.dev)
+            else:
+                L["qkv"] = _Packed([w[p + "attn_q.weight"], w[p + "attn_k.weight"], w[p + "attn_v.weight"]])
+                L["o"] = _Packed([w[p + "attn_output.weight"]])
+                L["q_norm"] = w[p + "attn_q_norm.weight"].float().contiguous()
+                L["k_norm"] = w[p + "attn_k_norm.weight"].float().contiguous()
+                L["k_cache"] = torch.zeros(max_len, nkv, hd, device=self.dev)
+                L["v_cache"] = torch.zeros(max_len, nkv, hd, device=self.dev)
+            self.layers.append(L)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=self.dev)   # next position (decode)
+        self.cur_id = torch.zeros(1, dtype=torch.int32, device=self.dev)  # token to feed next (decode)
+        self.n_pos = 0  # host copy of the position (prefill bookkeeping)
+        self._graph = None
+        inv = cfg.rope_theta ** (-torch.arange(0, cfg.rotary_dim, 2, dtype=torch.float32) / cfg.rotary_dim)
+        self._inv_freq = inv.to(self.dev)
+
+    # ---- sizes ----
+    def packed_bytes_per_token(self) -> int:
+        """Packed weight bytes one decode token reads (every projection and
+        the LM head; one embedding row)."""
+        total = self.lm_head.nbytes + self.embed.num_bytes // self.cfg.vocab_size
+        for L in self.layers:
+            for key in ("gate_up", "down", "qkvz", "out", "qkv", "o"):
+                if key in L:
+                    total += L[key].nbytes
+        return total
+
+    def reset(self) -> None:
+        for L in self.layers:
+            if L["linear"]:
+                L["conv_state"].zero_()
+                L["state"].zero_()
+        self.pos.zero_()
+        self.n_pos = 0
+
+    # ---- blocks ----
+    def _gdn(self, L, p: torch.Tensor, ab: torch.Tensor) -> torch.Tensor:
+        cfg, T = self.cfg, p.shape[0]
+        nk, nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
+        lib = _lib.load()
+        need = lib.gsq_gdn_scratch_bytes(T, nk, nv)
+        scratch = torch.empty(need, dtype=torch.uint8, device=self.dev)
+        out = torch.empty(T, nv * cfg.linear_value_head_dim, dtype=torch.float16, device=self.dev)
+        _lib.check(lib.gsq_gdn(p.data_ptr(), p.stride(0), ab.data_ptr(), ab.stride(0), T, nk, nv,
+                               L["conv_state"].data_ptr(), L["conv_w"].data_ptr(), L["A"].data_ptr(),
+                               L["dt_bias"].data_ptr(), L["norm"].data_ptr(), self.eps, L["state"].data_ptr(),
+                               scratch.data_ptr(), need, out.data_ptr(), _lib.DTYPE_CODES[torch.float16],
+                               _stream(self.dev)))
+        return out
+
+    def _rope(self, x: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        rot = self.cfg.rotary_dim
+        ang = pos.float()[:, None] * self._inv_freq[None, :]
+        cos, sin = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+        x1, x2 = x[..., :rot // 2], x[..., rot // 2:rot]
+        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin, x[..., rot:]], dim=-1)
+
+    def _attn_prefill(self, L, p: torch.Tensor, pos0: int) -> torch.Tensor:
+        cfg, T = self.cfg, p.shape[0]
+        nq, nkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        if pos0 != 0:
+            raise NotImplementedError("multi-token calls start at position 0 (prefill of an empty cache)")
+        qg = p[:, :nq * 2 * hd].reshape(T, nq, 2 * hd)
+        q, gate = qg[..., :hd], qg[..., hd:]
+        k = p[:, nq * 2 * hd:nq * 2 * hd + nkv * hd].reshape(T, nkv, hd)
+        v = p[:, nq * 2 * hd + nkv * hd:].reshape(T, nkv, hd)
+        q = F.rms_norm(q, (hd,), L["q_norm"], self.eps)
+        k = F.rms_norm(k, (hd,), L["k_norm"], self.eps)
+        pos = torch.arange(pos0, pos0 + T, device=self.dev)
+        q, k = self._rope(q, pos), self._rope(k, pos)
+        L["k_cache"][pos0:pos0 + T] = k
+        L["v_cache"][pos0:pos0 + T] = v
+        att = F.scaled_dot_product_attention(q.transpose(0, 1)[None].to(torch.float16),
+                                             k.transpose(0, 1)[None].to(torch.float16),
+                                             v.transpose(0, 1)[None].to(torch.float16), is_causal=True,
+                                             enable_gqa=True, scale=1.0 / math.sqrt(hd))
+        o = att[0].transpose(0, 1).float() * torch.sigmoid(gate)
+        return o.reshape(T, nq * hd).to(torch.float16)
+
+    def _attn_decode(self, L, p: torch.Tensor) -> torch.Tensor:
+        cfg = self.cfg
+        nq, nkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        out = torch.empty(1, nq * hd, dtype=torch.float16, device=self.dev)
+        _lib.check(_lib.load().gsq_attn_decode(p.data_ptr(), nq, nkv, L["q_norm"].data_ptr(),
+                                               L["k_norm"].data_ptr(), self.eps, cfg.rotary_dim, cfg.rope_theta,
+                                               L["k_cache"].data_ptr(), L["v_cache"].data_ptr(), self.max_len,
+                                               self.pos.data_ptr(), out.data_ptr(),
+                                               _lib.DTYPE_CODES[torch.float16], _stream(self.dev)))
+        return out
+
+    def _layers(self, x: torch.Tensor, pos0: int | None) -> torch.Tensor:
+        """Runs every layer over x (fp32 residual rows, updated in place);
+        returns the last layer's FFN output (the pending residual delta).
+        pos0 None = a decode token at the device position."""
+        delta = None
+        for L in self.layers:
+            h = rmsnorm(x, delta, L["attn_norm"], self.eps)
+            if L["linear"]:
+                p = L["qkvz"](h)
+                ab = F.linear(h, L["ab"])
+                d = L["out"](self._gdn(L, p, ab))
+            else:
+                p = L["qkv"](h)
+                o = self._attn_decode(L, p) if pos0 is None else self._attn_prefill(L, p, pos0)
+                d = L["o"](o)
+            h2 = rmsnorm(x, d, L["post_norm"], self.eps)
+            delta = L["down"](silu_mul(L["gate_up"](h2)))
+        return delta
+
+    # ---- public ----
+    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
+        """Runs a prompt from position 0 (the caches are reset); returns the
+        last token's logits (fp32, vocab) and sets the next token to their
+        argmax."""
+        self.reset()
+        cfg, T = self.cfg, ids.numel()
+        if T > self.max_len:
+            raise ValueError("prompt longer than the cache")
+        x = packed_embedding(ids.reshape(-1).to(self.dev), self.embed.data, qtype=self.embed.quantization_type,
+                             vocab_size=cfg.vocab_size, dimensions=cfg.hidden_size, dtype=torch.float32)
+        x = x.reshape(T, cfg.hidden_size).contiguous()
+        delta = self._layers(x, 0)
+        last = x[T - 1:].clone()
+        hf = rmsnorm(last, delta[T - 1:].contiguous(), self.out_norm, self.eps)
+        logits = self.lm_head(hf)[0]
+        self.cur_id.copy_(torch.argmax(logits).to(torch.int32).reshape(1))
+        self.pos.fill_(T)
+        self.n_pos = T
+        return logits
+
+    def _decode_body(self) -> torch.Tensor:
+        cfg = self.cfg
+        x = packed_embedding(self.cur_id, self.embed.data, qtype=self.embed.quantization_type,
+                             vocab_size=cfg.vocab_size, dimensions=cfg.hidden_size, dtype=torch.float32)
+        x = x.reshape(1, cfg.hidden_size)
+        delta = self._layers(x, None)
+        hf = rmsnorm(x, delta, self.out_norm, self.eps)
+        logits = self.lm_head(hf)
+        self.cur_id.copy_(torch.argmax(logits, dim=-1).to(torch.int32))
+        self.pos.add_(1)
+        return logits
+
+    def decode_step(self, token: int | None = None) -> torch.Tensor:
+        """One decode token, eagerly: feeds ``token`` (default: the argmax of
+        the previous step) at the current position; returns the logits
+        (1 x vocab, fp32)."""
+        if self.n_pos >= self.max_len:
+            raise ValueError("cache full")
+        if token is not None:
+            self.cur_id.fill_(int(token))
+        logits = self._decode_body()
+        self.n_pos += 1
+        return logits
+
+    def capture_decode(self) -> None:
+        """Captures one decode step as a CUDA graph (run one eager step
+        first: it sizes the library workspaces, and advances the position)."""
+        st = torch.cuda.Stream(device=self.dev)
+        st.wait_stream(torch.cuda.current_stream(self.dev))
+        g = torch.cuda.CUDAGraph()
+        saved = [(L["conv_state"].clone(), L["state"].clone()) for L in self.layers if L["linear"]]
+        pos, cur = self.pos.clone(), self.cur_id.clone()
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                self._graph_logits = self._decode_body()
+        torch.cuda.current_stream(self.dev).wait_stream(st)
+        # Capture does not execute; restore anyway in case a kernel ran eagerly.
+        it = iter(saved)
+        for L in self.layers:
+            if L["linear"]:
+                cs, s = next(it)
+                L["conv_state"].copy_(cs)
+                L["state"].copy_(s)
+        self.pos.copy_(pos)
+        self.cur_id.copy_(cur)
+        self._graph = g
+
+    def replay_decode(self, n: int = 1) -> None:
+        """n decode tokens through the captured graph (greedy)."""
+        if self._graph is None:
+            raise RuntimeError("capture_decode() first")
+        if self.n_pos + n > self.max_len:
+            raise ValueError("cache full")
+        for _ in range(n):
+            self._graph.replay()
+        self.n_pos += n
+
+    @property
+    def graph_logits(self) -> torch.Tensor:
+        return self._graph_logits
+
+
+def build_qwen35(weights: dict, cfg: Qwen35Config | None = None, device="cuda", max_len: int = 2304) -> Qwen35:
+    """The model from GGUF-named weights (``qwen35.py:104-152``): packed
+    projections as ``PackedWeight`` on the device, plain tensors as arrays."""
+    return Qwen35(weights, cfg or Qwen35Config(), device, max_len=max_len)

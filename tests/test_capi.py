@@ -1,6 +1,6 @@
-"""The C-ABI library loads, exports every entry point include/gsq_b200.h
-declares, and validates arguments before touching the GPU (these calls only
-exercise host-side validation; no kernel is launched)."""
+"""The C-ABI library loads, exports every entry point include/gsq_b200.h and
+include/gsq_model.h declare, and validates arguments before touching the GPU
+(these calls only exercise host-side validation; no kernel is launched)."""
 import ctypes
 import os
 import re
@@ -10,12 +10,15 @@ import pytest
 from gsq_b200 import _lib
 from gsq_b200.quant.layouts import QUANT_BLOCK_SIZES, SUPPORTED_QUANT_TYPES, type_id
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "gsq_b200.h")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+HEADERS = [os.path.join(INCLUDE, h) for h in ("gsq_b200.h", "gsq_model.h")]
 
 
 def declared_functions():
-    src = open(HEADER).read()
-    return re.findall(r"GSQ_API\s+[\w\s\*]+?\b(gsq_\w+)\s*\(", src)
+    names = []
+    for h in HEADERS:
+        names += re.findall(r"GSQ_API\s+[\w\s\*]+?\b(gsq_\w+)\s*\(", open(h).read())
+    return names
 
 
 def test_header_declares_the_abi():

@@ -1,0 +1,161 @@
+"""Qwen3.5-hybrid harness against a plain fp32 PyTorch restatement of the
+same model (a reduced configuration with the real head widths: 3 gated-DeltaNet
+layers and 1 attention layer).
+
+The reference below decodes every packed tensor bit-exactly (``decode``),
+runs the model one token at a time in fp32 (dense projections, the
+delta-rule recurrence written out per head, attention over the cache), and
+is compared with the harness's prefill (tcgen05 matmul + torch attention),
+its eager decode steps (fused matvec + the decode kernels) and its captured
+CUDA-graph decode.  mlx_lm's model sources are not in the reference
+repository, so the formulas are the ones written in include/gsq_model.h.
+"""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from gsq_b200.models import Qwen35Config, build_qwen35, random_weights
+from gsq_b200.runtime.kernels import decode
+
+pytestmark = pytest.mark.gpu
+
+CFG = Qwen35Config(hidden_size=512, intermediate_size=768, num_hidden_layers=4, num_attention_heads=4,
+                   num_key_value_heads=2, vocab_size=512, linear_num_value_heads=4, linear_num_key_heads=2)
+TOL = 2e-2  # rel-L2 of logits: fp16 activations between projections + 16-bit activation quantisation
+
+
+def rel(a, b):
+    return float((a.float() - b.float()).norm() / b.float().norm())
+
+
+class Reference:
+    """fp32, token by token."""
+
+    def __init__(self, w, cfg, dev):
+        self.cfg, self.w, self.dev = cfg, {}, dev
+        for name, t in w.items():
+            if hasattr(t, "quantization_type"):
+                self.w[name] = decode(t.data, t.quantization_type).reshape(t.logical_shape).float()
+            else:
+                self.w[name] = t.float()
+        c = cfg
+        self.conv = {i: torch.zeros(3, c.gdn_conv_dim, device=dev) for i in range(c.num_hidden_layers)
+                     if c.is_linear(i)}
+        self.S = {i: torch.zeros(c.linear_num_value_heads, 128, 128, device=dev) for i in self.conv}
+        self.K = {i: [] for i in range(c.num_hidden_layers) if not c.is_linear(i)}
+        self.V = {i: [] for i in self.K}
+        self.pos = 0
+
+    @staticmethod
+    def norm(x, w, eps):
+        return x * torch.rsqrt((x * x).mean(-1, keepdim=True) + eps) * (w if w is not None else 1.0)
+
+    def rope(self, x, pos):
+        c = self.cfg
+        rot = c.rotary_dim
+        i = torch.arange(rot // 2, device=self.dev, dtype=torch.float64)
+        ang = (pos * c.rope_theta ** (-2.0 * i / rot)).float()
+        x1, x2 = x[..., :rot // 2], x[..., rot // 2:rot]
+        return torch.cat([x1 * ang.cos() - x2 * ang.sin(), x2 * ang.cos() + x1 * ang.sin(), x[..., rot:]], -1)
+
+    def step(self, tok):
+        c, w, eps = self.cfg, self.w, self.cfg.rms_norm_eps
+        x = w["token_embd.weight"][tok].clone()
+        for i in range(c.num_hidden_layers):
+            p = f"blk.{i}."
+            h = self.norm(x, w[p + "attn_norm.weight"], eps)
+            if c.is_linear(i):
+                nk, nv = c.linear_num_key_heads, c.linear_num_value_heads
+                qkv = w[p + "attn_qkv.weight"] @ h
+                z = (w[p + "attn_gate.weight"] @ h).reshape(nv, 128)
+                a = w[p + "ssm_alpha.weight"] @ h
+                b = w[p + "ssm_beta.weight"] @ h
+                win = torch.cat([self.conv[i], qkv[None]], 0)  # 4 x C, oldest first
+                self.conv[i] = win[1:]
+                cv = F.silu((win.T * w[p + "ssm_conv1d.weight"]).sum(-1))
+                q = cv[:nk * 128].reshape(nk, 128)
+                k = cv[nk * 128:2 * nk * 128].reshape(nk, 128)
+                v = cv[2 * nk * 128:].reshape(nv, 128)
+                q = self.norm(q, None, 1e-6) / 128.0
+                k = self.norm(k, None, 1e-6) / math.sqrt(128.0)
+                g = torch.exp(w[p + "ssm_a"] * F.softplus(a + w[p + "ssm_dt.bias"]))
+                beta = torch.sigmoid(b)
+                o = torch.empty(nv, 128, device=self.dev)
+                for hh in range(nv):
+                    kh = hh % nk
+                    S = self.S[i][hh] * g[hh]             # [v index, k index]
+                    u = (v[hh] - S @ k[kh]) * beta[hh]
+                    S = S + u[:, None] * k[kh][None, :]
+                    self.S[i][hh] = S
+                    o[hh] = S @ q[kh]
+                o = self.norm(o, w[p + "ssm_norm.weight"], eps) * F.silu(z)
+                d = w[p + "ssm_out.weight"] @ o.reshape(-1)
+            else:
+                nq, nkv, hd = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+                qg = (w[p + "attn_q.weight"] @ h).reshape(nq, 2 * hd)
+                q, gate = qg[:, :hd], qg[:, hd:]
+                k = (w[p + "attn_k.weight"] @ h).reshape(nkv, hd)
+                v = (w[p + "attn_v.weight"] @ h).reshape(nkv, hd)
+                q = self.rope(self.norm(q, w[p + "attn_q_norm.weight"], eps), self.pos)
+                k = self.rope(self.norm(k, w[p + "attn_k_norm.weight"], eps), self.pos)
+                self.K[i].append(k)
+                self.V[i].append(v)
+                Ks, Vs = torch.stack(self.K[i]), torch.stack(self.V[i])  # [t, nkv, hd]
+                o = torch.empty(nq, hd, device=self.dev)
+                for hh in range(nq):
+                    kv = hh // (nq // nkv)
+                    pr = torch.softmax(Ks[:, kv] @ q[hh] / math.sqrt(hd), 0)
+                    o[hh] = (pr[:, None] * Vs[:, kv]).sum(0) * torch.sigmoid(gate[hh])
+                d = w[p + "attn_output.weight"] @ o.reshape(-1)
+            x = x + d
+            h2 = self.norm(x, w[p + "post_attention_norm.weight"], eps)
+            gu = F.silu(w[p + "ffn_gate.weight"] @ h2) * (w[p + "ffn_up.weight"] @ h2)
+            x = x + w[p + "ffn_down.weight"] @ gu
+        self.pos += 1
+        return w["output.weight"] @ self.norm(x, w["output_norm.weight"], eps)
+
+
+@pytest.fixture(scope="module")
+def setup():
+    dev = torch.device("cuda:0")
+    w = random_weights(CFG, dev, seed=3)
+    return dev, w
+
+
+@pytest.mark.parametrize("T", [12, 3])  # tiled matmul prefill (rows >= 8) and the fused matvec (rows < 8)
+def test_prefill_then_decode_matches_reference(setup, T):
+    dev, w = setup
+    model = build_qwen35(w, CFG, dev, max_len=64)
+    ref = Reference(w, CFG, dev)
+    g = torch.Generator().manual_seed(5)
+    prompt = torch.randint(0, CFG.vocab_size, (T,), generator=g)
+    for t in prompt.tolist():
+        rl = ref.step(t)
+    logits = model.prefill(prompt.to(torch.int32).to(dev))
+    e = rel(logits, rl)
+    assert e <= TOL, f"prefill rel-L2 {e}"
+    for t in torch.randint(0, CFG.vocab_size, (4,), generator=g).tolist():
+        rl = ref.step(t)
+        ml = model.decode_step(t)[0]
+        e = rel(ml, rl)
+        assert e <= TOL, f"decode rel-L2 {e}"
+    torch.cuda.synchronize()
+
+
+def test_graph_decode_matches_eager(setup):
+    dev, w = setup
+    prompt = torch.arange(9, dtype=torch.int32, device=dev) * 37 % CFG.vocab_size
+    model = build_qwen35(w, CFG, dev, max_len=64)
+    model.prefill(prompt)
+    eager = [model.decode_step()[0].clone() for _ in range(5)]
+    model.prefill(prompt)
+    model.decode_step()
+    model.capture_decode()
+    for i in range(1, 5):
+        model.replay_decode(1)
+        e = rel(model.graph_logits[0], eager[i])
+        assert e <= 1e-5, f"graph step {i}: rel {e}"
+    assert model.n_pos == 9 + 5
+    torch.cuda.synchronize()
