@@ -42,13 +42,19 @@ GSQ_API int gsq_silu_mul(const float* gu, int64_t rows, int64_t n, void* out, in
  *   proj   [T, proj_stride] fp32: columns [0, C) the q|k|v projection
  *          (C = 2*nk*128 + nv*128), columns [C, C + nv*128) the gate z
  *   ab     [T, ab_stride] fp16: columns [0, nv) the decay input a,
- *          [nv, 2nv) the write-gate input b
- *   conv_state [3, C] fp32: the three previous q|k|v inputs, oldest first
- *          (zeros at the start of a sequence); advanced by T tokens
+ *          [nv, 2nv) the write-gate input b; or NULL, and then the kernel
+ *          computes them from x [T, x_stride] fp16 (the layer's normalised
+ *          input) and ab_w [2nv, hidden] fp16 (ssm_alpha rows, then
+ *          ssm_beta rows) -- one launch fewer for a decode token
+ *   conv_state [4, C] fp32: ring of the previous q|k|v inputs, slot p & 3
+ *          holding position p's (zeros at the start of a sequence); the T
+ *          tokens' inputs are written to their slots
+ *   pos    device int32: position of the first of the T tokens
  *   conv_w [C, 4] fp32 depthwise causal taps; A [nv] = -exp(A_log)
  *          (GGUF's ssm_a); dt_bias [nv]; norm_w [128]
  *   state  [nv, 128 (value index j), 128 (key index i)] fp32, updated
- *   scratch  >= gsq_gdn_scratch_bytes(T, nk, nv) bytes
+ *   scratch  >= gsq_gdn_scratch_bytes(T, nk, nv) bytes (none for T == 1:
+ *          one token runs as a single kernel, a CTA per value head)
  *   out    [T, nv*128] in out_dtype
  *
  * Per token: c = silu(conv(q|k|v)); q = rmsnorm(c_q)/128,
@@ -57,8 +63,9 @@ GSQ_API int gsq_silu_mul(const float* gu, int64_t rows, int64_t n, void* out, in
  * S <- g*S; u = (v - S k) * beta; S <- S + u k^T; o = S q;
  * out = rmsnorm(o) * norm_w * silu(z) (eps). */
 GSQ_API size_t gsq_gdn_scratch_bytes(int64_t T, int64_t nk, int64_t nv);
-GSQ_API int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t ab_stride, int64_t T,
-                    int64_t nk, int64_t nv, float* conv_state, const float* conv_w, const float* A,
+GSQ_API int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t ab_stride,
+                    const uint16_t* x, int64_t x_stride, const uint16_t* ab_w, int64_t hidden, int64_t T,
+                    int64_t nk, int64_t nv, float* conv_state, const int32_t* pos, const float* conv_w, const float* A,
                     const float* dt_bias, const float* norm_w, float eps, float* state, void* scratch,
                     size_t scratch_bytes, void* out, int out_dtype, gsq_stream_t stream);
 

@@ -1,9 +1,9 @@
 // Decoder-glue kernels of the Qwen3.5-hybrid model harness (include/gsq_model.h):
 // the work between the packed projections of one decoder layer.
 //
-//  * rmsnorm_kernel: one CTA per row; the residual add is fused in (the
-//    projection that produced `delta` writes fp32, the next projection reads
-//    the normalised row as 16-bit).
+//  * rmsnorm_vec_kernel: one CTA per row, the row held in registers; the
+//    residual add is fused in (the projection that produced `delta` writes
+//    fp32, the next projection reads the normalised row as 16-bit).
 //  * gated-DeltaNet, three launches per layer call:
 //      gdn_prep_kernel  (T x (nk + nv) CTAs of 128 threads): causal conv of
 //                       one head's q|k (or v) channels over the last four
@@ -20,6 +20,10 @@
 //                       while the current one is applied: one barrier per
 //                       token.  The same launch advances the conv window;
 //      gdn_norm_kernel  (T x nv CTAs): gated RMSNorm of each head's output.
+//  * Every kernel is launched with programmatic dependent launch: it lets the
+//    next kernel of the stream start (a matvec's weight stream overlaps it),
+//    loads only static weights before griddepcontrol.wait, and everything
+//    the previous kernels wrote after it.
 //  * attn_decode_kernel: one CTA per query head for a single token; the CTA
 //    normalises and rotates its own key (the first query head of each group
 //    also stores it), so no CTA reads a cache row another CTA is writing.
@@ -29,6 +33,7 @@
 #include <cstdio>
 
 #include "gsq_common.cuh"
+#include "gsq_host.h"
 #include "../../include/gsq_model.h"
 
 namespace gsq {
@@ -42,6 +47,7 @@ namespace {
 constexpr int GDN_D = 128;      // gated-DeltaNet key / value head width
 constexpr int GDN_COLS = 16;    // value columns per scan CTA
 constexpr int ATT_D = 256;      // attention head width
+constexpr int ATT_U = 8;        // key positions per warp step of the decode attention
 
 __device__ __forceinline__ float silu(float v) { return v / (1.f + __expf(-v)); }
 
@@ -70,9 +76,81 @@ __device__ float block_max(float v, float* red) {
   return s;
 }
 
-__global__ void __launch_bounds__(256) rmsnorm_kernel(float* resid, const float* delta, int64_t dim, const float* w,
-                                                      float eps, void* out, int dt) {
+// Rows of up to RMS_MAXV float4 per thread x 256 threads (dim <= 8192): the
+// whole row is loaded into registers before anything is stored, so every
+// load of the row is in flight at once (a loop that stores the residual
+// between loads waits for each load in turn).
+constexpr int RMS_THREADS = 256, RMS_MAXV = 8;
+
+__global__ void __launch_bounds__(RMS_THREADS) rmsnorm_vec_kernel(float* __restrict__ resid,
+                                                                 const float* __restrict__ delta, int dim,
+                                                                 const float* __restrict__ w, float eps,
+                                                                 void* __restrict__ out, int dt) {
   __shared__ float red[32];
+  pdl_launch_dependents();
+  const int64_t r = blockIdx.x;
+  const int n4 = dim >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4 wv[RMS_MAXV];  // static weights: loaded while the previous kernel finishes
+#pragma unroll
+  for (int u = 0; u < RMS_MAXV; u++) {
+    const int i = threadIdx.x + u * RMS_THREADS;
+    if (i < n4) wv[u] = w4[i];
+  }
+  pdl_wait();
+  float4* x = reinterpret_cast<float4*>(resid + r * dim);
+  const float4* d = delta ? reinterpret_cast<const float4*>(delta + r * dim) : nullptr;
+  float4 v[RMS_MAXV];
+  float ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < RMS_MAXV; u++) {
+    const int i = threadIdx.x + u * RMS_THREADS;
+    if (i < n4) {
+      v[u] = x[i];
+      if (d) {
+        const float4 b = d[i];
+        v[u].x += b.x;
+        v[u].y += b.y;
+        v[u].z += b.z;
+        v[u].w += b.w;
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < RMS_MAXV; u++) {
+    const int i = threadIdx.x + u * RMS_THREADS;
+    if (i < n4) {
+      if (d) x[i] = v[u];
+      ss = fmaf(v[u].x, v[u].x, fmaf(v[u].y, v[u].y, fmaf(v[u].z, v[u].z, fmaf(v[u].w, v[u].w, ss))));
+    }
+  }
+  const float inv = rsqrtf(block_sum(ss, red) / (float)dim + eps);
+#pragma unroll
+  for (int u = 0; u < RMS_MAXV; u++) {
+    const int i = threadIdx.x + u * RMS_THREADS;
+    if (i < n4) {
+      const float4 g = wv[u];
+      const float o0 = v[u].x * inv * g.x, o1 = v[u].y * inv * g.y, o2 = v[u].z * inv * g.z, o3 = v[u].w * inv * g.w;
+      const int64_t e = r * dim + 4 * (int64_t)i;
+      if (dt == DT_F32) {
+        reinterpret_cast<float4*>(out)[e >> 2] = make_float4(o0, o1, o2, o3);
+      } else if (dt == DT_F16) {
+        __half2 h[2] = {__floats2half2_rn(o0, o1), __floats2half2_rn(o2, o3)};
+        reinterpret_cast<uint2*>(out)[e >> 2] = *reinterpret_cast<uint2*>(h);
+      } else {
+        __nv_bfloat162 h[2] = {__floats2bfloat162_rn(o0, o1), __floats2bfloat162_rn(o2, o3)};
+        reinterpret_cast<uint2*>(out)[e >> 2] = *reinterpret_cast<uint2*>(h);
+      }
+    }
+  }
+}
+
+// Any width and alignment.
+__global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(float* resid, const float* delta, int64_t dim,
+                                                             const float* w, float eps, void* out, int dt) {
+  __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t r = blockIdx.x;
   float* x = resid + r * dim;
   const float* d = delta ? delta + r * dim : nullptr;
@@ -90,6 +168,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(float* resid, const float*
 }
 
 __global__ void silu_mul_kernel(const float* gu, int64_t rows, int64_t n, void* out, int dt) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t total = rows * n;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / n, c = i - r * n;
@@ -100,10 +180,15 @@ __global__ void silu_mul_kernel(const float* gu, int64_t rows, int64_t n, void* 
 struct GdnArgs {
   const float* proj;
   int64_t ps;
-  const __half* ab;
+  const __half* ab;   // precomputed gate inputs, or null:
   int64_t abs;
+  const __half* x;    // ... then from the layer input x [T, hidden]
+  int64_t xs;
+  const __half* abw;  // and the gate weights [2nv, hidden]
+  int hidden;
   int T, nk, nv, C;
-  float* conv_state;
+  float* conv_state;  // [4, C] ring: slot p & 3 holds the input of position p
+  const int* pos;     // position of token 0 (device)
   const float* conv_w;
   const float* A;
   const float* dt_bias;
@@ -120,25 +205,61 @@ struct GdnArgs {
   int dt;
 };
 
-// SiLU of the causal depthwise conv of channel c at token t: taps 0..3 meet
-// inputs t-3..t; inputs before the first token come from the conv window.
-__device__ __forceinline__ float gdn_conv(const GdnArgs& a, int t, int c) {
+// SiLU of the causal depthwise conv of channel c at token t (position
+// p0 + t): taps 0..3 meet inputs t-3..t; inputs before the first token come
+// from the conv window's ring slots.
+__device__ __forceinline__ float gdn_conv(const GdnArgs& a, int p0, int t, int c) {
   float acc = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; j++) {
     const int s = t - 3 + j;
-    const float in = s >= 0 ? a.proj[(int64_t)s * a.ps + c] : a.conv_state[(int64_t)(3 + s) * a.C + c];
+    const float in = s >= 0 ? a.proj[(int64_t)s * a.ps + c] : a.conv_state[(int64_t)((p0 + s) & 3) * a.C + c];
     acc = fmaf(a.conv_w[(int64_t)c * 4 + j], in, acc);
   }
   return silu(acc);
 }
 
+// Dot products of one fp16 input row with two fp16 weight rows, summed over
+// the CTA (8 halves per 16-byte load; hidden % 8 == 0, rows 16-byte aligned).
+__device__ __forceinline__ void dot2_rows(const __half* x, const __half* wa, const __half* wb, int hidden,
+                                          float* red, float& da, float& db) {
+  const uint4* xr = reinterpret_cast<const uint4*>(x);
+  const uint4* ar = reinterpret_cast<const uint4*>(wa);
+  const uint4* br = reinterpret_cast<const uint4*>(wb);
+  float sa = 0.f, sb = 0.f;
+#pragma unroll 4
+  for (int e = threadIdx.x; e < hidden / 8; e += blockDim.x) {
+    const uint4 xv = xr[e], av = ar[e], bv = br[e];
+    const __half2* xh = reinterpret_cast<const __half2*>(&xv);
+    const __half2* ah = reinterpret_cast<const __half2*>(&av);
+    const __half2* bh = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const float2 xf = __half22float2(xh[q]), af = __half22float2(ah[q]), bf = __half22float2(bh[q]);
+      sa = fmaf(xf.x, af.x, fmaf(xf.y, af.y, sa));
+      sb = fmaf(xf.x, bf.x, fmaf(xf.y, bf.y, sb));
+    }
+  }
+  da = block_sum(sa, red);
+  db = block_sum(sb, red);
+}
+
+__device__ __forceinline__ void gdn_gates(const GdnArgs& a, int h, float av, float bv, float& g, float& beta) {
+  av += a.dt_bias[h];
+  const float sp = av > 20.f ? av : log1pf(__expf(av));
+  g = __expf(a.A[h] * sp);
+  beta = 1.f / (1.f + __expf(-bv));
+}
+
 __global__ void __launch_bounds__(GDN_D) gdn_prep_kernel(GdnArgs a) {
   __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int t = blockIdx.x, grp = blockIdx.y, i = threadIdx.x;
+  const int p0 = *a.pos;
   if (grp < a.nk) {
-    const float q = gdn_conv(a, t, grp * GDN_D + i);
-    const float k = gdn_conv(a, t, a.nk * GDN_D + grp * GDN_D + i);
+    const float q = gdn_conv(a, p0, t, grp * GDN_D + i);
+    const float k = gdn_conv(a, p0, t, a.nk * GDN_D + grp * GDN_D + i);
     const float sq = block_sum(q * q, red);
     const float sk = block_sum(k * k, red);
     const int64_t o = ((int64_t)t * a.nk + grp) * GDN_D + i;
@@ -146,19 +267,25 @@ __global__ void __launch_bounds__(GDN_D) gdn_prep_kernel(GdnArgs a) {
     a.kn[o] = k * rsqrtf(sk / GDN_D + 1e-6f) * rsqrtf((float)GDN_D);
   } else {
     const int h = grp - a.nk;
-    a.vv[((int64_t)t * a.nv + h) * GDN_D + i] = gdn_conv(a, t, 2 * a.nk * GDN_D + h * GDN_D + i);
+    a.vv[((int64_t)t * a.nv + h) * GDN_D + i] = gdn_conv(a, p0, t, 2 * a.nk * GDN_D + h * GDN_D + i);
+    float av = 0.f, bv = 0.f;
+    if (!a.ab)  // the two gate rows of this head against the token's input
+      dot2_rows(a.x + (int64_t)t * a.xs, a.abw + (int64_t)h * a.hidden, a.abw + (int64_t)(a.nv + h) * a.hidden,
+                a.hidden, red, av, bv);
     if (i == 0) {
-      const float av = __half2float(a.ab[(int64_t)t * a.abs + h]) + a.dt_bias[h];
-      const float bv = __half2float(a.ab[(int64_t)t * a.abs + a.nv + h]);
-      const float sp = av > 20.f ? av : log1pf(__expf(av));
-      a.gdec[(int64_t)t * a.nv + h] = __expf(a.A[h] * sp);
-      a.beta[(int64_t)t * a.nv + h] = 1.f / (1.f + __expf(-bv));
+      if (a.ab) {
+        av = __half2float(a.ab[(int64_t)t * a.abs + h]);
+        bv = __half2float(a.ab[(int64_t)t * a.abs + a.nv + h]);
+      }
+      gdn_gates(a, h, av, bv, a.gdec[(int64_t)t * a.nv + h], a.beta[(int64_t)t * a.nv + h]);
     }
   }
 }
 
 __global__ void __launch_bounds__(GDN_D) gdn_scan_kernel(GdnArgs a) {
   __shared__ float qs[2][GDN_D], ks[2][GDN_D];
+  pdl_launch_dependents();
+  pdl_wait();
   const int h = blockIdx.x, kh = h % a.nk;
   const int tid = threadIdx.x, col = tid >> 3, seg = tid & 7;
   const int j = blockIdx.y * GDN_COLS + col;
@@ -217,21 +344,103 @@ __global__ void __launch_bounds__(GDN_D) gdn_scan_kernel(GdnArgs a) {
   for (int r = 0; r < 16; r++) sp[8 * r] = S[r];
 
   // Advance the conv window by T inputs (the prep launch, which read it, has
-  // completed).  Rows ascend, and new row r reads old row r + T > r.
+  // completed): the last (up to) four inputs go to their positions' slots.
   const int64_t nthr = (int64_t)gridDim.x * gridDim.y * blockDim.x;
   const int64_t gid = ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + tid;
+  const int p0 = *a.pos;
   for (int64_t c = gid; c < a.C; c += nthr) {
+    for (int t = max(0, a.T - 4); t < a.T; t++)
+      a.conv_state[(int64_t)((p0 + t) & 3) * a.C + c] = a.proj[(int64_t)t * a.ps + c];
+  }
+}
+
+// One token (T == 1) of the whole block in one launch: CTA = value head h,
+// 256 threads.  Threads 0..127 take the q channels of key head h % nk and
+// the v channels of h, threads 128..255 the k channels; all 256 form the
+// gate dot products; then thread (j = tid / 2, r = tid % 2) applies the
+// recurrence to column j, key indices 64r..64r+63, held in registers; the
+// gated norm closes the head.  The conv window slot of this position is
+// written by the CTAs that own the channels (q/k: h < nk) and is not read by
+// any CTA at this position.
+__global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(GdnArgs a) {
+  __shared__ float red[32];
+  __shared__ float qs[GDN_D], ks[GDN_D], vs[GDN_D];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int h = blockIdx.x, kh = h % a.nk, tid = threadIdx.x, warp = tid >> 5;
+  const int pos = *a.pos;
+  const int i = tid & (GDN_D - 1);
+  const int cqk = (tid < GDN_D ? 0 : a.nk * GDN_D) + kh * GDN_D + i;
+  const int cv = 2 * a.nk * GDN_D + h * GDN_D + i;
+  const float c = gdn_conv(a, pos, 0, cqk);
+  const float v = tid < GDN_D ? gdn_conv(a, pos, 0, cv) : 0.f;
+  float av = 0.f, bv = 0.f;
+  if (a.ab) {
+    av = __half2float(a.ab[h]);
+    bv = __half2float(a.ab[a.nv + h]);
+  } else {
+    dot2_rows(a.x, a.abw + (int64_t)h * a.hidden, a.abw + (int64_t)(a.nv + h) * a.hidden, a.hidden, red, av, bv);
+  }
+  float g, beta;
+  gdn_gates(a, h, av, bv, g, beta);
+  // q and k norms: warps 0-3 hold q, warps 4-7 k
+  float sq = c * c;
 #pragma unroll
-    for (int r = 0; r < 3; r++) {
-      const int s = a.T - 3 + r;
-      a.conv_state[(int64_t)r * a.C + c] =
-          s >= 0 ? a.proj[(int64_t)s * a.ps + c] : a.conv_state[(int64_t)(r + a.T) * a.C + c];
-    }
+  for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  __syncthreads();  // red is free again
+  if ((tid & 31) == 0) red[warp] = sq;
+  __syncthreads();
+  const float part = tid < GDN_D ? red[0] + red[1] + red[2] + red[3] : red[4] + red[5] + red[6] + red[7];
+  if (tid < GDN_D) {
+    qs[i] = c * rsqrtf(part / GDN_D + 1e-6f) * (1.f / GDN_D);
+    vs[i] = v;
+  } else {
+    ks[i] = c * rsqrtf(part / GDN_D + 1e-6f) * rsqrtf((float)GDN_D);
+  }
+  const int slot = pos & 3;
+  if (h < a.nk) a.conv_state[(int64_t)slot * a.C + cqk] = a.proj[cqk];
+  if (tid < GDN_D) a.conv_state[(int64_t)slot * a.C + cv] = a.proj[cv];
+  __syncthreads();
+
+  const int j = tid >> 1, r = tid & 1;
+  float4* sp = reinterpret_cast<float4*>(a.state + ((int64_t)h * GDN_D + j) * GDN_D + 64 * r);
+  float S[64];
+#pragma unroll
+  for (int m = 0; m < 16; m++) {
+    const float4 t4 = sp[m];
+    S[4 * m] = t4.x;
+    S[4 * m + 1] = t4.y;
+    S[4 * m + 2] = t4.z;
+    S[4 * m + 3] = t4.w;
+  }
+  float kv = 0.f;
+#pragma unroll
+  for (int m = 0; m < 64; m++) {
+    S[m] *= g;
+    kv = fmaf(S[m], ks[64 * r + m], kv);
+  }
+  kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+  const float u = (vs[j] - kv) * beta;
+  float y = 0.f;
+#pragma unroll
+  for (int m = 0; m < 64; m++) {
+    S[m] = fmaf(ks[64 * r + m], u, S[m]);
+    y = fmaf(S[m], qs[64 * r + m], y);
+  }
+  y += __shfl_xor_sync(0xffffffffu, y, 1);
+#pragma unroll
+  for (int m = 0; m < 16; m++) sp[m] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
+  const float ss = block_sum(r == 0 ? y * y : 0.f, red);
+  if (r == 0) {
+    const float z = a.proj[a.C + h * GDN_D + j];
+    store_out(a.out, a.dt, (int64_t)h * GDN_D + j, y * rsqrtf(ss / GDN_D + a.eps) * a.norm_w[j] * silu(z));
   }
 }
 
 __global__ void __launch_bounds__(GDN_D) gdn_norm_kernel(GdnArgs a) {
   __shared__ float red[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
   const float v = a.o[((int64_t)t * a.nv + h) * GDN_D + i];
   const float ss = block_sum(v * v, red);
@@ -248,7 +457,9 @@ __global__ void __launch_bounds__(ATT_D) attn_decode_kernel(const float* qkv, in
                                                             void* out, int dt) {
   extern __shared__ float sc[];
   __shared__ float red[32];
-  __shared__ float qs[ATT_D], ks[ATT_D], vs[ATT_D];
+  __shared__ __align__(16) float qs[ATT_D], ks[ATT_D], vs[ATT_D];
+  pdl_launch_dependents();
+  pdl_wait();
   const int h = blockIdx.x, d = threadIdx.x;
   const int group = nq / nkv, kvh = h / group;
   const int pos = min(max(*pos_p, 0), max_len - 1);
@@ -281,22 +492,31 @@ __global__ void __launch_bounds__(ATT_D) attn_decode_kernel(const float* qkv, in
   }
   __syncthreads();
 
-  // Scores: warp w takes positions w, w + 8, ...; lane l holds dimensions
-  // 8l..8l+7.  The current position's key comes from shared memory.
+  // Scores: warp w takes positions ATT_U*w.., then 8*ATT_U further on; lane
+  // l holds dimensions 8l..8l+7.  ATT_U positions' loads are in flight at once.
+  // The current position's key comes from shared memory.
   const int warp = d >> 5, lane = d & 31;
   float qr[8];
 #pragma unroll
   for (int e = 0; e < 8; e++) qr[e] = qs[8 * lane + e];
   const float scale = rsqrtf((float)ATT_D);
-  for (int s = warp; s <= pos; s += ATT_D / 32) {
-    const float* kr = s == pos ? ks : kc + ((int64_t)s * nkv + kvh) * ATT_D;
-    const float4 k0 = *reinterpret_cast<const float4*>(kr + 8 * lane);
-    const float4 k1 = *reinterpret_cast<const float4*>(kr + 8 * lane + 4);
-    float p = qr[0] * k0.x + qr[1] * k0.y + qr[2] * k0.z + qr[3] * k0.w + qr[4] * k1.x + qr[5] * k1.y +
-              qr[6] * k1.z + qr[7] * k1.w;
+  for (int s0 = ATT_U * warp; s0 <= pos; s0 += ATT_U * (ATT_D / 32)) {
+    float4 k0[ATT_U], k1[ATT_U];
 #pragma unroll
-    for (int o = 16; o; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-    if (lane == 0) sc[s] = p * scale;
+    for (int u = 0; u < ATT_U; u++) {
+      const int s = min(s0 + u, pos);
+      const float* kr = s == pos ? ks : kc + ((int64_t)s * nkv + kvh) * ATT_D;
+      k0[u] = *reinterpret_cast<const float4*>(kr + 8 * lane);
+      k1[u] = *reinterpret_cast<const float4*>(kr + 8 * lane + 4);
+    }
+#pragma unroll
+    for (int u = 0; u < ATT_U; u++) {
+      float p = qr[0] * k0[u].x + qr[1] * k0[u].y + qr[2] * k0[u].z + qr[3] * k0[u].w + qr[4] * k1[u].x +
+                qr[5] * k1[u].y + qr[6] * k1[u].z + qr[7] * k1[u].w;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+      if (lane == 0 && s0 + u <= pos) sc[s0 + u] = p * scale;
+    }
   }
   __syncthreads();
   float m = -INFINITY;
@@ -309,10 +529,35 @@ __global__ void __launch_bounds__(ATT_D) attn_decode_kernel(const float* qkv, in
     l += e;
   }
   l = block_sum(l, red);  // its barriers also publish sc
-  float acc = 0.f;
-  for (int s = 0; s < pos; s++) acc = fmaf(sc[s], vc[((int64_t)s * nkv + kvh) * ATT_D + d], acc);
-  acc = fmaf(sc[pos], vs[d], acc);
-  store_out(out, dt, (int64_t)h * ATT_D + d, acc / l / (1.f + __expf(-gate)));
+
+  // Weighted values: warp w takes positions w, w + 8, ... (lane: dimensions
+  // 8l..8l+7), then the eight warps' partial sums are added per dimension.
+  float acc[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) acc[e] = 0.f;
+#pragma unroll 8
+  for (int s = warp; s <= pos; s += ATT_D / 32) {
+    const float* vr = s == pos ? vs : vc + ((int64_t)s * nkv + kvh) * ATT_D;
+    const float4 a0 = *reinterpret_cast<const float4*>(vr + 8 * lane);
+    const float4 a1 = *reinterpret_cast<const float4*>(vr + 8 * lane + 4);
+    const float pr = sc[s];
+    acc[0] = fmaf(pr, a0.x, acc[0]);
+    acc[1] = fmaf(pr, a0.y, acc[1]);
+    acc[2] = fmaf(pr, a0.z, acc[2]);
+    acc[3] = fmaf(pr, a0.w, acc[3]);
+    acc[4] = fmaf(pr, a1.x, acc[4]);
+    acc[5] = fmaf(pr, a1.y, acc[5]);
+    acc[6] = fmaf(pr, a1.z, acc[6]);
+    acc[7] = fmaf(pr, a1.w, acc[7]);
+  }
+  __shared__ float part[ATT_D / 32][ATT_D];
+#pragma unroll
+  for (int e = 0; e < 8; e++) part[warp][8 * lane + e] = acc[e];
+  __syncthreads();
+  float o = 0.f;
+#pragma unroll
+  for (int w = 0; w < ATT_D / 32; w++) o += part[w][d];
+  store_out(out, dt, (int64_t)h * ATT_D + d, o / l / (1.f + __expf(-gate)));
 }
 
 bool dt_ok(int d) { return d == DT_F32 || d == DT_F16 || d == DT_BF16; }
@@ -341,7 +586,15 @@ int gsq_rmsnorm(float* resid, const float* delta, int64_t rows, int64_t dim, con
   if (rows < 0 || dim <= 0 || rows > INT32_MAX) return fail(GSQ_ERR_SIZE, "gsq_rmsnorm: bad shape");
   if (!dt_ok(out_dtype)) return fail(GSQ_ERR_ARG, "gsq_rmsnorm: bad output dtype");
   if (rows == 0) return GSQ_OK;
-  rmsnorm_kernel<<<(unsigned)rows, 256, 0, (cudaStream_t)stream>>>(resid, delta, dim, weight, eps, out, out_dtype);
+  auto al = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  const bool vec = dim % 4 == 0 && dim <= (int64_t)RMS_THREADS * RMS_MAXV * 4 && al(resid) && al(weight) &&
+                   (!delta || al(delta)) && reinterpret_cast<uintptr_t>(out) % (out_dtype == DT_F32 ? 16 : 8) == 0;
+  if (vec)
+    launch_pdl(rmsnorm_vec_kernel, dim3((unsigned)rows), dim3(RMS_THREADS), 0, (cudaStream_t)stream, resid, delta,
+               (int)dim, weight, eps, out, out_dtype);
+  else
+    launch_pdl(rmsnorm_kernel, dim3((unsigned)rows), dim3(RMS_THREADS), 0, (cudaStream_t)stream, resid, delta, dim,
+               weight, eps, out, out_dtype);
   return launched("gsq_rmsnorm");
 }
 
@@ -352,47 +605,67 @@ int gsq_silu_mul(const float* gu, int64_t rows, int64_t n, void* out, int out_dt
   if (rows == 0) return GSQ_OK;
   const int64_t total = rows * n;
   const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-  silu_mul_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(gu, rows, n, out, out_dtype);
+  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, (cudaStream_t)stream, gu, rows, n, out, out_dtype);
   return launched("gsq_silu_mul");
 }
 
 size_t gsq_gdn_scratch_bytes(int64_t T, int64_t nk, int64_t nv) {
-  if (T <= 0 || nk <= 0 || nv <= 0) return 0;
+  if (T <= 1 || nk <= 0 || nv <= 0) return 0;  // one token needs none
   const size_t f = sizeof(float);
   return 2 * align16(T * nk * GDN_D * f) + 2 * align16(T * nv * GDN_D * f) + 2 * align16(T * nv * f);
 }
 
-int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t ab_stride, int64_t T, int64_t nk,
-            int64_t nv, float* conv_state, const float* conv_w, const float* A, const float* dt_bias,
+int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t ab_stride, const uint16_t* x,
+            int64_t x_stride, const uint16_t* ab_w, int64_t hidden, int64_t T, int64_t nk, int64_t nv,
+            float* conv_state, const int32_t* pos, const float* conv_w, const float* A, const float* dt_bias,
             const float* norm_w, float eps, float* state, void* scratch, size_t scratch_bytes, void* out,
             int out_dtype, gsq_stream_t stream) {
-  if (!proj || !ab || !conv_state || !conv_w || !A || !dt_bias || !norm_w || !state || !out)
+  auto al16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  if (!proj || !conv_state || !pos || !conv_w || !A || !dt_bias || !norm_w || !state || !out)
     return fail(GSQ_ERR_ARG, "gsq_gdn: null pointer");
+  if (!ab && (!x || !ab_w || hidden <= 0 || hidden > INT32_MAX || x_stride < hidden))
+    return fail(GSQ_ERR_ARG, "gsq_gdn: without ab, x and ab_w are required");
+  if (!ab && (hidden % 8 || x_stride % 8 || !al16(x) || !al16(ab_w)))
+    return fail(GSQ_ERR_ALIGN, "gsq_gdn: x and ab_w rows must be 16-byte aligned (hidden % 8 == 0)");
   if (T < 0 || T > INT32_MAX / 2 || nk <= 0 || nv <= 0 || nv % nk || nv > 65535 || nk > 65535)
     return fail(GSQ_ERR_SIZE, "gsq_gdn: bad shape (nv must be a multiple of nk)");
   const int64_t C = 2 * nk * GDN_D + nv * GDN_D;
-  if (proj_stride < C + nv * GDN_D || ab_stride < 2 * nv) return fail(GSQ_ERR_SIZE, "gsq_gdn: stride too small");
+  if (proj_stride < C + nv * GDN_D || (ab && ab_stride < 2 * nv))
+    return fail(GSQ_ERR_SIZE, "gsq_gdn: stride too small");
   if (!dt_ok(out_dtype)) return fail(GSQ_ERR_ARG, "gsq_gdn: bad output dtype");
+  if (!al16(state)) return fail(GSQ_ERR_ALIGN, "gsq_gdn: state not 16-byte aligned");
   if (T == 0) return GSQ_OK;
-  if (!scratch || scratch_bytes < gsq_gdn_scratch_bytes(T, nk, nv))
+  if (T > 1 && (!scratch || scratch_bytes < gsq_gdn_scratch_bytes(T, nk, nv)))
     return fail(GSQ_ERR_WORKSPACE, "gsq_gdn: scratch missing or too small");
-  if (reinterpret_cast<uintptr_t>(scratch) % 16) return fail(GSQ_ERR_ALIGN, "gsq_gdn: scratch not 16-byte aligned");
-  GdnArgs a;
+  if (T > 1 && !al16(scratch)) return fail(GSQ_ERR_ALIGN, "gsq_gdn: scratch not 16-byte aligned");
+  GdnArgs a = {};
   a.proj = proj;
   a.ps = proj_stride;
   a.ab = reinterpret_cast<const __half*>(ab);
   a.abs = ab_stride;
+  a.x = reinterpret_cast<const __half*>(x);
+  a.xs = x_stride;
+  a.abw = reinterpret_cast<const __half*>(ab_w);
+  a.hidden = (int)hidden;
   a.T = (int)T;
   a.nk = (int)nk;
   a.nv = (int)nv;
   a.C = (int)C;
   a.conv_state = conv_state;
+  a.pos = pos;
   a.conv_w = conv_w;
   a.A = A;
   a.dt_bias = dt_bias;
   a.norm_w = norm_w;
   a.eps = eps;
   a.state = state;
+  a.out = out;
+  a.dt = out_dtype;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (T == 1) {
+    launch_pdl(gdn_decode_kernel, dim3((unsigned)nv), dim3(2 * GDN_D), 0, st, a);
+    return launched("gsq_gdn (one token)");
+  }
   uint8_t* p = static_cast<uint8_t*>(scratch);
   const size_t f = sizeof(float);
   a.qn = reinterpret_cast<float*>(p);
@@ -406,15 +679,12 @@ int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t 
   a.gdec = reinterpret_cast<float*>(p);
   p += align16(T * nv * f);
   a.beta = reinterpret_cast<float*>(p);
-  a.out = out;
-  a.dt = out_dtype;
-  cudaStream_t st = (cudaStream_t)stream;
-  gdn_prep_kernel<<<dim3((unsigned)T, (unsigned)(nk + nv)), GDN_D, 0, st>>>(a);
+  launch_pdl(gdn_prep_kernel, dim3((unsigned)T, (unsigned)(nk + nv)), dim3(GDN_D), 0, st, a);
   int rc = launched("gsq_gdn (prep)");
   if (rc) return rc;
-  gdn_scan_kernel<<<dim3((unsigned)nv, GDN_D / GDN_COLS), GDN_D, 0, st>>>(a);
+  launch_pdl(gdn_scan_kernel, dim3((unsigned)nv, GDN_D / GDN_COLS), dim3(GDN_D), 0, st, a);
   if ((rc = launched("gsq_gdn (scan)"))) return rc;
-  gdn_norm_kernel<<<dim3((unsigned)T, (unsigned)nv), GDN_D, 0, st>>>(a);
+  launch_pdl(gdn_norm_kernel, dim3((unsigned)T, (unsigned)nv), dim3(GDN_D), 0, st, a);
   return launched("gsq_gdn (norm)");
 }
 
@@ -431,14 +701,13 @@ int gsq_attn_decode(const float* qkv, int64_t nq, int64_t nkv, const float* q_no
     return fail(GSQ_ERR_ALIGN, "gsq_attn_decode: caches not 16-byte aligned");
   const size_t smem = (size_t)max_len * sizeof(float);
   cudaStream_t st = (cudaStream_t)stream;
-  if (smem > 48 * 1024) {
+  if (smem + 12 * 1024 > 48 * 1024) {  // with the static arrays (about 11 KB)
     const cudaError_t e =
         cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(GSQ_ERR_CUDA, "gsq_attn_decode: shared memory attribute");
   }
-  attn_decode_kernel<<<(unsigned)nq, ATT_D, smem, st>>>(qkv, (int)nq, (int)nkv, q_norm_w, k_norm_w, eps, (int)rot,
-                                                        theta, k_cache, v_cache, (int)max_len, pos, out,
-                                                        out_dtype);
+  launch_pdl(attn_decode_kernel, dim3((unsigned)nq), dim3(ATT_D), smem, st, qkv, (int)nq, (int)nkv, q_norm_w,
+             k_norm_w, eps, (int)rot, theta, k_cache, v_cache, (int)max_len, pos, out, out_dtype);
   return launched("gsq_attn_decode");
 }
 

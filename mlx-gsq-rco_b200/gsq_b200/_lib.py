@@ -51,8 +51,8 @@ SIGNATURES = {
     "gsq_rmsnorm": (_I, [_P, _P, _I64, _I64, _P, ctypes.c_float, _P, _I, _P]),
     "gsq_silu_mul": (_I, [_P, _I64, _I64, _P, _I, _P]),
     "gsq_gdn_scratch_bytes": (_SZ, [_I64, _I64, _I64]),
-    "gsq_gdn": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _SZ, _P, _I,
-                     _P]),
+    "gsq_gdn": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P,
+                     ctypes.c_float, _P, _P, _SZ, _P, _I, _P]),
     "gsq_attn_decode": (_I, [_P, _I64, _I64, _P, _P, ctypes.c_float, _I64, ctypes.c_float, _P, _P, _I64, _P, _P, _I,
                              _P]),
 }

@@ -241,7 +241,7 @@ class Qwen35:
                 L["A"] = w[p + "ssm_a"].float().contiguous()
                 L["dt_bias"] = w[p + "ssm_dt.bias"].float().contiguous()
                 L["norm"] = w[p + "ssm_norm.weight"].float().contiguous()
-                L["conv_state"] = torch.zeros(3, cfg.gdn_conv_dim, device=self.dev)
+                L["conv_state"] = torch.zeros(4, cfg.gdn_conv_dim, device=self.dev)  # ring, slot = position & 3
                 L["state"] = torch.zeros(nv, cfg.linear_value_head_dim, cfg.linear_key_head_dim, device=self.dev)
             else:
                 L["qkv"] = _Packed([w[p + "attn_q.weight"], w[p + "attn_k.weight"], w[p + "attn_v.weight"]])
@@ -278,17 +278,24 @@ class Qwen35:
         self.n_pos = 0
 
     # ---- blocks ----
-    def _gdn(self, L, p: torch.Tensor, ab: torch.Tensor) -> torch.Tensor:
+    def _gdn(self, L, p: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+        """The gated-DeltaNet block on the q|k|v|z projection p of input h.
+        The 2 x 48 gate rows (plain fp16) are a cuBLAS GEMM for prompts and
+        are computed inside the block's first kernel for decode tokens."""
         cfg, T = self.cfg, p.shape[0]
         nk, nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
         lib = _lib.load()
         need = lib.gsq_gdn_scratch_bytes(T, nk, nv)
-        scratch = torch.empty(need, dtype=torch.uint8, device=self.dev)
+        scratch = torch.empty(need, dtype=torch.uint8, device=self.dev) if need else None
         out = torch.empty(T, nv * cfg.linear_value_head_dim, dtype=torch.float16, device=self.dev)
-        _lib.check(lib.gsq_gdn(p.data_ptr(), p.stride(0), ab.data_ptr(), ab.stride(0), T, nk, nv,
-                               L["conv_state"].data_ptr(), L["conv_w"].data_ptr(), L["A"].data_ptr(),
-                               L["dt_bias"].data_ptr(), L["norm"].data_ptr(), self.eps, L["state"].data_ptr(),
-                               scratch.data_ptr(), need, out.data_ptr(), _lib.DTYPE_CODES[torch.float16],
+        ab = F.linear(h, L["ab"]) if T >= 8 else None
+        _lib.check(lib.gsq_gdn(p.data_ptr(), p.stride(0), ab.data_ptr() if ab is not None else None,
+                               ab.stride(0) if ab is not None else 0, h.data_ptr(), h.stride(0), L["ab"].data_ptr(),
+                               cfg.hidden_size, T, nk, nv, L["conv_state"].data_ptr(), self.pos.data_ptr(),
+                               L["conv_w"].data_ptr(), L["A"].data_ptr(), L["dt_bias"].data_ptr(),
+                               L["norm"].data_ptr(), self.eps, L["state"].data_ptr(),
+                               scratch.data_ptr() if scratch is not None else None, need, out.data_ptr(),
+                               _lib.DTYPE_CODES[torch.float16],
                                _stream(self.dev)))
         return out
 
@@ -341,8 +348,7 @@ class Qwen35:
             h = rmsnorm(x, delta, L["attn_norm"], self.eps)
             if L["linear"]:
                 p = L["qkvz"](h)
-                ab = F.linear(h, L["ab"])
-                d = L["out"](self._gdn(L, p, ab))
+                d = L["out"](self._gdn(L, p, h))
             else:
                 p = L["qkv"](h)
                 o = self._attn_decode(L, p) if pos0 is None else self._attn_prefill(L, p, pos0)

@@ -75,13 +75,17 @@ def test_glue_abi_validation():
     assert lib.gsq_rmsnorm(None, None, 1, 16, fake, 1e-6, fake, 1, None) == _lib.GSQ_ERR_ARG
     assert lib.gsq_rmsnorm(fake, None, 1, 16, fake, 1e-6, fake, 9, None) == _lib.GSQ_ERR_ARG
     assert lib.gsq_silu_mul(fake, 1, 0, fake, 1, None) == _lib.GSQ_ERR_SIZE
-    assert lib.gsq_gdn_scratch_bytes(1, 16, 48) > 0
-    # value heads must be a multiple of key heads
-    assert lib.gsq_gdn(fake, 20000, fake, 96, 1, 16, 40, fake, fake, fake, fake, fake, 1e-6, fake, fake, 1 << 30,
-                       fake, 1, None) == _lib.GSQ_ERR_SIZE
-    # scratch too small
-    assert lib.gsq_gdn(fake, 16384, fake, 96, 4, 16, 48, fake, fake, fake, fake, fake, 1e-6, fake, fake, 16,
-                       fake, 1, None) == _lib.GSQ_ERR_WORKSPACE
+    assert lib.gsq_gdn_scratch_bytes(1, 16, 48) == 0  # one token runs as a single kernel
+    assert lib.gsq_gdn_scratch_bytes(2, 16, 48) > 0
+
+    def gdn(proj_stride, ab, T, nv, scratch_bytes, x=None, hidden=0):
+        return lib.gsq_gdn(fake, proj_stride, ab, 96, x, hidden, fake if x else None, hidden, T, 16, nv, fake, fake,
+                           fake, fake, fake, fake, 1e-6, fake, fake, scratch_bytes, fake, 1, None)
+
+    assert gdn(20000, fake, 1, 40, 1 << 30) == _lib.GSQ_ERR_SIZE  # value heads a multiple of key heads
+    assert gdn(16384, fake, 4, 48, 16) == _lib.GSQ_ERR_WORKSPACE  # scratch too small
+    assert gdn(16384, None, 1, 48, 0) == _lib.GSQ_ERR_ARG  # no gates and no input to form them
+    assert gdn(16384, None, 1, 48, 0, x=fake + 8, hidden=5120) == _lib.GSQ_ERR_ALIGN
     assert lib.gsq_attn_decode(fake, 24, 5, fake, fake, 1e-6, 64, 1e7, fake, fake, 256, fake, fake, 1,
                                None) == _lib.GSQ_ERR_SIZE
     assert lib.gsq_attn_decode(fake, 24, 4, fake, fake, 1e-6, 65, 1e7, fake, fake, 256, fake, fake, 1,
