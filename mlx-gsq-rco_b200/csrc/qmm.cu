@@ -96,8 +96,9 @@ struct QmmArgs {
 
 // One output value: y, or every rank's gather region (coalesced per warp:
 // 32 consecutive rows of one token).
+template <bool GATHER>
 __device__ __forceinline__ void qmm_store(const QmmArgs& a, int64_t m, int64_t erow, float v) {
-  if (a.world <= 1) {
+  if constexpr (!GATHER) {
     a.y[m * a.N + erow] = v;
     return;
   }
@@ -214,7 +215,9 @@ __device__ __forceinline__ void st_sw128(uint8_t* tile, int row, int chunk, cons
   *reinterpret_cast<uint4*>(tile + row * 128 + ((chunk ^ (row & 7)) << 4)) = *reinterpret_cast<const uint4*>(h);
 }
 
-template <int T>
+// GATHER: the instance used by gsq_qmm_gather (a separate instance, so the
+// single-GPU kernel carries none of its code).
+template <int T, bool GATHER>
 __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, const __grid_constant__ CUtensorMap xmap) {
   using G = QmmGeom<T>;
   extern __shared__ uint8_t smem_raw[];
@@ -434,7 +437,7 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
 #pragma unroll
             for (int jj = 0; jj < 16; jj++) {
               const int64_t m = (int64_t)m0 + j0 + jj;
-              if (m < a.M) qmm_store(a, m, erow, __uint_as_float(vv[jj]));
+              if (m < a.M) qmm_store<GATHER>(a, m, erow, __uint_as_float(vv[jj]));
             }
           }
         }
@@ -478,17 +481,19 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
 #pragma unroll
             for (int z = 1; z < QMM_KSPLIT_MAX; z++) acc += v[z][jj];  // zeros beyond ksplit
             const int64_t m = (int64_t)m0 + j0 + jj;
-            if (m < a.M) qmm_store(a, m, erow, acc);
+            if (m < a.M) qmm_store<GATHER>(a, m, erow, acc);
           }
         }
       }
     }
   }
-  if (a.world > 1 && warp >= QMM_DEC0) {
-    const bool stored = a.ksplit == 1 || *last_flag;
-    if (stored) __threadfence_system();  // this thread's stores into the peers' regions
-    named_sync_decoders();
-    if (warp == QMM_DEC0 && lane == 0) qmm_gather_signal(a, stored);
+  if constexpr (GATHER) {
+    if (warp >= QMM_DEC0) {
+      const bool stored = a.ksplit == 1 || *last_flag;
+      if (stored) __threadfence_system();  // this thread's stores into the peers' regions
+      named_sync_decoders();
+      if (warp == QMM_DEC0 && lane == 0) qmm_gather_signal(a, stored);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -582,19 +587,25 @@ size_t qmm_workspace_bytes(int t, int64_t N, int64_t K, int64_t M, int x_dtype) 
   return qmm_plan(t, N, K, M, x_dtype).workspace;
 }
 
-template <int T>
-static cudaError_t qmm_launch_t(const QmmArgs& a, const QmmPlan& p, const CUtensorMap& map, cudaStream_t st) {
+template <int T, bool GATHER>
+static cudaError_t qmm_launch_g(const QmmArgs& a, const QmmPlan& p, const CUtensorMap& map, cudaStream_t st) {
   const size_t smem = QmmPipe<T>::smem((size_t)a.bn * a.nacc * 128);
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && configured[dev] < (int)smem) {
-    cudaError_t e = cudaFuncSetAttribute(qmm_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e =
+        cudaFuncSetAttribute(qmm_kernel<T, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured[dev] = (int)smem;
   }
   dim3 grid((unsigned)p.row_tiles, (unsigned)p.token_groups, (unsigned)p.ksplit);
-  return launch_pdl(qmm_kernel<T>, grid, dim3(QMM_THREADS), smem, st, a, map);
+  return launch_pdl(qmm_kernel<T, GATHER>, grid, dim3(QMM_THREADS), smem, st, a, map);
+}
+
+template <int T>
+static cudaError_t qmm_launch_t(const QmmArgs& a, const QmmPlan& p, const CUtensorMap& map, cudaStream_t st) {
+  return a.world > 1 ? qmm_launch_g<T, true>(a, p, map, st) : qmm_launch_g<T, false>(a, p, map, st);
 }
 
 #define GSQ_QMM_LAUNCH_CASE(TT) case TT: return qmm_launch_t<TT>(a, p, map, st);
