@@ -31,9 +31,25 @@ extern "C" {
 GSQ_API int gsq_rmsnorm(float* resid, const float* delta, int64_t rows, int64_t dim, const float* weight, float eps,
                         void* out, int out_dtype, gsq_stream_t stream);
 
-/* out[r,i] = silu(gu[r,i]) * gu[r,n+i] for a [rows, 2n] fp32 input holding
- * the gate projection's outputs then the up projection's. */
-GSQ_API int gsq_silu_mul(const float* gu, int64_t rows, int64_t n, void* out, int out_dtype, gsq_stream_t stream);
+/* out[r,i] = silu(gate[r,i]) * up[r,i] from a [rows, 2n] fp32 input: with
+ * group == 0 the gate projection's n outputs then the up projection's; with
+ * group g > 0 (n % g == 0) interleaved groups of g gate then g up outputs
+ * (the layout of an interleaved gate|up matrix, see gsq_qmv_swiglu). */
+GSQ_API int gsq_silu_mul(const float* gu, int64_t rows, int64_t n, int64_t group, void* out, int out_dtype,
+                         gsq_stream_t stream);
+
+/* The FFN's gate and up projections and their SwiGLU product in one fused
+ * matvec (decode, 0 < rows < 8): `packed` is a packed matrix of 2*n_out rows
+ * (K inputs) holding, per 16 rows, 8 rows of ffn_gate then the same 8 rows
+ * of ffn_up (n_out % 8 == 0); y[r,i] = silu(gate_i . x_r) * (up_i . x_r),
+ * [rows, n_out] in y_dtype -- the down projection's input, with no fp32
+ * round trip and no separate kernel.  Arguments and workspace as gsq_qmv
+ * for a 2*n_out-row matrix (gsq_qmv_workspace_size(qtype, 2*n_out, K,
+ * rows)).  Token counts of 8 and more use gsq_qmm on the same matrix, then
+ * gsq_silu_mul with group 8. */
+GSQ_API int gsq_qmv_swiglu(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t n_out, int64_t K,
+                           int64_t rows, void* y, int y_dtype, void* workspace, size_t workspace_bytes,
+                           gsq_stream_t stream);
 
 /* Gated-DeltaNet block of T consecutive tokens (the GDN layer of
  * qwen35.py:48-101; nk key heads, nv = multiple of nk value heads, value

@@ -10,6 +10,7 @@
 
 #include "gsq_common.cuh"
 #include "../../include/gsq_b200.h"
+#include "../../include/gsq_model.h"
 
 #include "gsq_host.h"
 
@@ -121,6 +122,29 @@ int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_
   cudaError_t e = qmv_run(qtype, x, x_dtype, packed, N, K, (int)rows, y, y_dtype, workspace, p, device_error_word(),
                           (cudaStream_t)stream);
   return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_qmv launch");
+}
+
+int gsq_qmv_swiglu(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t n_out, int64_t K,
+                   int64_t rows, void* y, int y_dtype, void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
+  if (n_out < 0 || n_out % 8) return fail(GSQ_ERR_SIZE, "gsq_qmv_swiglu: n_out must be a multiple of 8");
+  const int64_t N = 2 * n_out;  // packed rows: 8 gate rows, then the same 8 up rows, per 16
+  int rc = check_matrix(qtype, packed, N, K);
+  if (rc) return rc;
+  if (rows < 0 || rows >= 8) return fail(GSQ_ERR_SIZE, "gsq_qmv_swiglu takes 0..7 rows (%lld)", (long long)rows);
+  if (rows == 0 || N == 0) return GSQ_OK;
+  if (!x || !y) return fail(GSQ_ERR_ARG, "null x or y");
+  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return fail(GSQ_ERR_ARG, "unsupported dtype");
+  if (!aligned(x, 16) || !aligned(y, dtype_size(y_dtype)))
+    return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned and y aligned to its dtype");
+  const QmvPlan p = qmv_plan(qtype, N, K, (int)rows);
+  if (p.ctas <= 0)
+    return fail(GSQ_ERR_SIZE, "matrix too large for the matvec (N=%lld, K=%lld)", (long long)N, (long long)K);
+  if (p.workspace > 0 && (!workspace || workspace_bytes < p.workspace || !aligned(workspace, 256)))
+    return fail(GSQ_ERR_WORKSPACE, "gsq_qmv_swiglu needs %zu workspace bytes (256-byte aligned), got %zu",
+                p.workspace, workspace_bytes);
+  cudaError_t e = qmv_run(qtype, x, x_dtype, packed, N, K, (int)rows, y, y_dtype, workspace, p, device_error_word(),
+                          (cudaStream_t)stream, nullptr, 1);
+  return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_qmv_swiglu launch");
 }
 
 size_t gsq_gather_region_bytes(int64_t rows, int64_t ntot) {

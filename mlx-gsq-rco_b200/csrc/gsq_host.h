@@ -62,7 +62,7 @@ struct QmvGather {
 
 cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int rows,
                     void* y, int y_dtype, void* ws, const QmvPlan& p, int* err, cudaStream_t st,
-                    const QmvGather* gather = nullptr);
+                    const QmvGather* gather = nullptr, int glu = 0);
 size_t qmv_gather_inbox_offset(int64_t rows, int64_t ntot);
 size_t qmv_gather_region_bytes(int64_t rows, int64_t ntot);
 

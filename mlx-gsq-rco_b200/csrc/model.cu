@@ -167,13 +167,21 @@ __global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(float* resid, cons
   for (int64_t i = threadIdx.x; i < dim; i += blockDim.x) store_out(out, dt, r * dim + i, x[i] * inv * w[i]);
 }
 
-__global__ void silu_mul_kernel(const float* gu, int64_t rows, int64_t n, void* out, int dt) {
+// group 0: gu = [gate | up] halves; group g > 0: gate and up interleaved in
+// groups of g columns (g gate columns, then the same g up columns).
+__global__ void silu_mul_kernel(const float* gu, int64_t rows, int64_t n, int64_t group, void* out, int dt) {
   pdl_launch_dependents();
   pdl_wait();
   const int64_t total = rows * n;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / n, c = i - r * n;
-    store_out(out, dt, i, silu(gu[r * 2 * n + c]) * gu[r * 2 * n + n + c]);
+    int64_t gcol = c, ucol = n + c;
+    if (group > 0) {
+      const int64_t q = c / group;
+      gcol = c + q * group;
+      ucol = gcol + group;
+    }
+    store_out(out, dt, i, silu(gu[r * 2 * n + gcol]) * gu[r * 2 * n + ucol]);
   }
 }
 
@@ -598,14 +606,15 @@ int gsq_rmsnorm(float* resid, const float* delta, int64_t rows, int64_t dim, con
   return launched("gsq_rmsnorm");
 }
 
-int gsq_silu_mul(const float* gu, int64_t rows, int64_t n, void* out, int out_dtype, gsq_stream_t stream) {
+int gsq_silu_mul(const float* gu, int64_t rows, int64_t n, int64_t group, void* out, int out_dtype,
+                 gsq_stream_t stream) {
   if (!gu || !out) return fail(GSQ_ERR_ARG, "gsq_silu_mul: null pointer");
-  if (rows < 0 || n <= 0) return fail(GSQ_ERR_SIZE, "gsq_silu_mul: bad shape");
+  if (rows < 0 || n <= 0 || group < 0 || (group > 0 && n % group)) return fail(GSQ_ERR_SIZE, "gsq_silu_mul: bad shape");
   if (!dt_ok(out_dtype)) return fail(GSQ_ERR_ARG, "gsq_silu_mul: bad output dtype");
   if (rows == 0) return GSQ_OK;
   const int64_t total = rows * n;
   const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, (cudaStream_t)stream, gu, rows, n, out, out_dtype);
+  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, (cudaStream_t)stream, gu, rows, n, group, out, out_dtype);
   return launched("gsq_silu_mul");
 }
 

@@ -88,6 +88,7 @@ struct QmvArgs {
   int cb, rowb, stage;  // ring geometry: blocks per stage, staged row stride, stage bytes
   int pre;              // stages issued before the activations are quantised (<= ns)
   int xbulk;            // one 16-bit activation row, copied into shared memory in bulk
+  int glu;              // SwiGLU epilogue (gsq_qmv_swiglu): y = silu(gate) * up, N/2 columns
   // Fused row gather (world > 1): output rows [row0, row0 + N) of ntot are
   // stored into every rank's gather region (fp32, [rows][ntot]) over
   // NVLink, and the regions' flag words synchronise the ranks at the end.
@@ -123,6 +124,26 @@ __device__ __forceinline__ void store_y(const QmvArgs& a, int batch, int64_t rr,
 #pragma unroll
   for (int p = 0; p < QMV_GATHER_MAX; p++)
     if (p < a.world && p != a.rank) st_pair_sys(a.ginbox[p] + slot + off, v, ep);
+}
+
+// Final value v of packed row 16*tile + r for activation row `batch`, by the
+// lanes in `mask` (the tile's 16 rows per activation row, lane = b*16 + r);
+// `ok`: this lane's row exists.  With the SwiGLU epilogue the packed rows of a
+// tile are 8 gate rows then the same 8 up rows (gsq_qmv_swiglu): lane r < 8
+// takes its up value from lane r + 8 and stores silu(gate) * up as output
+// column 8*tile + r.
+template <bool GATHER>
+__device__ __forceinline__ void final_store(const QmvArgs& a, unsigned mask, int batch, int64_t tile, int r, float v,
+                                            bool ok, unsigned ep) {
+  if constexpr (!GATHER) {
+    if (a.glu) {
+      const float up = __shfl_xor_sync(mask, v, 8);
+      if (ok && r < 8)
+        store_out(a.y, a.y_dtype, (int64_t)batch * (a.N >> 1) + tile * 8 + r, v / (1.f + __expf(-v)) * up);
+      return;
+    }
+  }
+  if (ok) store_y<GATHER>(a, batch, tile * 16 + r, v, ep);
 }
 
 // Call count of this call on the gather region (read after griddepcontrol.wait:
@@ -563,7 +584,7 @@ __device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t
   const int b = lane >> 4, r = lane & 15;
   const int batch = btile * NB + b;
   const int64_t rr = tile * 16 + r;
-  if (batch < a.rows && rr < a.N) store_y<GATHER>(a, batch, rr, sum, ep);
+  final_store<GATHER>(a, NB == 1 ? 0xffffu : 0xffffffffu, batch, tile, r, sum, batch < a.rows && rr < a.N, ep);
 }
 
 // Global combination of one piece of a tile shared with other CTAs (other
@@ -616,7 +637,7 @@ __device__ void combine_piece(const QmvArgs& a, int btile, int slice, int C, int
     const int b = lane >> 4, r = lane & 15;
     const int batch = btile * NB + b;
     const int64_t rr = tile * 16 + r;
-    if (batch < a.rows && rr < a.N) store_y<GATHER>(a, batch, rr, sum, ep);
+    final_store<GATHER>(a, NB == 1 ? 0xffffu : 0xffffffffu, batch, tile, r, sum, batch < a.rows && rr < a.N, ep);
   }
   if (lane == 0) *tk = 0u;
 }
@@ -1016,7 +1037,7 @@ __global__ void __launch_bounds__(QMV_THREADS, 2) qmv_kernel(const QmvArgs a) {
         const int b = lane >> 4, r = lane & 15;
         const int batch = btile * NB + b;
         const int64_t rr = tile * 16 + r;
-        if (lane < NB * 16 && batch < a.rows && rr < a.N) store_y<GATHER>(a, batch, rr, v, gep);
+        final_store<GATHER>(a, 0xffffffffu, batch, tile, r, v, lane < NB * 16 && batch < a.rows && rr < a.N, gep);
       }
       if (++rbuf == RB) { rbuf = 0; rph ^= 1u; }
       seg_no++;
@@ -1206,8 +1227,9 @@ size_t qmv_gather_region_bytes(int64_t rows, int64_t ntot) {
 
 cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int rows,
                     void* y, int y_dtype, void* ws, const QmvPlan& p, int* err, cudaStream_t st,
-                    const QmvGather* gather) {
+                    const QmvGather* gather, int glu) {
   if (p.ctas <= 0) return cudaErrorInvalidValue;
+  if (glu && ((N & 15) || (gather && gather->world > 1))) return cudaErrorInvalidValue;
   uint8_t* w = static_cast<uint8_t*>(ws);
   QmvArgs a;
   a.packed = packed;
@@ -1235,6 +1257,7 @@ cudaError_t qmv_run(int t, const void* x, int x_dtype, const uint8_t* packed, in
   a.rowb = p.rowb;
   a.stage = p.stage;
   a.pre = p.pre;
+  a.glu = glu ? 1 : 0;
   a.world = 0;
   a.rank = 0;
   a.row0 = 0;

@@ -12,10 +12,13 @@ SwiGLU FFN 17408, vocab 248320.  Here the same model runs on B200:
     rows, the tcgen05 dequant-matmul above), with fp16 activations in and
     fp32 out;
   * the projections of a layer that read the same input and share a quant
-    type are joined row-wise at load time (ffn_gate|ffn_up,
-    attn_qkv|attn_gate, attn_q|attn_k|attn_v): a packed matrix is rows of
-    whole blocks, so the join is a byte concatenation and each layer makes
-    fewer, larger calls;
+    type are joined row-wise at load time (attn_qkv|attn_gate,
+    attn_q|attn_k|attn_v, and ffn_gate|ffn_up interleaved in groups of 8
+    rows): a packed matrix is rows of whole blocks, so the join is a byte
+    rearrangement and each layer makes fewer, larger calls;
+  * the FFN's gate|up matvec ends in the SwiGLU product (``gsq_qmv_swiglu``:
+    each 16-row tile holds 8 gate rows and their 8 up rows, so the epilogue
+    pairs them in-lane) and writes the down projection's fp16 input;
   * the work between projections is in ``include/gsq_model.h``: residual
     add + RMSNorm, SiLU-mul, the gated-DeltaNet block (conv, norms, gates,
     recurrence, gated norm) and the single-token attention step; prefill
@@ -171,9 +174,14 @@ def random_weights(cfg: Qwen35Config, device, seed: int = 0, type_mix: dict[str,
 
 
 class _Packed:
-    """A packed projection: flat uint8 payload of n rows x k inputs."""
+    """A packed projection: flat uint8 payload of n rows x k inputs.
 
-    def __init__(self, parts: list[PackedWeight]):
+    Several same-type projections of one input are joined row-wise; with
+    ``interleave=g`` two of them (gate, up) alternate in groups of g rows
+    (g gate rows, then the same g up rows), the layout of the fused SwiGLU
+    matvec (``gsq_qmv_swiglu``)."""
+
+    def __init__(self, parts: list[PackedWeight], interleave: int = 0):
         q = {p.quantization_type for p in parts}
         k = {p.logical_shape[1] for p in parts}
         if len(q) != 1 or len(k) != 1:
@@ -181,12 +189,42 @@ class _Packed:
                              + ", ".join(p.name for p in parts))
         self.qtype, self.k = q.pop(), k.pop()
         self.n = sum(p.logical_shape[0] for p in parts)
-        self.data = parts[0].data if len(parts) == 1 else torch.cat([p.data.reshape(-1) for p in parts])
+        self.interleave = interleave
+        if interleave:
+            if len(parts) != 2 or parts[0].logical_shape != parts[1].logical_shape or \
+                    parts[0].logical_shape[0] % interleave:
+                raise ValueError("interleaving needs two projections of equal shape, rows a multiple of the group")
+            rb = parts[0].num_bytes // parts[0].logical_shape[0]
+            g = [p.data.reshape(-1, interleave, rb) for p in parts]
+            self.data = torch.stack(g, dim=1).reshape(-1)
+        else:
+            self.data = parts[0].data if len(parts) == 1 else torch.cat([p.data.reshape(-1) for p in parts])
         self.nbytes = self.data.numel()
 
     def __call__(self, x16: torch.Tensor) -> torch.Tensor:
         return quantized_matvec(x16, self.data, qtype=self.qtype, out_features=self.n, in_features=self.k,
                                 out_dtype=torch.float32)
+
+    def swiglu(self, x16: torch.Tensor, out_dtype=torch.float16) -> torch.Tensor:
+        """silu(gate . x) * (up . x) of an interleaved gate|up join: one fused
+        matvec below 8 rows, else the matmul then ``gsq_silu_mul``."""
+        if self.interleave != 8:
+            raise ValueError("swiglu needs the gate|up join interleaved in groups of 8")
+        rows = x16.shape[0]
+        if rows >= 8:
+            return silu_mul(self(x16), out_dtype, group=8)
+        from ..quant.layouts import type_id
+        dev = x16.device
+        lib = _lib.load()
+        tid = type_id(self.qtype)
+        need = lib.gsq_qmv_workspace_size(tid, self.n, self.k, rows)
+        ws = _lib.workspaces.get(dev, need, "qmv")
+        out = torch.empty((rows, self.n // 2), dtype=out_dtype, device=dev)
+        _lib.check(lib.gsq_qmv_swiglu(tid, x16.data_ptr(), _lib.DTYPE_CODES[x16.dtype], self.data.data_ptr(),
+                                      self.n // 2, self.k, rows, out.data_ptr(), _lib.DTYPE_CODES[out_dtype],
+                                      ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                                      _stream(dev)))
+        return out
 
 
 def _stream(dev):
@@ -204,11 +242,11 @@ def rmsnorm(resid: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tenso
     return out
 
 
-def silu_mul(gu: torch.Tensor, out_dtype=torch.float16) -> torch.Tensor:
+def silu_mul(gu: torch.Tensor, out_dtype=torch.float16, group: int = 0) -> torch.Tensor:
     rows, n2 = gu.shape
     out = torch.empty((rows, n2 // 2), dtype=out_dtype, device=gu.device)
-    _lib.check(_lib.load().gsq_silu_mul(gu.data_ptr(), rows, n2 // 2, out.data_ptr(), _lib.DTYPE_CODES[out_dtype],
-                                        _stream(gu.device)))
+    _lib.check(_lib.load().gsq_silu_mul(gu.data_ptr(), rows, n2 // 2, group, out.data_ptr(),
+                                        _lib.DTYPE_CODES[out_dtype], _stream(gu.device)))
     return out
 
 
@@ -231,7 +269,7 @@ class Qwen35:
             L = {"linear": cfg.is_linear(i),
                  "attn_norm": w[p + "attn_norm.weight"].float().contiguous(),
                  "post_norm": w[p + "post_attention_norm.weight"].float().contiguous(),
-                 "gate_up": _Packed([w[p + "ffn_gate.weight"], w[p + "ffn_up.weight"]]),
+                 "gate_up": _Packed([w[p + "ffn_gate.weight"], w[p + "ffn_up.weight"]], interleave=8),
                  "down": _Packed([w[p + "ffn_down.weight"]])}
             if L["linear"]:
                 L["qkvz"] = _Packed([w[p + "attn_qkv.weight"], w[p + "attn_gate.weight"]])
@@ -354,7 +392,7 @@ class Qwen35:
                 o = self._attn_decode(L, p) if pos0 is None else self._attn_prefill(L, p, pos0)
                 d = L["o"](o)
             h2 = rmsnorm(x, d, L["post_norm"], self.eps)
-            delta = L["down"](silu_mul(L["gate_up"](h2)))
+            delta = L["down"](L["gate_up"].swiglu(h2))
         return delta
 
     # ---- public ----

@@ -159,3 +159,35 @@ def test_graph_decode_matches_eager(setup):
         assert e <= 1e-5, f"graph step {i}: rel {e}"
     assert model.n_pos == 9 + 5
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("qtype", ["IQ2_XS", "IQ2_S", "Q4_K", "IQ4_XS"])
+@pytest.mark.parametrize("rows", [1, 3])
+@pytest.mark.parametrize("n_out,k", [(1024, 5120), (256, 17408)])
+def test_fused_swiglu_matvec(qtype, rows, n_out, k):
+    """gsq_qmv_swiglu on an interleaved gate|up join against two separate
+    matvecs and the SwiGLU product in fp32 (rows 1: one-row tiles; 3: two-row
+    tiles; 17408 inputs: K split over CTAs)."""
+    from gsq_b200.models.qwen35 import _Packed
+    from gsq_b200.quant.synthetic import random_matrix_torch
+    from gsq_b200.runtime import PackedWeight
+    from gsq_b200.runtime.kernels import quantized_matvec
+    dev = torch.device("cuda:0")
+    g = random_matrix_torch(qtype, n_out, k, seed=11, device=dev)
+    u = random_matrix_torch(qtype, n_out, k, seed=12, device=dev)
+    pg = PackedWeight.from_packed("gate", g, qtype, (n_out, k), device=None)
+    pu = PackedWeight.from_packed("up", u, qtype, (n_out, k), device=None)
+    joined = _Packed([pg, pu], interleave=8)
+    x = torch.randn(rows, k, device=dev, generator=torch.Generator(device=dev).manual_seed(2)).to(torch.float16)
+    y = joined.swiglu(x, out_dtype=torch.float32)
+    yg = quantized_matvec(x, g, qtype=qtype, out_features=n_out, in_features=k, out_dtype=torch.float32)
+    yu = quantized_matvec(x, u, qtype=qtype, out_features=n_out, in_features=k, out_dtype=torch.float32)
+    ref = F.silu(yg) * yu
+    assert y.shape == (rows, n_out)
+    assert rel(y, ref) <= 1e-5, rel(y, ref)
+    # the matmul path (8 rows and more) on the same join, then gsq_silu_mul with group 8
+    xm = torch.randn(12, k, device=dev, generator=torch.Generator(device=dev).manual_seed(3)).to(torch.float16)
+    ym = joined.swiglu(xm, out_dtype=torch.float32)
+    refm = F.silu(quantized_matvec(xm, g, qtype=qtype, out_features=n_out, in_features=k, out_dtype=torch.float32)) \
+        * quantized_matvec(xm, u, qtype=qtype, out_features=n_out, in_features=k, out_dtype=torch.float32)
+    assert rel(ym, refm) <= 1e-5, rel(ym, refm)

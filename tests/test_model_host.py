@@ -74,7 +74,11 @@ def test_glue_abi_validation():
     fake = 1 << 20  # never dereferenced: every call fails validation first
     assert lib.gsq_rmsnorm(None, None, 1, 16, fake, 1e-6, fake, 1, None) == _lib.GSQ_ERR_ARG
     assert lib.gsq_rmsnorm(fake, None, 1, 16, fake, 1e-6, fake, 9, None) == _lib.GSQ_ERR_ARG
-    assert lib.gsq_silu_mul(fake, 1, 0, fake, 1, None) == _lib.GSQ_ERR_SIZE
+    assert lib.gsq_silu_mul(fake, 1, 0, 0, fake, 1, None) == _lib.GSQ_ERR_SIZE
+    assert lib.gsq_silu_mul(fake, 1, 12, 8, fake, 1, None) == _lib.GSQ_ERR_SIZE  # n not a multiple of the group
+    q4k = 12
+    assert lib.gsq_qmv_swiglu(q4k, fake, 1, fake, 12, 256, 1, fake, 1, None, 0, None) == _lib.GSQ_ERR_SIZE
+    assert lib.gsq_qmv_swiglu(q4k, fake, 1, fake, 16, 256, 8, fake, 1, None, 0, None) == _lib.GSQ_ERR_SIZE
     assert lib.gsq_gdn_scratch_bytes(1, 16, 48) == 0  # one token runs as a single kernel
     assert lib.gsq_gdn_scratch_bytes(2, 16, 48) > 0
 
@@ -90,3 +94,23 @@ def test_glue_abi_validation():
                                None) == _lib.GSQ_ERR_SIZE
     assert lib.gsq_attn_decode(fake, 24, 4, fake, fake, 1e-6, 65, 1e7, fake, fake, 256, fake, fake, 1,
                                None) == _lib.GSQ_ERR_SIZE
+
+
+def test_interleaved_join():
+    import oracle
+    k = 256
+    a = random_matrix("IQ2_XS", 32, k, seed=3)
+    b = random_matrix("IQ2_XS", 32, k, seed=4)
+    pa = PackedWeight.from_packed("gate", a, "IQ2_XS", (32, k), device=None)
+    pb = PackedWeight.from_packed("up", b, "IQ2_XS", (32, k), device=None)
+    j = _Packed([pa, pb], interleave=8)
+    rows = oracle.dequantize(j.data.numpy(), "IQ2_XS").reshape(64, k)
+    ga = oracle.dequantize(a, "IQ2_XS").reshape(32, k)
+    gb = oracle.dequantize(b, "IQ2_XS").reshape(32, k)
+    for t in range(4):
+        np.testing.assert_array_equal(rows[16 * t:16 * t + 8], ga[8 * t:8 * t + 8])
+        np.testing.assert_array_equal(rows[16 * t + 8:16 * t + 16], gb[8 * t:8 * t + 8])
+    with pytest.raises(ValueError):
+        _Packed([pa, PackedWeight.from_packed("c", random_matrix("IQ2_XS", 24, k, seed=5), "IQ2_XS", (24, k),
+                                              device=None)], interleave=8)
+
