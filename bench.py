@@ -20,9 +20,10 @@ larger than the 126 MB L2, so no step reuses another's weights from L2).
   qmm_prefill config 3 at M=512 (tcgen05 QMM) in TFLOP/s vs measured bf16 peak;
               on one GPU also M = 16, 182, 2048 against the max(FLOP, byte)
               roofline (``by_M``).
-  model       config 4 on one GPU: the 27B Qwen3.5-hybrid decoder with
-              random-init packed weights; prefill (182 and 512 tokens) and
-              batch-1 decode tok/s (CUDA-graph replay per token).
+  model       config 4: the 27B Qwen3.5-hybrid decoder with random-init
+              packed weights; prefill (182 and 512 tokens) and batch-1
+              decode tok/s (CUDA-graph replay per token); with --gpus N
+              (config 5) split by output rows over the N ranks.
   cpu_baseline the reference's CPU path (gguf-py dequantize, which
               mlx_gsq/quant/reference.py:10-18 calls, + numpy matvec) on a
               bounded sample of the same workload.
@@ -239,32 +240,47 @@ def qmm_by_m(dev, pk, ms=(16, 182, 2048)):
     return out
 
 
-def model_bench(dev, pk, prompt=182, decode_tokens=64, prefill_m=512):
+def model_bench(dev, pk, world=1, prompt=182, decode_tokens=64, prefill_m=512):
     """Config 4 (BASELINE): the Qwen3.5-hybrid 27B decoder (64 layers) with
-    random-init packed weights of the config's type mix, one GPU.  A
-    ``prompt``-token prefill, then ``decode_tokens`` greedy decode tokens at
-    batch 1, each a replay of the captured decode-step graph (embedding ->
-    64 layers -> LM head -> argmax); and a ``prefill_m``-token prefill.
-    CUDA events around each timed region; every decode token reads all
-    packed projections (12 GB, ~90x L2)."""
+    random-init packed weights of the config's type mix.  A ``prompt``-token
+    prefill, then ``decode_tokens`` greedy decode tokens at batch 1, each a
+    replay of the captured decode-step graph (embedding -> 64 layers -> LM
+    head -> argmax); and a ``prefill_m``-token prefill.  CUDA events around
+    each timed region; every decode token reads all packed projections
+    (12 GB, ~90x L2).  With ``world`` > 1 (config 5) every packed projection
+    is split by output rows over the ranks (the decode gathers fused into the
+    matvec, the prefill ones NCCL all-gathers); times are the max over
+    ranks."""
     import torch
+    import torch.distributed as dist
     from gsq_b200.models import Qwen35Config, build_qwen35, random_weights
 
     cfg = Qwen35Config()
-    w = random_weights(cfg, dev, seed=0)
-    model = build_qwen35(w, cfg, dev, max_len=prefill_m + decode_tokens + 16)
+    w = random_weights(cfg, dev, seed=0)  # the same bytes on every rank; each keeps its rows
+    model = build_qwen35(w, cfg, dev, max_len=prefill_m + decode_tokens + 16,
+                         group=dist.group.WORLD if world > 1 else None)
     del w
     torch.cuda.empty_cache()
     gen = torch.Generator(device=dev).manual_seed(1)
 
+    def max_over_ranks(t):
+        if world > 1:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
     def timed(fn, reps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
             fn()
         e1.record()
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / 1e3 / reps
+        return max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps)
 
     out = {"workload": "config 4: Qwen3.5-hybrid 27B (64 layers, 48 gated-DeltaNet + 16 GQA), random-init packed "
                        "weights (embedding/LM head Q6_K, FFN gate/up IQ2_XS|IQ2_S, down Q4_K, attention IQ3_S|IQ4_XS)",
@@ -282,19 +298,19 @@ def model_bench(dev, pk, prompt=182, decode_tokens=64, prefill_m=512):
     model.decode_step()
     model.capture_decode()
     model.replay_decode(3)  # warm-up replays
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    model.replay_decode(decode_tokens)
-    e1.record()
-    torch.cuda.synchronize()
-    t = e0.elapsed_time(e1) / 1e3 / decode_tokens
+    t = timed(lambda: model.replay_decode(decode_tokens), 1) / decode_tokens
     gbs = out["packed_bytes_per_token"] / t / 1e9
     out.update({"decode_tokens": decode_tokens, "decode_ms_per_token": round(t * 1e3, 3),
                 "decode_tok_s": round(1.0 / t, 1), "decode_packed_gbs": round(gbs, 1),
                 "decode_roofline_frac": round(gbs / pk["hbm"], 4),
                 "decode_note": "batch 1 after the prompt prefill; each token one CUDA-graph replay of the whole "
-                               "step; roofline = packed weight bytes per token / time vs measured HBM copy peak"})
+                               "step; roofline = packed weight bytes per token / time vs measured HBM copy peak"
+                               + (f" x {world} GPUs" if world > 1 else "")})
+    if world > 1:
+        out["decode_roofline_frac"] = round(gbs / (pk["hbm"] * world), 4)
+        out["parallelism"] = (f"tp{world}: every packed projection split by output rows; decode gathers fused "
+                              "into the matvec over NVLink, prefill gathers by NCCL all-gather")
+    model.close()
     del model
     torch.cuda.empty_cache()
     return out
@@ -562,7 +578,7 @@ def main():
 
     if qmm is not None and world == 1:
         qmm["by_M"] = qmm_by_m(dev, pk)
-    model = model_bench(dev, pk) if world == 1 and not args.no_model else None
+    model = model_bench(dev, pk, world) if not args.no_model else None
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:

@@ -38,6 +38,7 @@ import math
 from dataclasses import dataclass
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 
 from .. import _lib
@@ -199,11 +200,42 @@ class _Packed:
             self.data = torch.stack(g, dim=1).reshape(-1)
         else:
             self.data = parts[0].data if len(parts) == 1 else torch.cat([p.data.reshape(-1) for p in parts])
-        self.nbytes = self.data.numel()
+        self.nbytes = self.data.numel()  # the whole projection's payload (all ranks together)
+        self.world, self.rank, self.group, self.region = 1, 0, None, None
+        self.n_local, self.row0 = self.n, 0
+
+    def shard(self, group) -> None:
+        """Keep this rank's rows [r*n/P, (r+1)*n/P) (a byte slice of the
+        payload) and create the call site's gather region (collective: every
+        rank shards the same projections in the same order)."""
+        from ..parallel import GatherRegion, shard_bounds
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        lo, hi = shard_bounds(self.n, world, rank)
+        if self.interleave and lo % (2 * self.interleave):
+            raise ValueError("a rank's rows must hold whole gate|up groups")
+        rb = self.nbytes // self.n
+        self.data = self.data[lo * rb:hi * rb].clone()
+        self.world, self.rank, self.group = world, rank, group
+        self.n_local, self.row0 = hi - lo, lo
+        self.region = GatherRegion(1, self.n, group=group, device=self.data.device)
+
+    def close(self) -> None:
+        if self.region is not None:
+            self.region.close()
+            self.region = None
 
     def __call__(self, x16: torch.Tensor) -> torch.Tensor:
-        return quantized_matvec(x16, self.data, qtype=self.qtype, out_features=self.n, in_features=self.k,
-                                out_dtype=torch.float32)
+        if self.world == 1:
+            return quantized_matvec(x16, self.data, qtype=self.qtype, out_features=self.n, in_features=self.k,
+                                    out_dtype=torch.float32)
+        if x16.shape[0] == 1:  # decode: the gather is fused into the matvec (every rank's rows, over NVLink)
+            from ..parallel import quantized_matvec_gather
+            return quantized_matvec_gather(x16, self.data, qtype=self.qtype, out_features=self.n_local,
+                                           in_features=self.k, region=self.region, row0=self.row0)
+        from ..parallel import gather_rows
+        y = quantized_matvec(x16, self.data, qtype=self.qtype, out_features=self.n_local, in_features=self.k,
+                             out_dtype=torch.float32)
+        return gather_rows(y, self.group)
 
     def swiglu(self, x16: torch.Tensor, out_dtype=torch.float16) -> torch.Tensor:
         """silu(gate . x) * (up . x) of an interleaved gate|up join: one fused
@@ -211,7 +243,7 @@ class _Packed:
         if self.interleave != 8:
             raise ValueError("swiglu needs the gate|up join interleaved in groups of 8")
         rows = x16.shape[0]
-        if rows >= 8:
+        if rows >= 8 or self.world > 1:
             return silu_mul(self(x16), out_dtype, group=8)
         from ..quant.layouts import type_id
         dev = x16.device
@@ -251,9 +283,16 @@ def silu_mul(gu: torch.Tensor, out_dtype=torch.float16, group: int = 0) -> torch
 
 
 class Qwen35:
-    """The model on one GPU, built from GGUF-named weights (``build_qwen35``)."""
+    """The model, built from GGUF-named weights (``build_qwen35``).
 
-    def __init__(self, weights: dict, cfg: Qwen35Config, device, max_len: int = 2304):
+    With ``group`` (an initialised process group of P ranks, one GPU each;
+    BASELINE config 5) every packed projection is split by output rows over
+    the ranks: decode tokens gather the rows inside the matvec kernel
+    (``gsq_qmv_gather``), prompts with an NCCL all-gather after the matmul.
+    Norms, the gated-DeltaNet and attention blocks run on every rank on the
+    gathered (identical) vectors."""
+
+    def __init__(self, weights: dict, cfg: Qwen35Config, device, max_len: int = 2304, group=None):
         cfg.check()
         self.cfg, self.dev, self.max_len = cfg, torch.device(device), max_len
         self.eps = cfg.rms_norm_eps
@@ -289,6 +328,10 @@ class Qwen35:
                 L["k_cache"] = torch.zeros(max_len, nkv, hd, device=self.dev)
                 L["v_cache"] = torch.zeros(max_len, nkv, hd, device=self.dev)
             self.layers.append(L)
+        self.world = dist.get_world_size(group) if group is not None else 1
+        if self.world > 1:
+            for pk in self._projections():
+                pk.shard(group)
         self.pos = torch.zeros(1, dtype=torch.int32, device=self.dev)   # next position (decode)
         self.cur_id = torch.zeros(1, dtype=torch.int32, device=self.dev)  # token to feed next (decode)
         self.n_pos = 0  # host copy of the position (prefill bookkeeping)
@@ -296,16 +339,24 @@ class Qwen35:
         inv = cfg.rope_theta ** (-torch.arange(0, cfg.rotary_dim, 2, dtype=torch.float32) / cfg.rotary_dim)
         self._inv_freq = inv.to(self.dev)
 
+    def _projections(self) -> list:
+        """Every packed projection, in a fixed order (the same on all ranks)."""
+        out = [self.lm_head]
+        for L in self.layers:
+            out += [L[key] for key in ("qkvz", "out", "qkv", "o", "gate_up", "down") if key in L]
+        return out
+
+    def close(self) -> None:
+        """Release the gather regions (collective with ``group``)."""
+        self._graph = None
+        for pk in self._projections():
+            pk.close()
+
     # ---- sizes ----
     def packed_bytes_per_token(self) -> int:
-        """Packed weight bytes one decode token reads (every projection and
-        the LM head; one embedding row)."""
-        total = self.lm_head.nbytes + self.embed.num_bytes // self.cfg.vocab_size
-        for L in self.layers:
-            for key in ("gate_up", "down", "qkvz", "out", "qkv", "o"):
-                if key in L:
-                    total += L[key].nbytes
-        return total
+        """Packed weight bytes one decode token reads over all ranks (every
+        projection and the LM head; one embedding row)."""
+        return sum(pk.nbytes for pk in self._projections()) + self.embed.num_bytes // self.cfg.vocab_size
 
     def reset(self) -> None:
         for L in self.layers:
@@ -478,7 +529,9 @@ class Qwen35:
         return self._graph_logits
 
 
-def build_qwen35(weights: dict, cfg: Qwen35Config | None = None, device="cuda", max_len: int = 2304) -> Qwen35:
+def build_qwen35(weights: dict, cfg: Qwen35Config | None = None, device="cuda", max_len: int = 2304,
+                 group=None) -> Qwen35:
     """The model from GGUF-named weights (``qwen35.py:104-152``): packed
-    projections as ``PackedWeight`` on the device, plain tensors as arrays."""
-    return Qwen35(weights, cfg or Qwen35Config(), device, max_len=max_len)
+    projections as ``PackedWeight`` on the device, plain tensors as arrays;
+    ``group``: split every packed projection over the group's ranks."""
+    return Qwen35(weights, cfg or Qwen35Config(), device, max_len=max_len, group=group)
