@@ -1,4 +1,4 @@
 """Runtime: packed weight container and the CUDA kernel layer."""
-from .store import PackedWeight
+from .store import PackedModelStore, PackedWeight
 
-__all__ = ["PackedWeight"]
+__all__ = ["PackedModelStore", "PackedWeight"]

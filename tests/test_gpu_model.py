@@ -191,3 +191,20 @@ def test_fused_swiglu_matvec(qtype, rows, n_out, k):
     refm = F.silu(quantized_matvec(xm, g, qtype=qtype, out_features=n_out, in_features=k, out_dtype=torch.float32)) \
         * quantized_matvec(xm, u, qtype=qtype, out_features=n_out, in_features=k, out_dtype=torch.float32)
     assert rel(ym, refm) <= 1e-5, rel(ym, refm)
+
+
+def test_model_from_gguf_and_container(setup, tmp_path):
+    """The model's weights written as a GGUF checkpoint, read back (directly,
+    and through the packed container) and built: the same logits as the model
+    built from the weights in memory."""
+    from gsq_b200.gguf import GGUFReader, convert_gguf_to_safetensors, write_model_gguf
+    from gsq_b200.runtime import PackedModelStore
+    dev, w = setup
+    src = write_model_gguf(tmp_path / "tiny.gguf", w, {"general.architecture": "qwen35"})
+    prompt = torch.arange(10, dtype=torch.int32, device=dev) * 13 % CFG.vocab_size
+    ref = build_qwen35(w, CFG, dev, max_len=32).prefill(prompt)
+    from_gguf = build_qwen35(GGUFReader(src).model_weights(dev), CFG, dev, max_len=32).prefill(prompt)
+    assert torch.equal(from_gguf, ref)
+    dst = convert_gguf_to_safetensors(src, tmp_path / "tiny.safetensors")
+    from_store = build_qwen35(PackedModelStore(dst, device=dev).model_weights(), CFG, dev, max_len=32).prefill(prompt)
+    assert torch.equal(from_store, ref)
