@@ -208,3 +208,56 @@ def test_model_from_gguf_and_container(setup, tmp_path):
     dst = convert_gguf_to_safetensors(src, tmp_path / "tiny.safetensors")
     from_store = build_qwen35(PackedModelStore(dst, device=dev).model_weights(), CFG, dev, max_len=32).prefill(prompt)
     assert torch.equal(from_store, ref)
+
+
+@pytest.mark.parametrize("T", [64, 200])
+def test_gdn_prompt_matches_token_by_token(T):
+    """gsq_gdn over a T-token prompt (conv/gate kernel, the scan over 16-column
+    blocks, the gated-norm kernel) against T one-token calls (the single
+    kernel of a decode token) on the same inputs, at the model's head counts
+    (16 key / 48 value heads): the same outputs, final state and conv window."""
+    from gsq_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    nk, nv = 16, 48
+    C = 2 * nk * 128 + nv * 128
+    g = torch.Generator(device=dev).manual_seed(7)
+    proj = torch.randn(T, C + nv * 128, device=dev, generator=g)
+    ab = (torch.randn(T, 2 * nv, device=dev, generator=g) * 1.5).half()
+    cw = torch.randn(C, 4, device=dev, generator=g) * 0.3
+    A = -torch.exp(torch.rand(nv, device=dev, generator=g) * 2)
+    dtb = torch.randn(nv, device=dev, generator=g) * 0.5
+    nw = 1 + 0.05 * torch.randn(128, device=dev, generator=g)
+    state0 = torch.randn(nv, 128, 128, device=dev, generator=g) * 0.05
+    conv0 = torch.randn(4, C, device=dev, generator=g)
+
+    def call(rows, state, conv, pos, out):
+        need = lib.gsq_gdn_scratch_bytes(rows.shape[0], nk, nv)
+        scratch = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+        _lib.check(lib.gsq_gdn(rows.data_ptr(), rows.stride(0), ab_rows(rows).data_ptr(), ab.stride(0), None, 0, None,
+                               0, rows.shape[0], nk, nv, conv.data_ptr(), pos.data_ptr(), cw.data_ptr(), A.data_ptr(),
+                               dtb.data_ptr(), nw.data_ptr(), 1e-6, state.data_ptr(),
+                               scratch.data_ptr() if need else None, need, out.data_ptr(), 0, _lib.stream_ptr(dev)))
+
+    row_of = {}
+
+    def ab_rows(rows):
+        return ab[row_of[rows.data_ptr()]:]
+
+    s_all, c_all = state0.clone(), conv0.clone()
+    out_all = torch.empty(T, nv * 128, device=dev)
+    row_of[proj.data_ptr()] = 0
+    call(proj, s_all, c_all, torch.zeros(1, dtype=torch.int32, device=dev), out_all)
+    s_one, c_one = state0.clone(), conv0.clone()
+    out_one = torch.empty(T, nv * 128, device=dev)
+    pos = torch.zeros(1, dtype=torch.int32, device=dev)
+    for t in range(T):
+        row = proj[t:t + 1]
+        row_of[row.data_ptr()] = t
+        pos.fill_(t)
+        call(row, s_one, c_one, pos, out_one[t:t + 1])
+    torch.cuda.synchronize()
+    assert lib.gsq_device_status(None) == 0
+    assert rel(out_all, out_one) <= 1e-4, rel(out_all, out_one)
+    assert rel(s_all, s_one) <= 1e-4, rel(s_all, s_one)
+    assert torch.equal(c_all, c_one)
