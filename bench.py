@@ -578,7 +578,12 @@ def main():
 
     if qmm is not None and world == 1:
         qmm["by_M"] = qmm_by_m(dev, pk)
-    model = model_bench(dev, pk, world) if not args.no_model else None
+    model = None
+    if not args.no_model:
+        try:
+            model = model_bench(dev, pk, world)
+        except Exception as e:  # recorded in the line; the QMV and QMM results above still stand
+            model = {"error": f"{type(e).__name__}: {e}"[:300]}
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
