@@ -469,20 +469,64 @@ def main():
             del g, ring
             torch.cuda.empty_cache()
 
-    # ---- e2e through the public API with host buffers ----
-    host_x = [c["x"].cpu().pin_memory() for c in cfgs]
-    host_y = [torch.empty(c["rows"] * world, dtype=torch.float32).pin_memory() for c in cfgs]
-    h2d = sum(h.numel() * h.element_size() for h in host_x)
-    d2h = sum(h.numel() * h.element_size() for h in host_y)
+    # ---- e2e through the C ABI with host buffers ----
+    if world == 1:
+        # As a C-ABI host drives it: the step's activations sit in one pinned
+        # host buffer and go to the device in one copy; one gsq_qmv call per
+        # projection (device pointers prepared once); the outputs come back
+        # to one pinned host buffer in one copy; one synchronisation per step.
+        from gsq_b200.quant.layouts import type_id
+        lib = _lib.load()
+        xoff, yoff = [], []
+        nx = ny = 0
+        for c in cfgs:
+            xoff.append(nx)
+            yoff.append(ny)
+            nx += -(-c["k"] // 8) * 8  # keep every activation row 16-byte aligned
+            ny += c["rows"]
+        host_xb = torch.zeros(nx, dtype=torch.float16).pin_memory()
+        for c, o in zip(cfgs, xoff):
+            host_xb[o:o + c["k"]] = c["x"].reshape(-1).cpu()
+        host_yb = torch.empty(ny, dtype=torch.float32).pin_memory()
+        dev_xb = torch.empty(nx, dtype=torch.float16, device=dev)
+        dev_yb = torch.empty(ny, dtype=torch.float32, device=dev)
+        need = max(lib.gsq_qmv_workspace_size(type_id(c["q"]), c["rows"], c["k"], 1) for c in cfgs)
+        ws = _lib.workspaces.get(dev, need, "qmv")
+        wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+        stream = _lib.stream_ptr(dev)
+        calls = [(type_id(c["q"]), dev_xb.data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16], c["packed"].data_ptr(),
+                  c["rows"], c["k"], 1, dev_yb.data_ptr() + 4 * yo, _lib.DTYPE_CODES[torch.float32], wsp, wsn, stream)
+                 for c, xo, yo in zip(cfgs, xoff, yoff)]
+        h2d, d2h = nx * 2, ny * 4
+        qmv = lib.gsq_qmv
 
-    def e2e_step():
-        # Every projection: pinned x -> device, one public-API call, y ->
-        # pinned host memory; the step ends when all its results are on the
-        # host (one stream synchronisation per step).
-        for c, hx, hy in zip(cfgs, host_x, host_y):
-            y = matvec(c, hx.to(dev, non_blocking=True))
-            hy.copy_(y.reshape(-1), non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
+        def e2e_step():
+            dev_xb.copy_(host_xb, non_blocking=True)
+            for args_ in calls:
+                rc = qmv(*args_)
+                if rc:
+                    _lib.check(rc)
+            host_yb.copy_(dev_yb, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        e2e_path = ("activations of the step in one pinned host buffer -> one copy to the device -> one gsq_qmv "
+                    "C-ABI call per projection (ctypes, device pointers prepared once) -> outputs in one copy to "
+                    "pinned host memory; one stream synchronisation per step")
+    else:
+        host_x = [c["x"].cpu().pin_memory() for c in cfgs]
+        host_y = [torch.empty(c["rows"] * world, dtype=torch.float32).pin_memory() for c in cfgs]
+        h2d = sum(h.numel() * h.element_size() for h in host_x)
+        d2h = sum(h.numel() * h.element_size() for h in host_y)
+
+        def e2e_step():
+            # Every projection: pinned x -> device, one public-API call, y ->
+            # pinned host memory; the step ends when all its results are on the
+            # host (one stream synchronisation per step).
+            for c, hx, hy in zip(cfgs, host_x, host_y):
+                y = matvec(c, hx.to(dev, non_blocking=True))
+                hy.copy_(y.reshape(-1), non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        e2e_path = ("pinned host x -> quantized_matvec_gather (one ctypes C-ABI call per projection) -> y copied to "
+                    "pinned host memory; one stream synchronisation per step")
 
     for _ in range(2):
         e2e_step()
@@ -498,14 +542,17 @@ def main():
     t1.record()
     torch.cuda.synchronize()
     e2e_ms = t0.elapsed_time(t1)
+    if world == 1:  # the host copy of the outputs is the library's result
+        ref = matvec(cfgs[0], cfgs[0]["x"]).reshape(-1).cpu()
+        if not torch.allclose(host_yb[:ref.numel()], ref, rtol=1e-6, atol=0):
+            raise RuntimeError("end-to-end outputs differ from the library call")
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e = {"value": round(step_bytes * e2e_steps / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-           "path": "pinned host x -> quantized_matvec (one ctypes C-ABI call per projection) -> y copied to "
-                   "pinned host memory; one stream synchronisation per step"}
+           "path": e2e_path}
 
     # ---- QMM prefill, config 3 at M=512 (ranks > 1: each rank's row shard,
     # with the gather fused into the matmul's epilogue) ----
