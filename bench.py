@@ -512,21 +512,47 @@ def main():
                     "C-ABI call per projection (ctypes, device pointers prepared once) -> outputs in one copy to "
                     "pinned host memory; one stream synchronisation per step")
     else:
-        host_x = [c["x"].cpu().pin_memory() for c in cfgs]
-        host_y = [torch.empty(c["rows"] * world, dtype=torch.float32).pin_memory() for c in cfgs]
-        h2d = sum(h.numel() * h.element_size() for h in host_x)
-        d2h = sum(h.numel() * h.element_size() for h in host_y)
+        # The same with the gather fused in: one gsq_qmv_gather call per
+        # projection (this rank's rows; every rank's rows land in the
+        # projection's gather region), then each region's gathered row is
+        # copied to the one pinned host buffer.
+        from gsq_b200.quant.layouts import type_id
+        lib = _lib.load()
+        xoff, yoff = [], []
+        nx = ny = 0
+        for c in cfgs:
+            xoff.append(nx)
+            yoff.append(ny)
+            nx += -(-c["k"] // 8) * 8
+            ny += c["n"]
+        host_xb = torch.zeros(nx, dtype=torch.float16).pin_memory()
+        for c, o in zip(cfgs, xoff):
+            host_xb[o:o + c["k"]] = c["x"].reshape(-1).cpu()
+        host_yb = torch.empty(ny, dtype=torch.float32).pin_memory()
+        dev_xb = torch.empty(nx, dtype=torch.float16, device=dev)
+        need = max(lib.gsq_qmv_workspace_size(type_id(c["q"]), c["rows"], c["k"], 1) for c in cfgs)
+        ws = _lib.workspaces.get(dev, need, "qmv")
+        wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+        stream = _lib.stream_ptr(dev)
+        calls = [(type_id(c["q"]), dev_xb.data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16], c["packed"].data_ptr(),
+                  c["rows"], c["k"], 1, c["region"].regions, world, rank, rank * c["rows"], c["n"], wsp, wsn, stream)
+                 for c, xo in zip(cfgs, xoff)]
+        outs = [(host_yb[yo:yo + c["n"]], c["region"].y.reshape(-1)) for c, yo in zip(cfgs, yoff)]
+        h2d, d2h = nx * 2, ny * 4
+        qmvg = lib.gsq_qmv_gather
 
         def e2e_step():
-            # Every projection: pinned x -> device, one public-API call, y ->
-            # pinned host memory; the step ends when all its results are on the
-            # host (one stream synchronisation per step).
-            for c, hx, hy in zip(cfgs, host_x, host_y):
-                y = matvec(c, hx.to(dev, non_blocking=True))
-                hy.copy_(y.reshape(-1), non_blocking=True)
+            dev_xb.copy_(host_xb, non_blocking=True)
+            for args_ in calls:
+                rc = qmvg(*args_)
+                if rc:
+                    _lib.check(rc)
+            for hy, y in outs:
+                hy.copy_(y, non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
-        e2e_path = ("pinned host x -> quantized_matvec_gather (one ctypes C-ABI call per projection) -> y copied to "
-                    "pinned host memory; one stream synchronisation per step")
+        e2e_path = ("activations of the step in one pinned host buffer -> one copy to the device -> one "
+                    "gsq_qmv_gather C-ABI call per projection (this rank's rows, every rank's rows gathered) -> "
+                    "each gathered output copied to one pinned host buffer; one stream synchronisation per step")
 
     for _ in range(2):
         e2e_step()
@@ -542,10 +568,10 @@ def main():
     t1.record()
     torch.cuda.synchronize()
     e2e_ms = t0.elapsed_time(t1)
-    if world == 1:  # the host copy of the outputs is the library's result
-        ref = matvec(cfgs[0], cfgs[0]["x"]).reshape(-1).cpu()
-        if not torch.allclose(host_yb[:ref.numel()], ref, rtol=1e-6, atol=0):
-            raise RuntimeError("end-to-end outputs differ from the library call")
+    # the host copy of the outputs is the library's result
+    ref = matvec(cfgs[0], cfgs[0]["x"]).reshape(-1).cpu()
+    if not torch.allclose(host_yb[:ref.numel()], ref, rtol=1e-6, atol=0):
+        raise RuntimeError("end-to-end outputs differ from the library call")
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
