@@ -6,13 +6,15 @@ own converter (mlx_gsq/gguf/parser.py and converter.py, loaded by file path
 under a stand-in package name so that mlx_gsq/__init__.py, which imports MLX,
 is not executed), and records the analysis (without the machine-specific
 path) and the SHA-256 of the container and manifest tensor hashes in
-gguf_golden.json.  Run in a container that has the reference checkout:
+gguf_golden.json.  Run where the reference checkout exists (the argument, else GSQ_REFERENCE,
+else a ``reference`` directory next to this repository):
 
-    python tests/golden/make_gguf_golden.py /path/to/reference
+    python tests/golden/make_gguf_golden.py [/path/to/reference]
 """
 import hashlib
 import importlib.util
 import json
+import os
 import sys
 import tempfile
 import types
@@ -71,4 +73,5 @@ def main(ref: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    default = os.environ.get("GSQ_REFERENCE") or str(HERE.parent.parent.parent / "reference")
+    main(sys.argv[1] if len(sys.argv) > 1 else default)

@@ -1,7 +1,7 @@
 """Generate tests/golden/golden.npz from the reference's own decoder.
 
-Runs only where the reference checkout exists (``GSQ_REFERENCE`` or
-``/root/reference``).  It loads ``mlx_gsq/quant/reference.py`` by file path (a
+Runs only where the reference checkout exists (``GSQ_REFERENCE``, else a
+``reference`` directory next to this repository).  It loads ``mlx_gsq/quant/reference.py`` by file path (a
 plain ``import mlx_gsq`` needs MLX, ``mlx_gsq/__init__.py:5``) and calls its
 ``dequantize_reference`` -- the decoder the reference's tests treat as ground
 truth (``tests/test_metal_decoders.py:21``) -- on seeded synthetic blocks.
@@ -44,7 +44,8 @@ def load_reference_decoder(root: str):
 
 
 def main(out: str = os.path.join(HERE, "golden.npz")) -> None:
-    root = os.environ.get("GSQ_REFERENCE", "/root/reference")
+    root = os.environ.get("GSQ_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))),
+                                                           "reference")
     dequantize_reference = load_reference_decoder(root)
     arrays = {}
     rng = np.random.default_rng(123)

@@ -10,7 +10,9 @@ from gsq_b200.quant.layouts import (LAYOUTS, QUANT_BLOCK_SIZES, SUPPORTED_QUANT_
                                     packed_bytes)
 from gsq_b200.quant.synthetic import SCALE_HI, SCALE_LO, random_blocks, random_matrix
 
-REF = os.environ.get("GSQ_REFERENCE", "/root/reference")
+# The reference checkout: GSQ_REFERENCE, else a "reference" directory next to this repository.
+REF = os.environ.get("GSQ_REFERENCE") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))), "reference")
 
 
 def test_block_sizes_match_gguf():
@@ -64,7 +66,7 @@ def test_synthetic_scales_in_range():
 
 
 def test_packed_bytes_config_sizes():
-    # SURVEY/BASELINE sizes: Q4_K 5120^2 = 14,745,600 B; Q6_K 17408x5120 = 73,113,600 B.
+    # Benchmark configuration sizes: Q4_K 5120^2 = 14,745,600 B; Q6_K 17408x5120 = 73,113,600 B.
     assert packed_bytes("Q4_K", 5120, 5120) == 14_745_600
     assert packed_bytes("IQ1_S", 5120, 5120) == 5_120_000
     assert packed_bytes("Q6_K", 5120, 17408) == 73_113_600
