@@ -668,7 +668,7 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s (packed weight bytes, QMV batch 1)",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8",
             "dtype_note": "decoded packed entries (s8/u8) x two int8 activation levels on the tensor cores, "
                           "s32 accumulate, fp32 scales and output; fp16 activations in",
