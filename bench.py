@@ -248,9 +248,8 @@ def model_bench(dev, pk, world=1, prompt=182, decode_tokens=64, prefill_m=512):
     head -> argmax); and a ``prefill_m``-token prefill.  CUDA events around
     each timed region; every decode token reads all packed projections
     (12 GB, ~90x L2).  With ``world`` > 1 (config 5) every packed projection
-    is split by output rows over the ranks (the decode gathers fused into the
-    matvec, the prefill ones NCCL all-gathers); times are the max over
-    ranks."""
+    is split by output rows over the ranks (the gathers fused into the matvec
+    and the matmul epilogue); times are the max over ranks."""
     import torch
     import torch.distributed as dist
     from gsq_b200.models import Qwen35Config, build_qwen35, random_weights
@@ -308,8 +307,8 @@ def model_bench(dev, pk, world=1, prompt=182, decode_tokens=64, prefill_m=512):
                                + (f" x {world} GPUs" if world > 1 else "")})
     if world > 1:
         out["decode_roofline_frac"] = round(gbs / (pk["hbm"] * world), 4)
-        out["parallelism"] = (f"tp{world}: every packed projection split by output rows; decode gathers fused "
-                              "into the matvec over NVLink, prefill gathers by NCCL all-gather")
+        out["parallelism"] = (f"tp{world}: every packed projection split by output rows; the row gathers fused "
+                              "into the matvec (decode) and the matmul epilogue (prefill) over NVLink")
     model.close()
     del model
     torch.cuda.empty_cache()

@@ -202,6 +202,7 @@ class _Packed:
             self.data = parts[0].data if len(parts) == 1 else torch.cat([p.data.reshape(-1) for p in parts])
         self.nbytes = self.data.numel()  # the whole projection's payload (all ranks together)
         self.world, self.rank, self.group, self.region = 1, 0, None, None
+        self.prefill_region = None  # shared by the projections of the same width (tensor parallel)
         self.n_local, self.row0 = self.n, 0
 
     def shard(self, group) -> None:
@@ -232,6 +233,11 @@ class _Packed:
             from ..parallel import quantized_matvec_gather
             return quantized_matvec_gather(x16, self.data, qtype=self.qtype, out_features=self.n_local,
                                            in_features=self.k, region=self.region, row0=self.row0)
+        reg = self.prefill_region
+        if reg is not None and 8 <= x16.shape[0] <= reg.rows:  # prompt: the gather fused into the matmul epilogue
+            from ..parallel import quantized_matmul_gather
+            return quantized_matmul_gather(x16, self.data, qtype=self.qtype, out_features=self.n_local,
+                                           in_features=self.k, region=reg, row0=self.row0)
         from ..parallel import gather_rows
         y = quantized_matvec(x16, self.data, qtype=self.qtype, out_features=self.n_local, in_features=self.k,
                              out_dtype=torch.float32)
@@ -288,7 +294,8 @@ class Qwen35:
     With ``group`` (an initialised process group of P ranks, one GPU each;
     BASELINE config 5) every packed projection is split by output rows over
     the ranks: decode tokens gather the rows inside the matvec kernel
-    (``gsq_qmv_gather``), prompts with an NCCL all-gather after the matmul.
+    (``gsq_qmv_gather``), prompts inside the matmul epilogue
+    (``gsq_qmm_gather``; prompts of 2-7 tokens, an NCCL all-gather).
     Norms, the gated-DeltaNet and attention blocks run on every rank on the
     gathered (identical) vectors."""
 
@@ -329,9 +336,24 @@ class Qwen35:
                 L["v_cache"] = torch.zeros(max_len, nkv, hd, device=self.dev)
             self.layers.append(L)
         self.world = dist.get_world_size(group) if group is not None else 1
+        self._prefill_regions = {}
         if self.world > 1:
             for pk in self._projections():
                 pk.shard(group)
+            # Prompts gather inside the matmul epilogue into one region per
+            # output width, shared by every projection of that width (the LM
+            # head only ever sees one row).  Sharing is safe because two calls
+            # of the same width always have another gathered call between
+            # them: no rank finishes that call before every rank's matmul has
+            # started storing, which each does only after the kernel that
+            # consumed the previous output of the width has completed.
+            from ..parallel import GatherRegion
+            widths = sorted({pk.n for pk in self._projections() if pk is not self.lm_head})
+            for n in widths:
+                self._prefill_regions[n] = GatherRegion(max_len, n, group=group, device=self.dev)
+            for pk in self._projections():
+                if pk is not self.lm_head:
+                    pk.prefill_region = self._prefill_regions[pk.n]
         self.pos = torch.zeros(1, dtype=torch.int32, device=self.dev)   # next position (decode)
         self.cur_id = torch.zeros(1, dtype=torch.int32, device=self.dev)  # token to feed next (decode)
         self.n_pos = 0  # host copy of the position (prefill bookkeeping)
@@ -351,6 +373,10 @@ class Qwen35:
         self._graph = None
         for pk in self._projections():
             pk.close()
+            pk.prefill_region = None
+        for reg in self._prefill_regions.values():
+            reg.close()
+        self._prefill_regions = {}
 
     # ---- sizes ----
     def packed_bytes_per_token(self) -> int:

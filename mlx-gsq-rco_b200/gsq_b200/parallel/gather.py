@@ -123,12 +123,13 @@ def quantized_matmul_gather(x: torch.Tensor, packed_shard: torch.Tensor, *, qtyp
     """The tiled matmul (prefill) of this rank's rows [row0, row0 + out_features)
     of a row-split projection with the gather fused into its epilogue
     (``gsq_qmm_gather``): every output tile goes into every rank's region over
-    NVLink as it is written.  Returns the region's ``rows x ntot`` fp32
-    output, complete once the call finishes on the current stream."""
+    NVLink as it is written.  Returns the first ``rows`` rows of the region's
+    fp32 output (a region of R rows serves calls of up to R rows), complete
+    once the call finishes on the current stream."""
     tid = _type_id(qtype)
     dev = _lib.require_cuda(x, packed_shard)
     rows = x.numel() // in_features
-    if rows != region.rows:
+    if rows > region.rows:
         raise ValueError(f"x has {rows} rows, the region {region.rows}")
     flat = x.reshape(rows, in_features).contiguous()
     if flat.data_ptr() % 16:
@@ -143,4 +144,4 @@ def quantized_matmul_gather(x: torch.Tensor, packed_shard: torch.Tensor, *, qtyp
                               ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
                               _lib.stream_ptr(dev))
     _lib.check(code)
-    return region.y
+    return region.y[:rows]
