@@ -175,3 +175,27 @@ def test_cli(tmp_path, capsys):
     main(["convert", str(src), str(tmp_path / "m.safetensors")])
     main(["verify", str(src), str(tmp_path / "m.safetensors")])
     assert "verification passed" in capsys.readouterr().out
+
+
+def test_model_checkpoint_round_trip(tmp_path):
+    """Every tensor of the model (a reduced configuration, random-init on the
+    host) written as a GGUF checkpoint and read back through the reader and
+    through the converted container: the same names, types, shapes and bytes
+    (plain tensors as fp32)."""
+    from gsq_b200.gguf import write_model_gguf
+    from gsq_b200.models import Qwen35Config, random_weights, tensor_shapes
+    cfg = Qwen35Config(hidden_size=512, intermediate_size=768, num_hidden_layers=4, num_attention_heads=4,
+                       num_key_value_heads=2, vocab_size=512, linear_num_value_heads=4, linear_num_key_heads=2)
+    w = random_weights(cfg, "cpu", seed=1)
+    assert set(w) == set(tensor_shapes(cfg))
+    src = write_model_gguf(tmp_path / "m.gguf", w, {"general.architecture": "qwen35"})
+    dst = convert_gguf_to_safetensors(src, tmp_path / "m.safetensors")
+    for loaded in (GGUFReader(src).model_weights(device=None), PackedModelStore(dst, device=None).model_weights()):
+        assert set(loaded) == set(w)
+        for name, t in w.items():
+            got = loaded[name]
+            if hasattr(t, "quantization_type"):
+                assert got.quantization_type == t.quantization_type and got.logical_shape == t.logical_shape
+                assert torch.equal(got.data.reshape(-1), t.data.reshape(-1))
+            else:
+                assert got.dtype == torch.float32 and torch.equal(got, t.float()), name
