@@ -141,34 +141,33 @@ def default_type_mix(cfg: Qwen35Config) -> dict[str, str]:
 
 
 def random_weights(cfg: Qwen35Config, device, seed: int = 0, type_mix: dict[str, str] | None = None) -> dict:
-    """Random-init weights of the model by GGUF name: packed tensors as
-    ``PackedWeight`` (the synthetic generator of the benchmarks: uniform
-    bytes, fp16 super-block scales in [1e-4, 4e-3]), plain tensors as fp32
-    CUDA tensors (norm weights near 1, conv taps, gates)."""
+    """Random-init weights of the model by GGUF name, on ``device``: packed
+    tensors as ``PackedWeight`` (the synthetic generator of the benchmarks:
+    uniform bytes, fp16 super-block scales in [1e-4, 4e-3]), plain tensors as
+    fp32 (norm weights near 1, conv taps, gates)."""
     from ..quant.synthetic import random_matrix_torch
     cfg.check()
     mix = type_mix or default_type_mix(cfg)
     gen = torch.Generator(device=device).manual_seed(seed)
+
+    def rnd(shape, scale, offset=0.0):
+        return torch.randn(shape, device=device, generator=gen) * scale + offset
+
     out = {}
     for idx, (name, shape) in enumerate(tensor_shapes(cfg).items()):
         if name in mix:
             data = random_matrix_torch(mix[name], shape[0], shape[1], seed=seed * 100003 + idx, device=device)
             out[name] = PackedWeight.from_packed(name, data, mix[name], shape, device=None)
-            continue
-
-        def rnd(scale, offset=0.0):
-            return torch.randn(shape, device=device, generator=gen) * scale + offset
-
-        if name.endswith("norm.weight"):
-            out[name] = rnd(0.05, 1.0)
+        elif name.endswith("norm.weight"):
+            out[name] = rnd(shape, 0.05, 1.0)
         elif name.endswith("ssm_conv1d.weight"):
-            out[name] = rnd(0.3)
+            out[name] = rnd(shape, 0.3)
         elif name.endswith("ssm_alpha.weight") or name.endswith("ssm_beta.weight"):
-            out[name] = rnd(1.0 / math.sqrt(shape[1]))
+            out[name] = rnd(shape, 1.0 / math.sqrt(shape[1]))
         elif name.endswith("ssm_a"):
             out[name] = -torch.exp(torch.rand(shape, device=device, generator=gen) * 2.0)
         elif name.endswith("ssm_dt.bias"):
-            out[name] = rnd(0.5)
+            out[name] = rnd(shape, 0.5)
         else:
             raise KeyError(name)
     return out
