@@ -78,3 +78,42 @@ def test_workspace_sizes_are_plain_host_math():
         # a fixed 64 KiB ticket region, then (bf16 input) an fp16 copy of x
         assert lib.gsq_qmm_workspace_size(t, 17408, 5120, 512, 2) == 65536 + 512 * 5120 * 2
         assert lib.gsq_qmm_workspace_size(t, 17408, 5120, 512, 1) == 0
+
+
+def test_gather_entry_points_validate_before_any_launch():
+    """The row-parallel entry points reject bad ranks, regions, row counts and
+    ranges with status codes before touching the GPU."""
+    lib = _lib.load()
+    fake = ctypes.c_void_p(1 << 20)  # never dereferenced: every call below fails validation first
+    q4k = type_id("Q4_K")
+    two = (ctypes.c_void_p * 2)(1 << 20, 1 << 21)
+    odd = (ctypes.c_void_p * 2)(1 << 20, (1 << 21) + 16)  # second region not 256-byte aligned
+
+    def qmv_gather(regions, world, rank, rows=1, row0=0, n=256, ntot=512, xdt=1):
+        return lib.gsq_qmv_gather(q4k, fake, xdt, fake, n, 256, rows, regions, world, rank, row0, ntot, None, 0, None)
+
+    assert qmv_gather(two, 1, 0) == _lib.GSQ_ERR_ARG      # one rank gathers nothing
+    assert qmv_gather(two, 9, 0) == _lib.GSQ_ERR_ARG      # more than 8 ranks
+    assert qmv_gather(two, 2, 2) == _lib.GSQ_ERR_ARG      # rank outside the group
+    assert qmv_gather(None, 2, 0) == _lib.GSQ_ERR_ARG
+    assert qmv_gather(odd, 2, 0) == _lib.GSQ_ERR_ALIGN
+    assert qmv_gather(two, 2, 0, rows=8) == _lib.GSQ_ERR_SIZE   # 8 rows and more: the matmul
+    assert qmv_gather(two, 2, 1, row0=384) == _lib.GSQ_ERR_SIZE  # rows [384, 640) outside 512
+    assert qmv_gather(two, 2, 0, xdt=7) == _lib.GSQ_ERR_ARG
+
+    def qmm_gather(regions, world, rank, m=64, row0=0, ntot=512):
+        return lib.gsq_qmm_gather(q4k, fake, 1, fake, 256, 256, m, regions, world, rank, row0, ntot, None, 0, None)
+
+    assert qmm_gather(two, 9, 0) == _lib.GSQ_ERR_ARG
+    assert qmm_gather(odd, 2, 0) == _lib.GSQ_ERR_ALIGN
+    assert qmm_gather(two, 2, 0, m=0) == _lib.GSQ_ERR_SIZE
+    assert qmm_gather(two, 2, 0, ntot=128) == _lib.GSQ_ERR_SIZE
+
+    assert lib.gsq_gather_region_bytes(0, 512) == 0
+    assert lib.gsq_gather_region_bytes(1, 5120) > 256 + 4 * 5120  # header, y, and the one-row inbox
+    p = ctypes.c_void_p()
+    assert lib.gsq_gather_region_alloc(100, ctypes.byref(p)) == _lib.GSQ_ERR_ARG  # below the header size
+    assert lib.gsq_gather_region_free(None) == _lib.GSQ_OK
+    assert lib.gsq_ipc_export(None, ctypes.create_string_buffer(64)) == _lib.GSQ_ERR_ARG
+    assert lib.gsq_ipc_import(None, ctypes.byref(p)) == _lib.GSQ_ERR_ARG
+    assert lib.gsq_ipc_close(None) == _lib.GSQ_OK
