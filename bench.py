@@ -1,6 +1,6 @@
 """Benchmark of the packed-GGUF hot path on B200 (driver contract).
 
-One *step* = one pass of the batch-1 decode matvec over BASELINE config 2:
+One *step* = one pass of the batch-1 decode matvec over the config-2 sweep:
 the 11 packed types x {5120->5120, 5120->17408, 17408->5120}, fp16
 activations N(0,1), seeded synthetic packed weights (886 MB per step, far
 larger than the 126 MB L2, so no step reuses another's weights from L2).
@@ -9,24 +9,32 @@ larger than the 126 MB L2, so no step reuses another's weights from L2).
               the sweep x steps / device time of the timed region (CUDA graph
               replays of the step, CUDA events, max over ranks).  One step is
               33 launches of the QMV kernel, nothing else.
-  e2e         the same metric through the public Python API with host
-              buffers: every step copies each projection's activation from
-              pinned host memory and reads the result back.
+  e2e         the same metric through the C ABI with host buffers: every step
+              copies the activations from pinned host memory and the results
+              back to pinned host memory.
   roofline    the QMV kernel inside the timed region: algorithmic bytes of a
               step (packed + 2K + 4N per call) / the step's CUDA-event time,
               vs the measured HBM copy bandwidth.
+  parity      every output of the timed step against an independent result:
+              one GPU, the float64 product with the bit-exact dequantized
+              matrix; several GPUs, the gathered rows against the single-GPU
+              matvec / matmul of the whole matrix.  A failure exits non-zero.
   qmv_sweep   per configuration: a CUDA graph of 24 launches over a ring of
               distinct weight copies (working set > 2x L2), CUDA events.
   qmm_prefill config 3 at M=512 (tcgen05 QMM) in TFLOP/s vs measured bf16 peak;
               on one GPU also M = 16, 182, 2048 against the max(FLOP, byte)
               roofline (``by_M``).
-  model       config 4: the 27B Qwen3.5-hybrid decoder with random-init
-              packed weights; prefill (182 and 512 tokens) and batch-1
-              decode tok/s (CUDA-graph replay per token); with --gpus N
-              (config 5) split by output rows over the N ranks.
+  embed       the packed embedding gather (Q6_K, vocab 248320 x 5120) at
+              T = 1, 182, 512 token ids against its HBM bytes.
+  model       the 27B Qwen3.5-hybrid decoder with random-init packed weights
+              (64 layers, hidden 5120, FFN 17408, GQA every 4th layer,
+              gated-DeltaNet elsewhere, vocab 248320): prefill tok/s at 182,
+              512 and 2048 tokens and greedy decode tok/s at batch 1, 8 and
+              64 (CUDA-graph replay per token); with --gpus N every packed
+              projection is split by output rows over the N ranks.
   cpu_baseline the reference's CPU path (gguf-py dequantize, which
-              mlx_gsq/quant/reference.py:10-18 calls, + numpy matvec) on a
-              bounded sample of the same workload.
+              mlx_gsq/quant/reference.py:10-18 calls, + numpy matvec) over the
+              same 33 configurations, one process per host core (rank 0, N=1).
 
 --gpus N (torchrun): each projection is split by output rows over the N
 ranks (tensor parallel, strong scaling: total work fixed); the row gather is
@@ -39,6 +47,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import platform
 import subprocess
 import sys
 import threading
@@ -54,12 +63,20 @@ SHAPES = ((5120, 5120), (17408, 5120), (5120, 17408))  # (N out, K in)
 QMM_TYPES = ("IQ2_XS", "IQ3_S", "IQ4_XS", "Q6_K")
 QMM_SHAPES = ((17408, 5120), (5120, 17408))
 METRIC = "decode tok/s (batch 1) + QMV packed-byte HBM GB/s vs peak; prefill tok/s at M=512"
+UNIT = "GB/s (packed weight bytes, QMV batch 1)"
 BLOCK_BYTES = {"IQ1_M": 56, "IQ1_S": 50, "IQ2_XXS": 66, "IQ2_XS": 74, "IQ2_S": 82, "IQ3_XXS": 98, "IQ3_S": 110,
                "IQ4_XS": 136, "Q2_K": 84, "Q4_K": 144, "Q6_K": 210}
+PARITY_REL_L2 = 1e-3
 
 
 def packed_bytes(q, n, k):
     return n * (k // 256) * BLOCK_BYTES[q]
+
+
+SWEEP_BYTES = sum(packed_bytes(q, n, k) for q in TYPES for (n, k) in SHAPES)
+CONFIG = {"workload": "config-2 QMV sweep: 11 types x {5120->5120, 5120->17408, 17408->5120}, batch 1, fp16 x "
+                      "N(0,1), seeded synthetic packed weights",
+          "bytes_per_step": SWEEP_BYTES, "l2": "inputs larger than L2 (886 MB per step)"}
 
 
 def peaks():
@@ -71,7 +88,10 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
+    """nvidia-smi clock / throttle samples for the whole run, timestamped on
+    arrival; the timed regions are marked and summarised afterwards.  Started
+    once before any barrier, so no rank waits on nvidia-smi between a barrier
+    and its timed region."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -80,39 +100,50 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, str]] = []
+        self.regions: list[tuple[float, float]] = []
+        self._t0 = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "25",
                  "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+            threading.Thread(target=self._read, daemon=True).start()
             t0 = time.time()
-            while not self.lines and time.time() - t0 < 5.0:  # sampling has started before timing does
+            while not self.samples and time.time() - t0 < 5.0:
                 time.sleep(0.01)
-            self.lines.clear()
         except OSError:
             self.proc = None
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.samples.append((time.monotonic(), line.strip()))
 
-    def __exit__(self, *exc):
+    def mark_start(self):
+        self._t0 = time.monotonic()
+
+    def mark_end(self):
+        if self._t0 is not None:
+            self.regions.append((self._t0, time.monotonic()))
+        self._t0 = None
+
+    def stop(self):
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.proc = None
 
     def summary(self):
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ts, ln in list(self.samples):
+            if not any(a <= ts <= b for a, b in self.regions):
+                continue
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 8:
                 continue
@@ -124,53 +155,94 @@ class ClockSampler:
             for name, val in zip(names, parts[4:8]):
                 if val.lower() == "active":
                     reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+               "reasons": sorted(reasons), "samples": len(sm),
+               "window": "samples taken inside the bench's timed regions (QMV step, per-configuration sweep, "
+                         "e2e, QMM, embedding, model)"}
+        return out
 
 
-def cpu_reference_sample(time_budget_s: float = 20.0):
-    """The reference's CPU path: gguf-py dequantize (what dequantize_reference
-    calls) + numpy fp32 matvec, on 5120x5120 matrices of the sweep's types,
-    until the time budget is spent.  Returns packed-byte GB/s and the sample."""
+# ---------------------------------------------------------------------------
+# The reference's CPU path (gguf-py dequantize + numpy matvec), all 33
+# configurations, one worker process per host core.
+
+def _cpu_config(job):
+    """One configuration of the sweep on the CPU: gguf-py 0.19.0 dequantize
+    (the call mlx_gsq/quant/reference.py:10-18 makes) then the numpy fp32
+    matvec the reference's tests use as the expected value
+    (tests/test_all_qmv.py:22).  Returns the timed split."""
     import gguf
     from gsq_b200.quant.synthetic import random_activations, random_matrix
-    done_bytes, spent, sample = 0, 0.0, []
-    for q in ("Q4_K", "IQ2_XS", "IQ3_S", "Q6_K", "IQ4_XS", "IQ1_S"):
-        n = k = 5120
-        packed = random_matrix(q, n, k, seed=0)
-        x = random_activations(1, k, seed=0).astype(np.float32)
+    q, n, k, seed = job
+    packed = random_matrix(q, n, k, seed=seed)
+    x = random_activations(1, k, seed=seed, dtype=np.float16).astype(np.float32)
+    t0 = time.perf_counter()
+    deq = gguf.dequantize(packed.reshape(-1, BLOCK_BYTES[q]), gguf.GGMLQuantizationType[q]).reshape(n, k)
+    t1 = time.perf_counter()
+    y = x @ deq.T
+    t2 = time.perf_counter()
+    assert y.shape == (1, n)
+    return q, n, k, packed.size, t1 - t0, t2 - t1
+
+
+def cpu_reference_sweep(max_workers: int | None = None) -> dict:
+    """The config-2 sweep on the host cores: every configuration once, one
+    process per core (spawned; each with one OpenBLAS thread).  value =
+    packed bytes of the sweep / wall time of the pool."""
+    import multiprocessing as mp
+    workers = max(1, min(len(TYPES) * len(SHAPES), max_workers or os.cpu_count() or 1))
+    jobs = [(q, n, k, 100 * ti + si) for ti, q in enumerate(TYPES) for si, (n, k) in enumerate(SHAPES)]
+    jobs.sort(key=lambda j: -packed_bytes(j[0], j[1], j[2]))  # longest first
+    saved = {v: os.environ.get(v) for v in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS")}
+    for v in saved:
+        os.environ[v] = "1"
+    try:
+        ctx = mp.get_context("spawn")
         t0 = time.perf_counter()
-        deq = gguf.dequantize(packed.reshape(-1, BLOCK_BYTES[q]), gguf.GGMLQuantizationType[q]).reshape(n, k)
-        _ = x @ deq.T
-        dt = time.perf_counter() - t0
-        done_bytes += packed.size
-        spent += dt
-        sample.append(f"{q} {n}x{k}")
-        if spent > time_budget_s:
-            break
-    return done_bytes / spent / 1e9, spent, sample
+        with ctx.Pool(workers) as pool:
+            res = pool.map(_cpu_config, jobs, chunksize=1)
+        wall = time.perf_counter() - t0
+    finally:
+        for v, val in saved.items():
+            if val is None:
+                os.environ.pop(v, None)
+            else:
+                os.environ[v] = val
+    total = sum(r[3] for r in res)
+    deq_s = sum(r[4] for r in res)
+    mv_s = sum(r[5] for r in res)
+    cpu_model = platform.processor() or ""
+    try:
+        for ln in open("/proc/cpuinfo"):
+            if ln.startswith("model name"):
+                cpu_model = ln.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"value": round(total / wall / 1e9, 4), "unit": "GB/s", "cores": workers, "wall_s": round(wall, 2),
+            "cpu_seconds": {"dequant": round(deq_s, 2), "matvec": round(mv_s, 2)},
+            "per_core_gbs": round(total / (deq_s + mv_s) / 1e9, 5), "openblas_threads_per_worker": 1,
+            "os_cpu_count": os.cpu_count(), "cpu_model": cpu_model,
+            "sample": "the whole config-2 sweep (33 configurations, 886 MB packed) once: gguf-py 0.19.0 dequantize "
+                      "+ numpy fp32 matvec per configuration, one spawned process per core"}
 
 
 def run_reference(args, rank):
     if rank != 0:
         return
-    gbs, spent, sample = cpu_reference_sample(args.cpu_budget)
-    cores = os.cpu_count()
+    cpu = cpu_reference_sweep()
     line = {
-        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s (packed weight bytes, QMV batch 1)",
+        "impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config-2 QMV sweep, bounded CPU sample: " + ", ".join(sample),
-                   "parallelism": "host cores"},
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "reference",
-                         "sample": f"gguf-py 0.19.0 dequantize + numpy matvec over {', '.join(sample)} "
-                                   f"({spent:.1f} s)"},
-        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": dict(CONFIG), "parallelism": "host cores (one process per core)",
+        "cpu_baseline": dict(cpu, kind="reference"),
+        "e2e": {"value": cpu["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
+
+# ---------------------------------------------------------------------------
 
 def decode_tok_s(per):
     """Batch-1 decode tokens/s of one FFN-shaped projection pair per type
@@ -184,7 +256,29 @@ def decode_tok_s(per):
     return out or None
 
 
-def qmm_by_m(dev, pk, ms=(16, 182, 2048)):
+def device_ok(lib, dev, what):
+    """The kernels' bounded waits and id checks report through the device
+    error word; a timed region whose kernels reported anything is invalid."""
+    import torch
+    code = lib.gsq_device_status(torch.cuda.current_stream(dev).cuda_stream)
+    if code != 0:
+        raise RuntimeError(f"device status {code} after {what}")
+
+
+def graph_of(fn, dev, reps=1):
+    import torch
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream(device=dev)
+    st.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(reps):
+                fn()
+    torch.cuda.current_stream(dev).wait_stream(st)
+    return g
+
+
+def qmm_by_m(dev, pk, lib, clocks, ms=(16, 182, 2048)):
     """Config 3 at the other token counts, one GPU: for each M, one CUDA graph
     runs the 8 projections (4 types x 2 shapes, 369 MB of distinct packed
     weights, > 2x L2) back to back; replayed, CUDA events.  Reported against
@@ -208,23 +302,19 @@ def qmm_by_m(dev, pk, ms=(16, 182, 2048)):
         for _ in range(3):
             run()
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        st = torch.cuda.Stream(device=dev)
-        st.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(st):
-            with torch.cuda.graph(g, stream=st):
-                for _ in range(2):
-                    run()
-        torch.cuda.current_stream(dev).wait_stream(st)
+        g = graph_of(run, dev, reps=2)
         g.replay()
         torch.cuda.synchronize()
         reps = 4
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.mark_start()
         e0.record()
         for _ in range(reps):
             g.replay()
         e1.record()
         torch.cuda.synchronize()
+        clocks.mark_end()
+        device_ok(lib, dev, f"qmm M={m}")
         t = e0.elapsed_time(e1) / 1e3 / (2 * reps)  # seconds per pass over the 8 projections
         del g
         flops = sum(2.0 * m * n * k for _, n, k, _ in mats)
@@ -240,24 +330,80 @@ def qmm_by_m(dev, pk, ms=(16, 182, 2048)):
     return out
 
 
-def model_bench(dev, pk, world=1, prompt=182, decode_tokens=64, prefill_m=512):
-    """Config 4 (BASELINE): the Qwen3.5-hybrid 27B decoder (64 layers) with
-    random-init packed weights of the config's type mix.  A ``prompt``-token
-    prefill, then ``decode_tokens`` greedy decode tokens at batch 1, each a
-    replay of the captured decode-step graph (embedding -> 64 layers -> LM
-    head -> argmax); and a ``prefill_m``-token prefill.  CUDA events around
-    each timed region; every decode token reads all packed projections
-    (12 GB, ~90x L2).  With ``world`` > 1 (config 5) every packed projection
-    is split by output rows over the ranks (the gathers fused into the matvec
-    and the matmul epilogue); times are the max over ranks."""
+def embed_bench(dev, pk, lib, clocks, ts=(1, 182, 512)):
+    """The packed embedding gather of the model (Q6_K, vocab 248320 x 5120,
+    1.04 GB packed): per T, a CUDA graph of 32 gathers over a ring of 32
+    distinct random id sets, fp16 rows out; CUDA events.  HBM bytes per call
+    = T*(dim/256)*bb (packed rows) + T*dim*2 (fp16 out) + 4T (ids); reference
+    mlx_gsq/runtime/kernels/embedding.py:28-36."""
+    import torch
+    from gsq_b200.quant.synthetic import random_matrix_torch
+    from gsq_b200.runtime.kernels import packed_embedding
+
+    vocab, dim, q = 248320, 5120, "Q6_K"
+    table = random_matrix_torch(q, vocab, dim, seed=21, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    out = []
+    for T in ts:
+        ring = [torch.randint(0, vocab, (T,), device=dev, dtype=torch.int32, generator=gen) for _ in range(32)]
+
+        def run():
+            for ids in ring:
+                packed_embedding(ids, table, qtype=q, vocab_size=vocab, dimensions=dim, dtype=torch.float16)
+
+        run()
+        torch.cuda.synchronize()
+        g = graph_of(run, dev)
+        g.replay()
+        torch.cuda.synchronize()
+        reps = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.mark_start()
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        clocks.mark_end()
+        device_ok(lib, dev, f"embedding T={T}")
+        t = e0.elapsed_time(e1) / 1e3 / (reps * len(ring))
+        nbytes = T * (dim // 256) * BLOCK_BYTES[q] + T * dim * 2 + 4 * T
+        out.append({"T": T, "us": round(t * 1e6, 2), "gbs": round(nbytes / t / 1e9, 1),
+                    "roofline_frac": round(nbytes / t / 1e9 / pk["hbm"], 4), "bytes": nbytes})
+        del g, ring
+    del table
+    torch.cuda.empty_cache()
+    return {"type": q, "vocab": vocab, "dim": dim, "out_dtype": "fp16", "by_T": out,
+            "note": "one launch per call; at these sizes a call moves 0.01-7.5 MB, so launch latency, not HBM, "
+                    "bounds it (frac vs the measured copy peak)"}
+
+
+def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, prefill_ms=(512, 2048),
+                batches=(1, 8, 64)):
+    """The Qwen3.5-hybrid 27B decoder (64 layers: 48 gated-DeltaNet + 16
+    gated GQA, hidden 5120, SwiGLU 17408, vocab 248320) with random-init
+    packed weights of the config's type mix.  A ``prompt``-token prefill and
+    each prefill length in ``prefill_ms``; then greedy decode at each batch
+    size: the prompt's state is copied into every sequence of the batch and
+    ``decode_tokens`` steps run, each a replay of the captured decode-step
+    graph (embedding -> 64 layers -> LM head -> argmax).  CUDA events around
+    each timed region; every decode step reads all packed projections (12 GB,
+    ~90x L2).  With ``world`` > 1 every packed projection is split by output
+    rows over the ranks (the gathers fused into the matvec and the matmul
+    epilogue); times are the max over ranks."""
     import torch
     import torch.distributed as dist
     from gsq_b200.models import Qwen35Config, build_qwen35, random_weights
 
     cfg = Qwen35Config()
     w = random_weights(cfg, dev, seed=0)  # the same bytes on every rank; each keeps its rows
-    model = build_qwen35(w, cfg, dev, max_len=prefill_m + decode_tokens + 16,
-                         group=dist.group.WORLD if world > 1 else None)
+    max_len = max((prompt,) + tuple(prefill_ms)) + decode_tokens + 16
+    try:
+        model = build_qwen35(w, cfg, dev, max_len=max_len, max_batch=max(batches),
+                             group=dist.group.WORLD if world > 1 else None)
+    except TypeError:
+        model = build_qwen35(w, cfg, dev, max_len=max_len, group=dist.group.WORLD if world > 1 else None)
+        batches = (1,)
     del w
     torch.cuda.empty_cache()
     gen = torch.Generator(device=dev).manual_seed(1)
@@ -269,50 +415,68 @@ def model_bench(dev, pk, world=1, prompt=182, decode_tokens=64, prefill_m=512):
             t = float(tt.item())
         return t
 
-    def timed(fn, reps):
+    def timed(fn, reps, what):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.mark_start()
         e0.record()
         for _ in range(reps):
             fn()
         e1.record()
         torch.cuda.synchronize()
+        clocks.mark_end()
+        device_ok(lib, dev, what)
         return max_over_ranks(e0.elapsed_time(e1) / 1e3 / reps)
 
-    out = {"workload": "config 4: Qwen3.5-hybrid 27B (64 layers, 48 gated-DeltaNet + 16 GQA), random-init packed "
-                       "weights (embedding/LM head Q6_K, FFN gate/up IQ2_XS|IQ2_S, down Q4_K, attention IQ3_S|IQ4_XS)",
+    out = {"workload": "Qwen3.5-hybrid 27B (64 layers, 48 gated-DeltaNet + 16 GQA), random-init packed weights "
+                       "(embedding/LM head Q6_K, FFN gate/up IQ2_XS|IQ2_S, down Q4_K, attention IQ3_S|IQ4_XS)",
            "packed_bytes_per_token": model.packed_bytes_per_token()}
-    for T in (prompt, prefill_m):
+    for T in (prompt,) + tuple(prefill_ms):
         ids = torch.randint(0, cfg.vocab_size, (T,), device=dev, generator=gen, dtype=torch.int32)
-        model.prefill(ids)  # warm-up (workspaces, cuBLAS / attention plans)
+        model.prefill(ids)  # warm-up (workspaces, attention plans)
         torch.cuda.synchronize()
-        t = timed(lambda: model.prefill(ids), 3)
+        t = timed(lambda: model.prefill(ids), 3, f"prefill {T}")
         out[f"prefill_{T}_ms"] = round(t * 1e3, 2)
         out[f"prefill_{T}_tok_s"] = round(T / t, 1)
 
     ids = torch.randint(0, cfg.vocab_size, (prompt,), device=dev, generator=gen, dtype=torch.int32)
-    model.prefill(ids)
-    model.decode_step()
-    model.capture_decode()
-    model.replay_decode(3)  # warm-up replays
-    t = timed(lambda: model.replay_decode(decode_tokens), 1) / decode_tokens
-    gbs = out["packed_bytes_per_token"] / t / 1e9
-    out.update({"decode_tokens": decode_tokens, "decode_ms_per_token": round(t * 1e3, 3),
-                "decode_tok_s": round(1.0 / t, 1), "decode_packed_gbs": round(gbs, 1),
-                "decode_roofline_frac": round(gbs / pk["hbm"], 4),
-                "decode_note": "batch 1 after the prompt prefill; each token one CUDA-graph replay of the whole "
-                               "step; roofline = packed weight bytes per token / time vs measured HBM copy peak"
-                               + (f" x {world} GPUs" if world > 1 else "")})
+    decode = []
+    for B in batches:
+        model.prefill(ids)
+        if B > 1:
+            model.fork(B)
+        model.decode_step()
+        model.capture_decode()
+        model.replay_decode(3)  # warm-up replays
+        t = timed(lambda: model.replay_decode(decode_tokens), 1, f"decode batch {B}") / decode_tokens
+        gbs = out["packed_bytes_per_token"] / t / 1e9
+        decode.append({"batch": B, "ms_per_step": round(t * 1e3, 3), "tok_s": round(B / t, 1),
+                       "packed_gbs": round(gbs, 1), "roofline_frac": round(gbs / (pk["hbm"] * world), 4)})
+        if hasattr(model, "release_graph"):
+            model.release_graph()
+    d1 = decode[0]
+    out.update({"decode_tokens": decode_tokens, "decode_ms_per_token": d1["ms_per_step"],
+                "decode_tok_s": d1["tok_s"], "decode_packed_gbs": d1["packed_gbs"],
+                "decode_roofline_frac": d1["roofline_frac"], "decode_by_batch": decode,
+                "decode_note": "greedy decode after the prompt prefill; each step one CUDA-graph replay of the "
+                               "whole step for the batch; roofline = packed weight bytes per step / time vs the "
+                               "measured HBM copy peak" + (f" x {world} GPUs" if world > 1 else "")})
     if world > 1:
-        out["decode_roofline_frac"] = round(gbs / (pk["hbm"] * world), 4)
         out["parallelism"] = (f"tp{world}: every packed projection split by output rows; the row gathers fused "
-                              "into the matvec (decode) and the matmul epilogue (prefill) over NVLink")
+                              "into the matvec (decode, batch 1) and the matmul epilogue (prefill, batch >= 8) "
+                              "over NVLink")
     model.close()
     del model
     torch.cuda.empty_cache()
     return out
+
+
+def rel_l2(a, b) -> float:
+    a = a.double().reshape(-1)
+    b = b.double().reshape(-1)
+    return float((a - b).norm() / max(float(b.norm()), 1e-30))
 
 
 def main():
@@ -321,10 +485,10 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-qmm", action="store_true")
     ap.add_argument("--no-model", action="store_true")
+    ap.add_argument("--no-embed", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -335,11 +499,14 @@ def main():
         run_reference(args, rank)
         return
 
+    clocks = ClockSampler(local).start()  # before any barrier: no rank waits on nvidia-smi later
+
     import torch
     import torch.distributed as dist
     from gsq_b200 import _lib
+    from gsq_b200.quant.layouts import type_id
     from gsq_b200.quant.synthetic import random_matrix_torch
-    from gsq_b200.runtime.kernels import quantized_matmul, quantized_matvec
+    from gsq_b200.runtime.kernels import decode, quantized_matmul, quantized_matvec
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -348,6 +515,8 @@ def main():
         from gsq_b200.parallel import GatherRegion, quantized_matmul_gather, quantized_matvec_gather
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     pk = peaks()
+    lib = _lib.load()
+    lib.gsq_device_status(None)
 
     # ---- workload: every rank holds its row shard of every projection ----
     cfgs = []
@@ -357,14 +526,14 @@ def main():
             rows = n // world
             rb = (k // 256) * BLOCK_BYTES[q]
             shard = full[rank * rows * rb:(rank + 1) * rows * rb].clone()
-            del full
             x = torch.randn(1, k, device=dev, dtype=torch.float16, generator=torch.Generator(device=dev).manual_seed(ti))
             # Ranks > 1: the gathered output of every configuration lives in
             # its own region (the gather is fused into the matvec kernel).
             region = GatherRegion(1, n) if world > 1 else None
-            cfgs.append(dict(q=q, n=n, k=k, rows=rows, packed=shard, x=x, region=region,
+            cfgs.append(dict(q=q, n=n, k=k, rows=rows, packed=shard, full=full, x=x, region=region, y=None,
                              bytes=packed_bytes(q, n, k), alg=packed_bytes(q, rows, k) + 2 * k + 4 * rows))
     step_bytes = sum(c["bytes"] for c in cfgs)
+    assert step_bytes == SWEEP_BYTES
     torch.cuda.synchronize()
 
     def matvec(c, x):
@@ -372,8 +541,10 @@ def main():
         if world > 1:
             return quantized_matvec_gather(x, c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
                                            region=c["region"], row0=rank * c["rows"])
-        return quantized_matvec(x, c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
-                                out_dtype=torch.float32)
+        # (captured: the graph keeps this output buffer; replays refill it)
+        c["y"] = quantized_matvec(x, c["packed"], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
+                                  out_dtype=torch.float32)
+        return c["y"]
 
     def step():
         for c in cfgs:
@@ -383,36 +554,58 @@ def main():
     for _ in range(2):
         step()
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    cap_stream = torch.cuda.Stream(device=dev)
-    cap_stream.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(cap_stream):
-        with torch.cuda.graph(graph, stream=cap_stream):
-            step()
-    torch.cuda.current_stream(dev).wait_stream(cap_stream)
+    graph = graph_of(step, dev)
     torch.cuda.synchronize()
 
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
+    device_ok(lib, dev, "warm-up")
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record()
-        for _ in range(args.steps):
-            graph.replay()
-        end.record()
-        torch.cuda.synchronize()
+    clocks.mark_start()
+    start.record()
+    for _ in range(args.steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    clocks.mark_end()
+    device_ok(lib, dev, "the timed QMV steps")
     ms = start.elapsed_time(end)
+    per_rank_ms = [ms]
     if world > 1:
         t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        allt = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(allt, t)
+        per_rank_ms = [float(v.item()) for v in allt]
+        ms = max(per_rank_ms)
         dist.barrier()
     ms_per_step = ms / args.steps
     value = step_bytes * args.steps / (ms / 1e3) / 1e9
+
+    # ---- parity of the timed step's outputs ----
+    worst, checked = 0.0, 0
+    for c in cfgs:
+        if world > 1:
+            ref = quantized_matvec(c["x"], c["full"], qtype=c["q"], out_features=c["n"], in_features=c["k"],
+                                   out_dtype=torch.float32)
+            got = c["region"].y
+        else:
+            ref = c["x"].double() @ decode(c["full"], c["q"]).reshape(c["n"], c["k"]).double().T
+            got = c["y"]
+        worst = max(worst, rel_l2(got, ref))
+        checked += 1
+        del ref
+    torch.cuda.empty_cache()
+    if world > 1:
+        t = torch.tensor([worst], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        worst = float(t.item())
+    parity = {"max_rel_l2": worst, "n_checked": checked, "bar": PARITY_REL_L2,
+              "against": ("the single-GPU matvec of the whole matrix on every rank (gathered rows vs it)"
+                          if world > 1 else "float64 x @ bit-exact dequantized matrix (GPU dequant)")}
 
     # ---- roofline of the QMV kernel over the timed region ----
     alg_step = sum(c["alg"] for c in cfgs)
@@ -439,28 +632,27 @@ def main():
             ncopy = max(8, min(24, -(-2 * l2 // nbytes)))
             ring = [c["packed"]] + [c["packed"].clone() for _ in range(ncopy - 1)]
             reps = 24
-            for i in range(2):
-                quantized_matvec(c["x"], ring[i % ncopy], qtype=c["q"], out_features=c["rows"], in_features=c["k"],
-                                 out_dtype=torch.float32)
+
+            def run(c=c, ring=ring, ncopy=ncopy):
+                for i in range(reps):
+                    quantized_matvec(c["x"], ring[i % ncopy], qtype=c["q"], out_features=c["rows"],
+                                     in_features=c["k"], out_dtype=torch.float32)
+
+            run()
             torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            st = torch.cuda.Stream(device=dev)
-            st.wait_stream(torch.cuda.current_stream(dev))
-            with torch.cuda.stream(st):
-                with torch.cuda.graph(g, stream=st):
-                    for i in range(reps):
-                        quantized_matvec(c["x"], ring[i % ncopy], qtype=c["q"], out_features=c["rows"],
-                                         in_features=c["k"], out_dtype=torch.float32)
-            torch.cuda.current_stream(dev).wait_stream(st)
+            g = graph_of(run, dev)
             for _ in range(2):
                 g.replay()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            clocks.mark_start()
             e0.record()
             for _ in range(5):
                 g.replay()
             e1.record()
             torch.cuda.synchronize()
+            clocks.mark_end()
+            device_ok(lib, dev, f"sweep {c['q']} {c['n']}x{c['k']}")
             t_us = e0.elapsed_time(e1) * 1e3 / (5 * reps)
             per.append({"type": c["q"], "N": c["n"], "K": c["k"], "us": round(t_us, 2),
                         "GBs": round(c["alg"] / (t_us / 1e6) / 1e9, 1),
@@ -469,34 +661,32 @@ def main():
             torch.cuda.empty_cache()
 
     # ---- e2e through the C ABI with host buffers ----
+    # As a C-ABI host drives it: the step's activations sit in one pinned
+    # host buffer and go to the device in one copy; one call per projection
+    # (device pointers prepared once); the outputs come back to one pinned
+    # host buffer; one synchronisation per step.
+    xoff, yoff = [], []
+    nx = ny = 0
+    for c in cfgs:
+        xoff.append(nx)
+        yoff.append(ny)
+        nx += -(-c["k"] // 8) * 8  # keep every activation row 16-byte aligned
+        ny += c["rows"] if world == 1 else c["n"]
+    host_xb = torch.zeros(nx, dtype=torch.float16).pin_memory()
+    for c, o in zip(cfgs, xoff):
+        host_xb[o:o + c["k"]] = c["x"].reshape(-1).cpu()
+    host_yb = torch.empty(ny, dtype=torch.float32).pin_memory()
+    dev_xb = torch.empty(nx, dtype=torch.float16, device=dev)
+    need = max(lib.gsq_qmv_workspace_size(type_id(c["q"]), c["rows"], c["k"], 1) for c in cfgs)
+    ws = _lib.workspaces.get(dev, need, "qmv")
+    wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+    stream = _lib.stream_ptr(dev)
+    h2d, d2h = nx * 2, ny * 4
     if world == 1:
-        # As a C-ABI host drives it: the step's activations sit in one pinned
-        # host buffer and go to the device in one copy; one gsq_qmv call per
-        # projection (device pointers prepared once); the outputs come back
-        # to one pinned host buffer in one copy; one synchronisation per step.
-        from gsq_b200.quant.layouts import type_id
-        lib = _lib.load()
-        xoff, yoff = [], []
-        nx = ny = 0
-        for c in cfgs:
-            xoff.append(nx)
-            yoff.append(ny)
-            nx += -(-c["k"] // 8) * 8  # keep every activation row 16-byte aligned
-            ny += c["rows"]
-        host_xb = torch.zeros(nx, dtype=torch.float16).pin_memory()
-        for c, o in zip(cfgs, xoff):
-            host_xb[o:o + c["k"]] = c["x"].reshape(-1).cpu()
-        host_yb = torch.empty(ny, dtype=torch.float32).pin_memory()
-        dev_xb = torch.empty(nx, dtype=torch.float16, device=dev)
         dev_yb = torch.empty(ny, dtype=torch.float32, device=dev)
-        need = max(lib.gsq_qmv_workspace_size(type_id(c["q"]), c["rows"], c["k"], 1) for c in cfgs)
-        ws = _lib.workspaces.get(dev, need, "qmv")
-        wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
-        stream = _lib.stream_ptr(dev)
         calls = [(type_id(c["q"]), dev_xb.data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16], c["packed"].data_ptr(),
                   c["rows"], c["k"], 1, dev_yb.data_ptr() + 4 * yo, _lib.DTYPE_CODES[torch.float32], wsp, wsn, stream)
                  for c, xo, yo in zip(cfgs, xoff, yoff)]
-        h2d, d2h = nx * 2, ny * 4
         qmv = lib.gsq_qmv
 
         def e2e_step():
@@ -511,33 +701,10 @@ def main():
                     "C-ABI call per projection (ctypes, device pointers prepared once) -> outputs in one copy to "
                     "pinned host memory; one stream synchronisation per step")
     else:
-        # The same with the gather fused in: one gsq_qmv_gather call per
-        # projection (this rank's rows; every rank's rows land in the
-        # projection's gather region), then each region's gathered row is
-        # copied to the one pinned host buffer.
-        from gsq_b200.quant.layouts import type_id
-        lib = _lib.load()
-        xoff, yoff = [], []
-        nx = ny = 0
-        for c in cfgs:
-            xoff.append(nx)
-            yoff.append(ny)
-            nx += -(-c["k"] // 8) * 8
-            ny += c["n"]
-        host_xb = torch.zeros(nx, dtype=torch.float16).pin_memory()
-        for c, o in zip(cfgs, xoff):
-            host_xb[o:o + c["k"]] = c["x"].reshape(-1).cpu()
-        host_yb = torch.empty(ny, dtype=torch.float32).pin_memory()
-        dev_xb = torch.empty(nx, dtype=torch.float16, device=dev)
-        need = max(lib.gsq_qmv_workspace_size(type_id(c["q"]), c["rows"], c["k"], 1) for c in cfgs)
-        ws = _lib.workspaces.get(dev, need, "qmv")
-        wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
-        stream = _lib.stream_ptr(dev)
         calls = [(type_id(c["q"]), dev_xb.data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16], c["packed"].data_ptr(),
                   c["rows"], c["k"], 1, c["region"].regions, world, rank, rank * c["rows"], c["n"], wsp, wsn, stream)
                  for c, xo in zip(cfgs, xoff)]
         outs = [(host_yb[yo:yo + c["n"]], c["region"].y.reshape(-1)) for c, yo in zip(cfgs, yoff)]
-        h2d, d2h = nx * 2, ny * 4
         qmvg = lib.gsq_qmv_gather
 
         def e2e_step():
@@ -561,27 +728,34 @@ def main():
     e2e_steps = max(3, args.steps // 4)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    clocks.mark_start()
     t0.record()
     for _ in range(e2e_steps):
         e2e_step()
     t1.record()
     torch.cuda.synchronize()
+    clocks.mark_end()
+    device_ok(lib, dev, "the e2e steps")
     e2e_ms = t0.elapsed_time(t1)
     # the host copy of the outputs is the library's result
-    ref = matvec(cfgs[0], cfgs[0]["x"]).reshape(-1).cpu()
-    if not torch.allclose(host_yb[:ref.numel()], ref, rtol=1e-6, atol=0):
-        raise RuntimeError("end-to-end outputs differ from the library call")
+    for c, yo in zip(cfgs, yoff):
+        ref = matvec(c, c["x"]).reshape(-1).cpu()
+        if not torch.allclose(host_yb[yo:yo + ref.numel()], ref, rtol=1e-6, atol=0):
+            raise RuntimeError("end-to-end outputs differ from the library call")
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e = {"value": round(step_bytes * e2e_steps / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
-           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-           "path": e2e_path}
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "path": e2e_path}
+    for c in cfgs:
+        c["full"] = None if world == 1 else c["full"]
+    torch.cuda.empty_cache()
 
     # ---- QMM prefill, config 3 at M=512 (ranks > 1: each rank's row shard,
     # with the gather fused into the matmul's epilogue) ----
     qmm = None
+    qmm_worst = 0.0
     if not args.no_qmm:
         qres = []
         flops_total, t_qmm = 0.0, 0.0
@@ -591,46 +765,44 @@ def main():
                 full = random_matrix_torch(q, n, k, seed=7, device=dev)
                 rb = (k // 256) * BLOCK_BYTES[q]
                 w = full[rank * rows * rb:(rank + 1) * rows * rb].clone()
-                del full
                 x = torch.randn(512, k, device=dev, dtype=torch.bfloat16,
                                 generator=torch.Generator(device=dev).manual_seed(11))
                 region = GatherRegion(512, n) if world > 1 else None
 
                 def prefill():
                     if world > 1:
-                        quantized_matmul_gather(x, w, qtype=q, out_features=rows, in_features=k, region=region,
-                                                row0=rank * rows)
-                    else:
-                        quantized_matmul(x, w, qtype=q, out_features=rows, in_features=k, out_dtype=torch.float32)
+                        return quantized_matmul_gather(x, w, qtype=q, out_features=rows, in_features=k, region=region,
+                                                       row0=rank * rows)
+                    return quantized_matmul(x, w, qtype=q, out_features=rows, in_features=k, out_dtype=torch.float32)
 
                 for _ in range(2):
                     prefill()
                 torch.cuda.synchronize()
-                g = torch.cuda.CUDAGraph()
-                st = torch.cuda.Stream(device=dev)
-                st.wait_stream(torch.cuda.current_stream(dev))
-                with torch.cuda.stream(st):
-                    with torch.cuda.graph(g, stream=st):
-                        for _ in range(8):
-                            prefill()
-                torch.cuda.current_stream(dev).wait_stream(st)
+                g = graph_of(prefill, dev, reps=8)
                 g.replay()
                 torch.cuda.synchronize()
                 if world > 1:
                     dist.barrier()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                clocks.mark_start()
                 e0.record()
                 for _ in range(3):
                     g.replay()
                 e1.record()
                 torch.cuda.synchronize()
+                clocks.mark_end()
+                device_ok(lib, dev, f"qmm {q} {n}x{k}")
                 t_ms = e0.elapsed_time(e1) / 24
                 if world > 1:
+                    # the gathered output of the last replay against the single-GPU matmul of the whole matrix
+                    ref = quantized_matmul(x, full, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
+                    qmm_worst = max(qmm_worst, rel_l2(region.y[:512], ref))
+                    del ref
                     tt = torch.tensor([t_ms], device=dev)
                     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
                     t_ms = float(tt.item())
                     region.close()
-                del g
+                del g, full
                 fl = 2.0 * 512 * n * k
                 flops_total += fl
                 t_qmm += t_ms / 1e3
@@ -647,38 +819,52 @@ def main():
                        "CUDA graph of 8 launches, CUDA events" + (
                            f"; {world} ranks: row shards, the gather fused into the matmul epilogue, max over ranks, "
                            f"peak = {world} x the measured bf16 peak" if world > 1 else "")}
-
+        if world > 1:
+            t = torch.tensor([qmm_worst], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            qmm_worst = float(t.item())
+            parity["qmm_max_rel_l2"] = qmm_worst
+            parity["qmm_n_checked"] = len(qres)
     if qmm is not None and world == 1:
-        qmm["by_M"] = qmm_by_m(dev, pk)
+        qmm["by_M"] = qmm_by_m(dev, pk, lib, clocks)
+    for c in cfgs:
+        c["full"] = None
+    torch.cuda.empty_cache()
+
+    embed = None
+    if world == 1 and not args.no_embed:
+        embed = embed_bench(dev, pk, lib, clocks)
+
     model = None
     if not args.no_model:
         try:
-            model = model_bench(dev, pk, world)
+            model = model_bench(dev, pk, lib, clocks, world)
         except Exception as e:  # recorded in the line; the QMV and QMM results above still stand
             model = {"error": f"{type(e).__name__}: {e}"[:300]}
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        gbs, spent, sample = cpu_reference_sample(args.cpu_budget)
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
-               "sample": f"gguf-py 0.19.0 dequantize + numpy matvec over {', '.join(sample)} ({spent:.1f} s)"}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = dict(cpu_reference_sweep(), kind="reference")
+    clocks.stop()
 
+    parity["ok"] = parity["max_rel_l2"] <= PARITY_REL_L2 and parity.get("qmm_max_rel_l2", 0.0) <= PARITY_REL_L2
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "GB/s (packed weight bytes, QMV batch 1)",
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "per_rank_ms_per_step": [round(v / args.steps, 4) for v in per_rank_ms],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int8",
-            "dtype_note": "decoded packed entries (s8/u8) x two int8 activation levels on the tensor cores, "
-                          "s32 accumulate, fp32 scales and output; fp16 activations in",
+            "dtype": "fp16 x as 16-bit per-group fixed point, exact integer weights, s32 accumulate",
+            "dtype_note": "fp16 activations in; each 32-group of x becomes two int8 levels against its max |x| "
+                          "(16-bit fixed point); decoded packed entries are exact s8/u8 integers; int8 tensor-core "
+                          "MMAs accumulate in s32; per-sub-block scales and the output are fp32",
             "data": "synthetic",
-            "config": {"workload": "config-2 QMV sweep: 11 types x {5120->5120, 5120->17408, 17408->5120}, batch 1",
-                       "bytes_per_step": step_bytes, "l2": "inputs larger than L2 (886 MB per step)",
-                       "parallelism": (f"tp{world} (output rows; the gather is fused into the matvec: each "
-                                       f"value goes to every rank's inbox over NVLink)") if world > 1 else "single GPU",
-                       "timing": "CUDA graph of one step, replayed; CUDA events"},
-            "roofline": roofline, "qmv_sweep": per, "qmm_prefill": qmm, "cpu_baseline": cpu, "e2e": e2e,
-            "decode_tok_s_per_projection_pair": decode_tok_s(per), "model": model,
+            "config": dict(CONFIG),
+            "parallelism": (f"tp{world} (output rows; the gather is fused into the matvec: each value goes to "
+                            f"every rank's inbox over NVLink)") if world > 1 else "single GPU",
+            "timing": "CUDA graph of one step, replayed; CUDA events; max over ranks",
+            "roofline": roofline, "parity": parity, "qmv_sweep": per, "qmm_prefill": qmm, "embed": embed,
+            "cpu_baseline": cpu, "e2e": e2e, "decode_tok_s_per_projection_pair": decode_tok_s(per), "model": model,
             "clocks": clocks.summary(), "gpu_launches": args.steps * len(cfgs),
         }
         print(json.dumps(line), flush=True)
@@ -688,6 +874,8 @@ def main():
             c["region"].close()
         dist.barrier()
         dist.destroy_process_group()
+    if not parity["ok"]:
+        sys.exit(1)
 
 
 if __name__ == "__main__":

@@ -76,7 +76,9 @@ GSQ_API size_t gsq_qmv_workspace_size(int qtype, int64_t N, int64_t K, int64_t r
  * x: rows x K (x_dtype), 16-byte aligned.  y: rows x N (y_dtype).
  * packed: 16-byte aligned, N*(K/256)*bb bytes.  K % 256 == 0.
  * workspace: gsq_qmv_workspace_size() bytes, zero-filled before its first use;
- * every completed call leaves it zero-filled again.
+ * every completed call leaves it zero-filled again -- except after a bounded
+ * wait expired (gsq_device_status() == 1), which can leave stale slots: zero
+ * the workspace again before its next use.
  * Replaces quantized_matvec (mlx_gsq/runtime/kernels/qmv.py:537-576). */
 GSQ_API int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t rows,
             void* y, int y_dtype, void* workspace, size_t workspace_bytes, gsq_stream_t stream);
@@ -110,7 +112,9 @@ GSQ_API int gsq_embed(int qtype, const int32_t* ids, int64_t T, const uint8_t* p
  * Shapes that need more scratch return GSQ_ERR_WORKSPACE.  The first call on
  * a device looks up the array's address and should come before any stream
  * capture.  Every call shares the array: calls that overlap on the GPU race,
- * so order them (one stream, or events). */
+ * so order them (one stream, or events).  Bounded waits report through
+ * gsq_device_status() like gsq_qmv; when it reports an expired wait it also
+ * zero-fills this array, so calls after it start from a clean array. */
 GSQ_API int gsq_qmv_noalloc(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
                             int64_t rows, void* y, int y_dtype, gsq_stream_t stream);
 
@@ -157,7 +161,10 @@ GSQ_API int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t*
 
 /* Synchronises `stream`, then returns and clears the device error word the
  * kernels of the current device write (0 = none; 1 = a bounded wait expired;
- * 2 = an embedding id was out of range).  No reference counterpart: the
+ * 2 = an embedding id was out of range).  On 1 it also synchronises the
+ * device and zero-fills gsq_qmv_noalloc's fixed scratch array; workspaces
+ * that the caller passed to gsq_qmv / gsq_qmm / the gathers must be
+ * zero-filled again by the caller.  No reference counterpart: the
  * reference's Metal kernels have no device-side error path. */
 GSQ_API int gsq_device_status(gsq_stream_t stream);
 

@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstring>
 #include <algorithm>
+#include <mutex>
 
 #include "gsq_common.cuh"
 #include "../../include/gsq_b200.h"
@@ -36,10 +37,15 @@ int set_last_error(int code, const char* msg) {
 }
 }  // namespace gsq
 
-static int* device_error_word() {
+namespace gsq {
+// Device address of the error word on the current device (looked up once per
+// device; nullptr if CUDA cannot provide it).
+int* device_error_word() {
   static int* cache[64] = {nullptr};
+  static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
   if (!cache[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
@@ -47,6 +53,7 @@ static int* device_error_word() {
   }
   return cache[dev];
 }
+}  // namespace gsq
 
 static bool supported(int t) {
   switch (t) {
@@ -303,6 +310,15 @@ int gsq_device_status(gsq_stream_t stream) {
   if (e != cudaSuccess) return cuda_fail(e, "gsq_device_status read");
   const int zero = 0;
   cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  if (v == DEV_WAIT_TIMEOUT) {
+    // A wait that gave up may have been followed by the late write it was
+    // waiting for, leaving a non-zero piece slot or ticket in scratch that
+    // the next call expects zero.  The library's own fixed scratch
+    // (gsq_qmv_noalloc) is cleared here; caller workspaces are the caller's
+    // to re-zero (include/gsq_b200.h).
+    e = qmv_noalloc_scratch_clear();
+    if (e != cudaSuccess) return cuda_fail(e, "gsq_device_status scratch reset");
+  }
   return v;
 }
 

@@ -94,6 +94,15 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
                        float* y, void* ws, int* err, cudaStream_t st, const char** why,
                        const struct QmmGather* gather = nullptr);
 
+// Device address of the library's error word on the current device (the
+// word gsq_device_status reads); nullptr if it cannot be looked up.
+int* device_error_word();
+
+// Zero-fills gsq_qmv_noalloc's fixed scratch array on the current device
+// (synchronising the device first, so no kernel is still using it).  No-op on
+// a device where the array was never used.  Allocates nothing.
+cudaError_t qmv_noalloc_scratch_clear();
+
 // Records `msg` as this thread's gsq_last_error() text and returns `code`.
 int set_last_error(int code, const char* msg);
 

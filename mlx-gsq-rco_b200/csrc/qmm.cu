@@ -139,7 +139,7 @@ __device__ void qmm_gather_signal(const QmmArgs& a, bool stored) {
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own + p) : "memory");
       if ((int)(v - expected) >= 0) break;
       if (clock64() - t0 > (1ll << 31)) {
-        atomicExch(a.err, DEV_WAIT_TIMEOUT);
+        if (a.err) atomicExch(a.err, DEV_WAIT_TIMEOUT);
         return;
       }
       __nanosleep(64);

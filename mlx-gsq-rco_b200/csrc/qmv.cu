@@ -184,7 +184,7 @@ __device__ void gather_finish(const QmvArgs& a, unsigned ep) {
     unsigned long long w = ld_pair_sys(in + i);
     while ((unsigned)(w >> 32) != ep) {
       if (clock64() - t0 > (1ll << 31)) {
-        atomicExch(a.err, DEV_WAIT_TIMEOUT);
+        if (a.err) atomicExch(a.err, DEV_WAIT_TIMEOUT);
         late = true;
         break;
       }
@@ -572,7 +572,7 @@ __device__ void gather_pieces(const QmvArgs& a, int btile, int C, int c, int64_t
         __nanosleep(64);
         e = ld_relaxed_gpu(p);
         if (e == 0u && clock64() - t0 > (1ll << 31)) {
-          atomicExch(a.err, DEV_WAIT_TIMEOUT);
+          if (a.err) atomicExch(a.err, DEV_WAIT_TIMEOUT);
           break;
         }
       }

@@ -19,8 +19,14 @@
 //  * All calls share the one array.  Calls that overlap on the GPU (different
 //    streams, or threads without ordering) race on it; order them.
 //  * The array starts zero-filled (static device storage) and every completed
-//    call returns the ticket counters it used to zero, which is the state the
-//    next call needs; the partial-sum region needs no clearing.
+//    call returns the ticket counters and piece slots it used to zero, which
+//    is the state the next call needs; the partial-sum region needs no
+//    clearing.
+//  * Bounded waits report through the same device error word as gsq_qmv
+//    (gsq_device_status).  A wait that gave up can be followed by the late
+//    write it waited for, which would leave a slot non-zero; when
+//    gsq_device_status() reports an expired wait it also zero-fills this
+//    array (a memset, no allocation), so the next call starts clean.
 #include <cstdio>
 #include <mutex>
 
@@ -34,9 +40,12 @@ constexpr size_t kScratchBytes = GSQ_QMV_NOALLOC_SCRATCH_BYTES;
 
 __device__ __align__(256) unsigned char g_qmv_scratch[kScratchBytes];
 
+void* g_scratch_cache[64] = {nullptr};  // device address per device, once looked up
+std::mutex g_scratch_mu;
+
 void* scratch_address(int* status) {
-  static void* cache[64] = {nullptr};
-  static std::mutex mu;
+  void** cache = g_scratch_cache;
+  std::mutex& mu = g_scratch_mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     *status = GSQ_ERR_CUDA;
@@ -69,6 +78,25 @@ int supported_type(int t) {
 
 }  // namespace
 
+namespace gsq {
+cudaError_t qmv_noalloc_scratch_clear() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) return e;
+  void* p = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    p = g_scratch_cache[dev];
+  }
+  if (!p) return cudaSuccess;  // never used on this device: still zero
+  // Every stream of the device: a noalloc call still running elsewhere must
+  // not see the array cleared under it.
+  if ((e = cudaDeviceSynchronize()) != cudaSuccess) return e;
+  if ((e = cudaMemset(p, 0, kScratchBytes)) != cudaSuccess) return e;
+  return cudaDeviceSynchronize();
+}
+}  // namespace gsq
+
 extern "C" GSQ_API int gsq_qmv_noalloc(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N,
                                        int64_t K, int64_t rows, void* y, int y_dtype, gsq_stream_t stream) {
   // Same argument contract as gsq_qmv, minus the workspace.
@@ -97,7 +125,7 @@ extern "C" GSQ_API int gsq_qmv_noalloc(int qtype, const void* x, int x_dtype, co
   int status = GSQ_OK;
   void* ws = p.workspace > 0 ? scratch_address(&status) : nullptr;
   if (p.workspace > 0 && !ws) return status;
-  cudaError_t e = gsq::qmv_run(qtype, x, x_dtype, packed, N, K, (int)rows, y, y_dtype, ws, p, nullptr,
-                               (cudaStream_t)stream);
+  cudaError_t e = gsq::qmv_run(qtype, x, x_dtype, packed, N, K, (int)rows, y, y_dtype, ws, p,
+                               gsq::device_error_word(), (cudaStream_t)stream);
   return e == cudaSuccess ? GSQ_OK : set_last_error(GSQ_ERR_CUDA, cudaGetErrorString(e));
 }

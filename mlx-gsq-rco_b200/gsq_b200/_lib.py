@@ -151,3 +151,22 @@ class _Workspaces:
 
 
 workspaces = _Workspaces()
+
+DEV_WAIT_TIMEOUT = 1
+
+
+def device_status(device: torch.device | None = None) -> int:
+    """Synchronise the device's current stream and return (and clear) the
+    device error word: 0 none, 1 a bounded wait expired, 2 an embedding id
+    out of range.  After 1 the scratch of the calls may hold stale slots: the
+    library re-zeroes its own fixed array, and this re-zeroes the workspaces
+    the Python layer manages for the device."""
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(dev):
+        code = load().gsq_device_status(stream_ptr(dev))
+        if code < 0:
+            check(code)
+        if code == DEV_WAIT_TIMEOUT:
+            workspaces.reset(dev)
+            torch.cuda.synchronize(dev)
+    return code

@@ -1,0 +1,166 @@
+"""gsq_gdn (the gated-DeltaNet block of the model harness) against a float64
+NumPy restatement of the reference's own GDN forward.
+
+The reference replaces mlx-lm's GatedDeltaNet.__call__ with
+``_gguf_gated_delta_call`` (mlx_gsq/models/qwen35.py:48-106).  The
+restatement below follows it line by line:
+
+  * the causal depthwise conv over ``concat(conv_state, qkv)`` and the new
+    conv state as its last 3 rows (qwen35.py:61-74), then silu;
+  * the split into q, k (nk heads) and v (nv heads) (qwen35.py:75-82);
+  * ``q = inv_scale**2 * rms_norm(q)``, ``k = inv_scale * rms_norm(k)`` with
+    ``inv_scale = 128**-0.5``, no weight, eps 1e-6 (qwen35.py:84-86);
+  * llama.cpp's cyclic routing: q and k tiled ``repeats`` times along the
+    head axis, so value head h reads key head ``h % nk`` (qwen35.py:87-94);
+  * ``A_log = log(-ssm_a)`` from GGUF's stored coefficient (qwen35.py:43-45,
+    141);
+  * mlx-lm's ``gated_delta_update`` (qwen35.py:95-98; the mlx-lm source is
+    not in the reference repository, so it is restated from the published
+    gated delta rule it implements): ``beta = sigmoid(b)``,
+    ``g = exp(-exp(A_log) * softplus(a + dt_bias))``, per value head
+    ``S <- g S``, ``S <- S + beta (v - S k) k^T``, ``o = S q``;
+  * ``self.norm(out, z)``: RMS norm over each 128-wide head with weight,
+    times silu(z) (qwen35.py:102).
+
+gsq_gdn is called through the C ABI for a prompt of several tokens (the
+three-kernel path), for single decode tokens (the one-kernel path, with the
+decay and write-gate inputs computed inside it from x and the ssm_alpha /
+ssm_beta rows) and for a short prompt on that path too, carrying the
+recurrent and conv state across calls.  Reduced head counts keep the
+reference's 3:1 value-to-key head ratio (48:16 in the 27B model).
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import rel_l2
+from gsq_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+D = 128          # head width (key and value), qwen35.py:26-27
+NK, NV = 2, 6    # key / value heads: ratio 1:3 as 16:48 in the model
+HIDDEN = 256
+EPS = 1e-6
+TOL = 1e-4       # fp32 kernels against float64
+
+
+def _silu(x):
+    return x / (1.0 + np.exp(-x))
+
+
+def _softplus(x):
+    return np.logaddexp(0.0, x)
+
+
+def _rms_norm(x, w, eps):
+    y = x / np.sqrt((x * x).mean(-1, keepdims=True) + eps)
+    return y * w if w is not None else y
+
+
+class ReferenceGDN:
+    """_gguf_gated_delta_call for one sequence (B = 1), float64."""
+
+    def __init__(self, conv_w, ssm_a, dt_bias, norm_w):
+        self.conv_w = conv_w.astype(np.float64)        # [C, 4]: (conv_dim, kernel) as conv1d.weight[..., 0]
+        self.A_log = np.log(-ssm_a.astype(np.float64))  # _restore_a_log
+        self.dt_bias = dt_bias.astype(np.float64)
+        self.norm_w = norm_w.astype(np.float64)
+        C = conv_w.shape[0]
+        self.conv_state = np.zeros((3, C))
+        self.state = np.zeros((NV, D, D))               # [value head, value index, key index]
+
+    def __call__(self, qkv, z, a, b):
+        S = qkv.shape[0]
+        conv_input = np.concatenate([self.conv_state, qkv], 0)
+        self.conv_state = conv_input[-3:].copy()
+        conv = np.stack([(conv_input[t:t + 4].T * self.conv_w).sum(-1) for t in range(S)])
+        conv_out = _silu(conv)
+        kd = NK * D
+        q = conv_out[:, :kd].reshape(S, NK, D)
+        k = conv_out[:, kd:2 * kd].reshape(S, NK, D)
+        v = conv_out[:, 2 * kd:].reshape(S, NV, D)
+        inv_scale = D ** -0.5
+        q = inv_scale ** 2 * _rms_norm(q, None, 1e-6)
+        k = inv_scale * _rms_norm(k, None, 1e-6)
+        repeats = NV // NK
+        q = np.tile(q, (1, repeats, 1))
+        k = np.tile(k, (1, repeats, 1))
+        beta = 1.0 / (1.0 + np.exp(-b))
+        g = np.exp(-np.exp(self.A_log) * _softplus(a + self.dt_bias))
+        out = np.empty((S, NV, D))
+        for t in range(S):
+            for h in range(NV):
+                St = self.state[h] * g[t, h]
+                delta = (v[t, h] - St @ k[t, h]) * beta[t, h]
+                St = St + np.outer(delta, k[t, h])
+                self.state[h] = St
+                out[t, h] = St @ q[t, h]
+        out = _rms_norm(out, self.norm_w, EPS) * _silu(z.reshape(S, NV, D))
+        return out.reshape(S, NV * D)
+
+
+def _f32(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
+
+
+def test_gdn_matches_reference_override():
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(11)
+    C = 2 * NK * D + NV * D
+    conv_w = rng.normal(0.0, 0.5, (C, 4)).astype(np.float32)
+    ssm_a = (-np.exp(rng.uniform(-1.5, 1.0, NV))).astype(np.float32)   # GGUF stores -exp(A_log)
+    dt_bias = rng.uniform(-1.0, 1.0, NV).astype(np.float32)
+    norm_w = (1.0 + 0.1 * rng.normal(size=D)).astype(np.float32)
+    ab_w = rng.normal(0.0, HIDDEN ** -0.5, (2 * NV, HIDDEN)).astype(np.float16)  # ssm_alpha rows, ssm_beta rows
+    ref = ReferenceGDN(conv_w, ssm_a, dt_bias, norm_w)
+
+    lib = _lib.load()
+    conv_state = torch.zeros(4, C, device=dev)
+    state = torch.zeros(NV, D, D, device=dev)
+    pos = torch.zeros(1, dtype=torch.int32, device=dev)
+    d_conv_w, d_A, d_dt, d_norm = (_f32(conv_w, dev), _f32(ssm_a, dev), _f32(dt_bias, dev), _f32(norm_w, dev))
+    d_abw = torch.from_numpy(ab_w).to(dev)
+    _lib.device_status(dev)
+
+    def run(T, with_ab):
+        qkv = rng.normal(0.0, 1.0, (T, C)).astype(np.float32)
+        z = rng.normal(0.0, 1.0, (T, NV * D)).astype(np.float32)
+        x = rng.normal(0.0, 1.0, (T, HIDDEN)).astype(np.float16)
+        ab_exact = x.astype(np.float64) @ ab_w.astype(np.float64).T       # in_proj_a | in_proj_b
+        proj = _f32(np.concatenate([qkv, z], 1), dev)
+        d_x = torch.from_numpy(x).to(dev)
+        if with_ab:  # a and b handed over as fp16 (the prompt path's GEMM output)
+            ab16 = ab_exact.astype(np.float16)
+            d_ab = torch.from_numpy(ab16).to(dev)
+            a, b = ab16[:, :NV].astype(np.float64), ab16[:, NV:].astype(np.float64)
+        else:        # computed inside the kernel from x and the ssm_alpha / ssm_beta rows
+            d_ab = None
+            a, b = ab_exact[:, :NV], ab_exact[:, NV:]
+        need = lib.gsq_gdn_scratch_bytes(T, NK, NV)
+        scratch = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+        out = torch.empty(T, NV * D, dtype=torch.float32, device=dev)
+        _lib.check(lib.gsq_gdn(proj.data_ptr(), proj.stride(0), d_ab.data_ptr() if d_ab is not None else None,
+                               d_ab.stride(0) if d_ab is not None else 0, d_x.data_ptr(), d_x.stride(0),
+                               d_abw.data_ptr(), HIDDEN, T, NK, NV, conv_state.data_ptr(), pos.data_ptr(),
+                               d_conv_w.data_ptr(), d_A.data_ptr(), d_dt.data_ptr(), d_norm.data_ptr(), EPS,
+                               state.data_ptr(), scratch.data_ptr(), need, out.data_ptr(), 0,
+                               _lib.stream_ptr(dev)))
+        pos.add_(T)
+        exp = ref(qkv.astype(np.float64), z.astype(np.float64), a, b)
+        got = out.cpu().numpy()
+        return rel_l2(got, exp), rel_l2(state.cpu().numpy(), ref.state)
+
+    for T, with_ab in ((9, True), (1, False), (1, False), (3, False), (12, True), (1, False)):
+        e_out, e_state = run(T, with_ab)
+        assert e_out <= TOL, (T, with_ab, e_out)
+        assert e_state <= TOL, (T, with_ab, e_state)
+    assert _lib.device_status(dev) == 0
+
+
+def test_cyclic_routing_differs_from_grouped_repeat():
+    """The restatement's routing is the one the reference asks for: with the
+    grouped repeat mlx-lm would otherwise apply (head h reading key head
+    h // repeats) the outputs differ, so the comparison above pins it."""
+    h = np.arange(NV)
+    assert list(h % NK) != list(h // (NV // NK))

@@ -54,8 +54,11 @@ def test_qmm_shapes(qtype, m, nk, oracle_mod):
 
 @pytest.mark.parametrize("qtype", ["IQ2_XS", "IQ3_S", "IQ4_XS", "Q6_K"])
 @pytest.mark.parametrize("nk", [(17408, 5120), (5120, 17408)])
-@pytest.mark.parametrize("m", [16, 512])
+@pytest.mark.parametrize("m", [16, 182, 512, 2048])
 def test_qmm_config3(qtype, nk, m):
+    """Config 3 at full size and every token count it names (M=2048 is the
+    one case with several 512-token groups per weight tile; M=182 is ragged
+    against every tile width)."""
     n, k = nk
     packed = random_packed_gpu(qtype, n, k, seed=m + n)
     x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)

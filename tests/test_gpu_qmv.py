@@ -86,3 +86,33 @@ def test_qmv_zero_activation():
     y = quantized_matvec(torch.zeros(1, 1024, device="cuda"), packed, qtype="Q6_K", out_features=256,
                          in_features=1024)
     assert torch.count_nonzero(y) == 0
+
+
+def _outlier_activations(k: int, seed: int) -> torch.Tensor:
+    """fp16 activations shaped like post-RMSNorm rows with outlier channels:
+    N(0,1) values, in every 32-group one channel 1000x larger, some groups
+    entirely tiny (1e-3 scale) and one group all zero."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(k // 32, 32, generator=g, dtype=torch.float64)
+    ch = torch.randint(0, 32, (k // 32,), generator=g)
+    sign = torch.where(torch.rand(k // 32, generator=g) < 0.5, -1.0, 1.0)
+    x[torch.arange(k // 32), ch] = sign * 1000.0 * (1.0 + torch.rand(k // 32, generator=g))
+    tiny = torch.randperm(k // 32, generator=g)[:8]
+    x[tiny] = torch.randn(8, 32, generator=g, dtype=torch.float64) * 1e-3
+    x[int(torch.randperm(k // 32, generator=g)[0])] = 0.0
+    return x.reshape(1, k).to(torch.float16).cuda()
+
+
+@pytest.mark.parametrize("qtype", SUPPORTED_QUANT_TYPES)
+def test_qmv_outlier_activations(qtype):
+    """The matvec quantises each 32-group of x to 16-bit fixed point against
+    the group's max |x|; activations with a 1000x outlier channel in every
+    group, all-tiny groups and an all-zero group are held to the same bar,
+    rel-L2 <= 1e-3 against the float64 product with the bit-exact dequant."""
+    n = k = 5120
+    packed = random_packed_gpu(qtype, n, k, seed=77)
+    x = _outlier_activations(k, seed=5)
+    y = quantized_matvec(x, packed, qtype=qtype, out_features=n, in_features=k, out_dtype=torch.float32)
+    exp = x.double() @ dense_gpu(packed, qtype, n, k).T
+    assert torch.isfinite(y).all()
+    assert rel_l2(y.cpu(), exp.cpu()) <= REL_L2

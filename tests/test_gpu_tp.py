@@ -1,8 +1,9 @@
-"""Output-row tensor parallelism on real GPUs: two NCCL ranks, each holding
-half of a packed projection's rows, must reproduce the single-GPU result
-(matvec with the gather fused in, matmul with an NCCL all-gather), also over
-repeated calls and CUDA-graph replays of the fused gather.  Skipped with
-fewer than two GPUs."""
+"""Output-row tensor parallelism on real GPUs: 2, 4 or 8 NCCL ranks, each
+holding its slice of a packed projection's rows, must reproduce the
+single-GPU result (matvec with the gather fused in, matmul with the gather
+fused into its epilogue, and the NCCL all-gather path), also over repeated
+calls and CUDA-graph replays of the fused gather.  Each world size is skipped
+when fewer GPUs are visible."""
 import os
 import socket
 
@@ -114,23 +115,28 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_row_parallel_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _spawn(target, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=240)
-    results = sorted(q.get(timeout=5) for _ in range(2))
-    assert results == [(0, True), (1, True)]
+        p.join(timeout=300)
+    results = sorted(q.get(timeout=5) for _ in range(world))
+    assert results == [(r, True) for r in range(world)]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_row_parallel(world):
+    _spawn(_worker, world)
 
 
 def _model_worker(rank, world, port, q):
-    """The Qwen3.5-hybrid harness split over two ranks against the same model
+    """The Qwen3.5-hybrid harness split over the ranks against the same model
     on one GPU (same weights, built on every rank from the same seed)."""
     import torch.distributed as dist
     from datetime import timedelta
@@ -171,16 +177,6 @@ def _model_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_model_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_model_worker, args=(r, 2, port, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=240)
-    results = sorted(q.get(timeout=5) for _ in range(2))
-    assert results == [(0, True), (1, True)]
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_model_tensor_parallel(world):
+    _spawn(_model_worker, world)
