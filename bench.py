@@ -398,12 +398,8 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
     cfg = Qwen35Config()
     w = random_weights(cfg, dev, seed=0)  # the same bytes on every rank; each keeps its rows
     max_len = max((prompt,) + tuple(prefill_ms)) + decode_tokens + 16
-    try:
-        model = build_qwen35(w, cfg, dev, max_len=max_len, max_batch=max(batches),
-                             group=dist.group.WORLD if world > 1 else None)
-    except TypeError:
-        model = build_qwen35(w, cfg, dev, max_len=max_len, group=dist.group.WORLD if world > 1 else None)
-        batches = (1,)
+    model = build_qwen35(w, cfg, dev, max_len=max_len, max_batch=max(batches),
+                         group=dist.group.WORLD if world > 1 else None)
     del w
     torch.cuda.empty_cache()
     gen = torch.Generator(device=dev).manual_seed(1)
@@ -454,8 +450,7 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
         gbs = out["packed_bytes_per_token"] / t / 1e9
         decode.append({"batch": B, "ms_per_step": round(t * 1e3, 3), "tok_s": round(B / t, 1),
                        "packed_gbs": round(gbs, 1), "roofline_frac": round(gbs / (pk["hbm"] * world), 4)})
-        if hasattr(model, "release_graph"):
-            model.release_graph()
+        model.release_graph()
     d1 = decode[0]
     out.update({"decode_tokens": decode_tokens, "decode_ms_per_token": d1["ms_per_step"],
                 "decode_tok_s": d1["tok_s"], "decode_packed_gbs": d1["packed_gbs"],

@@ -85,6 +85,19 @@ GSQ_API int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, 
                     const float* dt_bias, const float* norm_w, float eps, float* state, void* scratch,
                     size_t scratch_bytes, void* out, int out_dtype, gsq_stream_t stream);
 
+/* One decode token of each of `batch` sequences (batched decode), all at
+ * position *pos: sequence b's token is row b of proj [batch, proj_stride]
+ * and of ab [batch, ab_stride] (or of x [batch, x_stride] with ab NULL); its
+ * conv ring is conv_state[b] ([batch, 4, C]), its recurrent state state[b]
+ * ([batch, nv, 128, 128]) and its output row b of out [batch, nv*128].  The
+ * per-token formulas are gsq_gdn's.  No scratch.  Extends the reference's
+ * single-sequence GDN call (mlx_gsq/models/qwen35.py:48-106) to a batch. */
+GSQ_API int gsq_gdn_batch(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t ab_stride,
+                          const uint16_t* x, int64_t x_stride, const uint16_t* ab_w, int64_t hidden, int64_t batch,
+                          int64_t nk, int64_t nv, float* conv_state, const int32_t* pos, const float* conv_w,
+                          const float* A, const float* dt_bias, const float* norm_w, float eps, float* state,
+                          void* out, int out_dtype, gsq_stream_t stream);
+
 /* One decode token of gated GQA attention (qwen35.py:137-145 with mlx_lm's
  * attention): qkv [nq*512 + 2*nkv*256] fp32 = per query head 256 query
  * values then 256 gate values, then the key heads, then the value heads.
@@ -99,6 +112,15 @@ GSQ_API int gsq_attn_decode(const float* qkv, int64_t nq, int64_t nkv, const flo
                             const float* k_norm_w, float eps, int64_t rot, float theta, float* k_cache,
                             float* v_cache, int64_t max_len, const int32_t* pos, void* out, int out_dtype,
                             gsq_stream_t stream);
+
+/* gsq_attn_decode for one token of each of `batch` sequences at position
+ * *pos: sequence b's qkv is row b of qkv [batch, nq*512 + 2*nkv*256], its
+ * caches are k_cache[b] / v_cache[b] ([batch, max_len, nkv, 256]) and its
+ * output row b of out [batch, nq*256]. */
+GSQ_API int gsq_attn_decode_batch(const float* qkv, int64_t nq, int64_t nkv, const float* q_norm_w,
+                                  const float* k_norm_w, float eps, int64_t rot, float theta, float* k_cache,
+                                  float* v_cache, int64_t max_len, const int32_t* pos, void* out, int out_dtype,
+                                  int64_t batch, gsq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -369,12 +369,23 @@ __global__ void __launch_bounds__(GDN_D) gdn_scan_kernel(GdnArgs a) {
 // recurrence to column j, key indices 64r..64r+63, held in registers; the
 // gated norm closes the head.  The conv window slot of this position is
 // written by the CTAs that own the channels (q/k: h < nk) and is not read by
-// any CTA at this position.
-__global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(GdnArgs a) {
+// any CTA at this position.  Batched decode: blockIdx.y is the sequence b of
+// the batch, whose token is row b of proj / x / ab, whose conv ring and
+// state follow the previous sequence's (4*C and nv*128*128 floats), and whose
+// output is row b of out; every sequence is at position *pos.
+__global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(const GdnArgs a0) {
   __shared__ float red[32];
   __shared__ float qs[GDN_D], ks[GDN_D], vs[GDN_D];
   pdl_launch_dependents();
   pdl_wait();
+  const int64_t seq = blockIdx.y;
+  GdnArgs a = a0;
+  a.proj = a0.proj + seq * a0.ps;
+  if (a0.ab) a.ab = a0.ab + seq * a0.abs;
+  if (a0.x) a.x = a0.x + seq * a0.xs;
+  a.conv_state = a0.conv_state + seq * 4 * a0.C;
+  a.state = a0.state + seq * a0.nv * GDN_D * GDN_D;
+  const int64_t obase = seq * a0.nv * GDN_D;
   const int h = blockIdx.x, kh = h % a.nk, tid = threadIdx.x, warp = tid >> 5;
   const int pos = *a.pos;
   const int i = tid & (GDN_D - 1);
@@ -441,7 +452,7 @@ __global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(GdnArgs a) {
   const float ss = block_sum(r == 0 ? y * y : 0.f, red);
   if (r == 0) {
     const float z = a.proj[a.C + h * GDN_D + j];
-    store_out(a.out, a.dt, (int64_t)h * GDN_D + j, y * rsqrtf(ss / GDN_D + a.eps) * a.norm_w[j] * silu(z));
+    store_out(a.out, a.dt, obase + (int64_t)h * GDN_D + j, y * rsqrtf(ss / GDN_D + a.eps) * a.norm_w[j] * silu(z));
   }
 }
 
@@ -459,15 +470,24 @@ __global__ void __launch_bounds__(GDN_D) gdn_norm_kernel(GdnArgs a) {
 
 // One decode token of gated GQA attention; CTA = query head, 256 threads =
 // head dimensions.  Dynamic shared memory: scores of positions 0..pos.
-__global__ void __launch_bounds__(ATT_D) attn_decode_kernel(const float* qkv, int nq, int nkv, const float* qw,
+// Batched decode: blockIdx.y is the sequence b, whose qkv row follows the
+// previous sequence's (nq*512 + 2*nkv*256 floats), whose caches follow the
+// previous sequence's (max_len*nkv*256 floats each), and whose output is row
+// b of out; every sequence is at position *pos.
+__global__ void __launch_bounds__(ATT_D) attn_decode_kernel(const float* qkv0, int nq, int nkv, const float* qw,
                                                             const float* kw, float eps, int rot, float theta,
-                                                            float* kc, float* vc, int max_len, const int* pos_p,
+                                                            float* kc0, float* vc0, int max_len, const int* pos_p,
                                                             void* out, int dt) {
   extern __shared__ float sc[];
   __shared__ float red[32];
   __shared__ __align__(16) float qs[ATT_D], ks[ATT_D], vs[ATT_D];
   pdl_launch_dependents();
   pdl_wait();
+  const int64_t seq = blockIdx.y;
+  const float* qkv = qkv0 + seq * ((int64_t)nq * 2 * ATT_D + (int64_t)nkv * 2 * ATT_D);
+  float* kc = kc0 + seq * (int64_t)max_len * nkv * ATT_D;
+  float* vc = vc0 + seq * (int64_t)max_len * nkv * ATT_D;
+  const int64_t obase = seq * (int64_t)nq * ATT_D;
   const int h = blockIdx.x, d = threadIdx.x;
   const int group = nq / nkv, kvh = h / group;
   const int pos = min(max(*pos_p, 0), max_len - 1);
@@ -565,7 +585,7 @@ __global__ void __launch_bounds__(ATT_D) attn_decode_kernel(const float* qkv, in
   float o = 0.f;
 #pragma unroll
   for (int w = 0; w < ATT_D / 32; w++) o += part[w][d];
-  store_out(out, dt, (int64_t)h * ATT_D + d, o / l / (1.f + __expf(-gate)));
+  store_out(out, dt, obase + (int64_t)h * ATT_D + d, o / l / (1.f + __expf(-gate)));
 }
 
 bool dt_ok(int d) { return d == DT_F32 || d == DT_F16 || d == DT_BF16; }
@@ -624,12 +644,20 @@ size_t gsq_gdn_scratch_bytes(int64_t T, int64_t nk, int64_t nv) {
   return 2 * align16(T * nk * GDN_D * f) + 2 * align16(T * nv * GDN_D * f) + 2 * align16(T * nv * f);
 }
 
-int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t ab_stride, const uint16_t* x,
+}  // extern "C"
+
+namespace {
+
+// gsq_gdn (batch == 1: T tokens of one sequence) and gsq_gdn_batch (T == 1:
+// one token of each of `batch` sequences).
+int gdn_run(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t ab_stride, const uint16_t* x,
             int64_t x_stride, const uint16_t* ab_w, int64_t hidden, int64_t T, int64_t nk, int64_t nv,
             float* conv_state, const int32_t* pos, const float* conv_w, const float* A, const float* dt_bias,
             const float* norm_w, float eps, float* state, void* scratch, size_t scratch_bytes, void* out,
-            int out_dtype, gsq_stream_t stream) {
+            int out_dtype, int64_t batch, gsq_stream_t stream) {
   auto al16 = [](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  if (batch < 0 || batch > 65535 || (batch > 1 && T != 1)) return fail(GSQ_ERR_SIZE, "gsq_gdn: bad batch");
+  if (batch == 0) return GSQ_OK;
   if (!proj || !conv_state || !pos || !conv_w || !A || !dt_bias || !norm_w || !state || !out)
     return fail(GSQ_ERR_ARG, "gsq_gdn: null pointer");
   if (!ab && (!x || !ab_w || hidden <= 0 || hidden > INT32_MAX || x_stride < hidden))
@@ -672,7 +700,7 @@ int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t 
   a.dt = out_dtype;
   cudaStream_t st = (cudaStream_t)stream;
   if (T == 1) {
-    launch_pdl(gdn_decode_kernel, dim3((unsigned)nv), dim3(2 * GDN_D), 0, st, a);
+    launch_pdl(gdn_decode_kernel, dim3((unsigned)nv, (unsigned)batch), dim3(2 * GDN_D), 0, st, a);
     return launched("gsq_gdn (one token)");
   }
   uint8_t* p = static_cast<uint8_t*>(scratch);
@@ -697,9 +725,39 @@ int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t 
   return launched("gsq_gdn (norm)");
 }
 
+}  // namespace
+
+extern "C" {
+
+int gsq_gdn(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t ab_stride, const uint16_t* x,
+            int64_t x_stride, const uint16_t* ab_w, int64_t hidden, int64_t T, int64_t nk, int64_t nv,
+            float* conv_state, const int32_t* pos, const float* conv_w, const float* A, const float* dt_bias,
+            const float* norm_w, float eps, float* state, void* scratch, size_t scratch_bytes, void* out,
+            int out_dtype, gsq_stream_t stream) {
+  return gdn_run(proj, proj_stride, ab, ab_stride, x, x_stride, ab_w, hidden, T, nk, nv, conv_state, pos, conv_w, A,
+                 dt_bias, norm_w, eps, state, scratch, scratch_bytes, out, out_dtype, 1, stream);
+}
+
+int gsq_gdn_batch(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t ab_stride, const uint16_t* x,
+                  int64_t x_stride, const uint16_t* ab_w, int64_t hidden, int64_t batch, int64_t nk, int64_t nv,
+                  float* conv_state, const int32_t* pos, const float* conv_w, const float* A, const float* dt_bias,
+                  const float* norm_w, float eps, float* state, void* out, int out_dtype, gsq_stream_t stream) {
+  return gdn_run(proj, proj_stride, ab, ab_stride, x, x_stride, ab_w, hidden, 1, nk, nv, conv_state, pos, conv_w, A,
+                 dt_bias, norm_w, eps, state, nullptr, 0, out, out_dtype, batch, stream);
+}
+
 int gsq_attn_decode(const float* qkv, int64_t nq, int64_t nkv, const float* q_norm_w, const float* k_norm_w,
                     float eps, int64_t rot, float theta, float* k_cache, float* v_cache, int64_t max_len,
                     const int32_t* pos, void* out, int out_dtype, gsq_stream_t stream) {
+  return gsq_attn_decode_batch(qkv, nq, nkv, q_norm_w, k_norm_w, eps, rot, theta, k_cache, v_cache, max_len, pos,
+                               out, out_dtype, 1, stream);
+}
+
+int gsq_attn_decode_batch(const float* qkv, int64_t nq, int64_t nkv, const float* q_norm_w, const float* k_norm_w,
+                          float eps, int64_t rot, float theta, float* k_cache, float* v_cache, int64_t max_len,
+                          const int32_t* pos, void* out, int out_dtype, int64_t batch, gsq_stream_t stream) {
+  if (batch < 0 || batch > 65535) return fail(GSQ_ERR_SIZE, "gsq_attn_decode: bad batch");
+  if (batch == 0) return GSQ_OK;
   if (!qkv || !q_norm_w || !k_norm_w || !k_cache || !v_cache || !pos || !out)
     return fail(GSQ_ERR_ARG, "gsq_attn_decode: null pointer");
   if (nq <= 0 || nkv <= 0 || nq % nkv || nq > 65535) return fail(GSQ_ERR_SIZE, "gsq_attn_decode: bad head counts");
@@ -715,7 +773,8 @@ int gsq_attn_decode(const float* qkv, int64_t nq, int64_t nkv, const float* q_no
         cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(GSQ_ERR_CUDA, "gsq_attn_decode: shared memory attribute");
   }
-  launch_pdl(attn_decode_kernel, dim3((unsigned)nq), dim3(ATT_D), smem, st, qkv, (int)nq, (int)nkv, q_norm_w,
+  launch_pdl(attn_decode_kernel, dim3((unsigned)nq, (unsigned)batch), dim3(ATT_D), smem, st, qkv, (int)nq, (int)nkv,
+             q_norm_w,
              k_norm_w, eps, (int)rot, theta, k_cache, v_cache, (int)max_len, pos, out, out_dtype);
   return launched("gsq_attn_decode");
 }

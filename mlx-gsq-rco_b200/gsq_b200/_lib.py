@@ -56,6 +56,10 @@ SIGNATURES = {
                      ctypes.c_float, _P, _P, _SZ, _P, _I, _P]),
     "gsq_attn_decode": (_I, [_P, _I64, _I64, _P, _P, ctypes.c_float, _I64, ctypes.c_float, _P, _P, _I64, _P, _P, _I,
                              _P]),
+    "gsq_gdn_batch": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P,
+                           ctypes.c_float, _P, _P, _I, _P]),
+    "gsq_attn_decode_batch": (_I, [_P, _I64, _I64, _P, _P, ctypes.c_float, _I64, ctypes.c_float, _P, _P, _I64, _P, _P,
+                                   _I, _I64, _P]),
 }
 
 _lib = None

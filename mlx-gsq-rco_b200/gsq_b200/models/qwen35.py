@@ -298,9 +298,13 @@ class Qwen35:
     Norms, the gated-DeltaNet and attention blocks run on every rank on the
     gathered (identical) vectors."""
 
-    def __init__(self, weights: dict, cfg: Qwen35Config, device, max_len: int = 2304, group=None):
+    def __init__(self, weights: dict, cfg: Qwen35Config, device, max_len: int = 2304, group=None,
+                 max_batch: int = 1):
         cfg.check()
+        if max_batch < 1:
+            raise ValueError("max_batch must be at least 1")
         self.cfg, self.dev, self.max_len = cfg, torch.device(device), max_len
+        self.max_batch, self.batch = int(max_batch), 1
         self.eps = cfg.rms_norm_eps
         w = weights
         self.embed = w["token_embd.weight"]
@@ -324,15 +328,17 @@ class Qwen35:
                 L["A"] = w[p + "ssm_a"].float().contiguous()
                 L["dt_bias"] = w[p + "ssm_dt.bias"].float().contiguous()
                 L["norm"] = w[p + "ssm_norm.weight"].float().contiguous()
-                L["conv_state"] = torch.zeros(4, cfg.gdn_conv_dim, device=self.dev)  # ring, slot = position & 3
-                L["state"] = torch.zeros(nv, cfg.linear_value_head_dim, cfg.linear_key_head_dim, device=self.dev)
+                # per sequence of the batch: conv ring (slot = position & 3) and recurrent state
+                L["conv_state"] = torch.zeros(max_batch, 4, cfg.gdn_conv_dim, device=self.dev)
+                L["state"] = torch.zeros(max_batch, nv, cfg.linear_value_head_dim, cfg.linear_key_head_dim,
+                                         device=self.dev)
             else:
                 L["qkv"] = _Packed([w[p + "attn_q.weight"], w[p + "attn_k.weight"], w[p + "attn_v.weight"]])
                 L["o"] = _Packed([w[p + "attn_output.weight"]])
                 L["q_norm"] = w[p + "attn_q_norm.weight"].float().contiguous()
                 L["k_norm"] = w[p + "attn_k_norm.weight"].float().contiguous()
-                L["k_cache"] = torch.zeros(max_len, nkv, hd, device=self.dev)
-                L["v_cache"] = torch.zeros(max_len, nkv, hd, device=self.dev)
+                L["k_cache"] = torch.zeros(max_batch, max_len, nkv, hd, device=self.dev)
+                L["v_cache"] = torch.zeros(max_batch, max_len, nkv, hd, device=self.dev)
             self.layers.append(L)
         self.world = dist.get_world_size(group) if group is not None else 1
         self._prefill_regions = {}
@@ -354,7 +360,7 @@ class Qwen35:
                 if pk is not self.lm_head:
                     pk.prefill_region = self._prefill_regions[pk.n]
         self.pos = torch.zeros(1, dtype=torch.int32, device=self.dev)   # next position (decode)
-        self.cur_id = torch.zeros(1, dtype=torch.int32, device=self.dev)  # token to feed next (decode)
+        self.cur_id = torch.zeros(max_batch, dtype=torch.int32, device=self.dev)  # tokens to feed next (decode)
         self.n_pos = 0  # host copy of the position (prefill bookkeeping)
         self._graph = None
         inv = cfg.rope_theta ** (-torch.arange(0, cfg.rotary_dim, 2, dtype=torch.float32) / cfg.rotary_dim)
@@ -384,21 +390,54 @@ class Qwen35:
         return sum(pk.nbytes for pk in self._projections()) + self.embed.num_bytes // self.cfg.vocab_size
 
     def reset(self) -> None:
+        """Empties sequence 0 and makes it the only one (batch 1)."""
         for L in self.layers:
             if L["linear"]:
-                L["conv_state"].zero_()
-                L["state"].zero_()
+                L["conv_state"][0].zero_()
+                L["state"][0].zero_()
         self.pos.zero_()
         self.n_pos = 0
+        self.batch = 1
+        self._graph = None
+
+    def fork(self, batch: int) -> None:
+        """Batched decode from the current state: sequences 1..batch-1 become
+        copies of sequence 0 (conv rings, recurrent states, caches up to the
+        current position, next token); decode steps then advance all of them
+        together, one token per sequence."""
+        if not 1 <= batch <= self.max_batch:
+            raise ValueError(f"batch must be in 1..{self.max_batch}")
+        n = self.n_pos
+        for L in self.layers:
+            if L["linear"]:
+                L["conv_state"][1:batch].copy_(L["conv_state"][0:1].expand(batch - 1, -1, -1))
+                L["state"][1:batch].copy_(L["state"][0:1].expand(batch - 1, -1, -1, -1))
+            else:
+                for key in ("k_cache", "v_cache"):
+                    L[key][1:batch, :n].copy_(L[key][0:1, :n].expand(batch - 1, -1, -1, -1))
+        self.cur_id[1:batch].copy_(self.cur_id[0:1].expand(batch - 1))
+        self.batch = batch
+        self._graph = None
 
     # ---- blocks ----
-    def _gdn(self, L, p: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
-        """The gated-DeltaNet block on the q|k|v|z projection p of input h.
-        The 2 x 48 gate rows (plain fp16) are a cuBLAS GEMM for prompts and
-        are computed inside the block's first kernel for decode tokens."""
+    def _gdn(self, L, p: torch.Tensor, h: torch.Tensor, decode: bool = False) -> torch.Tensor:
+        """The gated-DeltaNet block on the q|k|v|z projection p of input h:
+        a prompt of p.shape[0] tokens of sequence 0, or (``decode``) one token
+        of each of the batch's p.shape[0] sequences.  The 2 x 48 gate rows
+        (plain fp16) are a cuBLAS GEMM for prompts and are computed inside the
+        block's first kernel for decode tokens."""
         cfg, T = self.cfg, p.shape[0]
         nk, nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
         lib = _lib.load()
+        if decode:
+            out = torch.empty(T, nv * cfg.linear_value_head_dim, dtype=torch.float16, device=self.dev)
+            _lib.check(lib.gsq_gdn_batch(p.data_ptr(), p.stride(0), None, 0, h.data_ptr(), h.stride(0),
+                                         L["ab"].data_ptr(), cfg.hidden_size, T, nk, nv, L["conv_state"].data_ptr(),
+                                         self.pos.data_ptr(), L["conv_w"].data_ptr(), L["A"].data_ptr(),
+                                         L["dt_bias"].data_ptr(), L["norm"].data_ptr(), self.eps,
+                                         L["state"].data_ptr(), out.data_ptr(), _lib.DTYPE_CODES[torch.float16],
+                                         _stream(self.dev)))
+            return out
         need = lib.gsq_gdn_scratch_bytes(T, nk, nv)
         scratch = torch.empty(need, dtype=torch.uint8, device=self.dev) if need else None
         out = torch.empty(T, nv * cfg.linear_value_head_dim, dtype=torch.float16, device=self.dev)
@@ -433,8 +472,8 @@ class Qwen35:
         k = F.rms_norm(k, (hd,), L["k_norm"], self.eps)
         pos = torch.arange(pos0, pos0 + T, device=self.dev)
         q, k = self._rope(q, pos), self._rope(k, pos)
-        L["k_cache"][pos0:pos0 + T] = k
-        L["v_cache"][pos0:pos0 + T] = v
+        L["k_cache"][0, pos0:pos0 + T] = k
+        L["v_cache"][0, pos0:pos0 + T] = v
         att = F.scaled_dot_product_attention(q.transpose(0, 1)[None].to(torch.float16),
                                              k.transpose(0, 1)[None].to(torch.float16),
                                              v.transpose(0, 1)[None].to(torch.float16), is_causal=True,
@@ -443,14 +482,16 @@ class Qwen35:
         return o.reshape(T, nq * hd).to(torch.float16)
 
     def _attn_decode(self, L, p: torch.Tensor) -> torch.Tensor:
-        cfg = self.cfg
+        """One decode token of each of the batch's p.shape[0] sequences."""
+        cfg, B = self.cfg, p.shape[0]
         nq, nkv, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
-        out = torch.empty(1, nq * hd, dtype=torch.float16, device=self.dev)
-        _lib.check(_lib.load().gsq_attn_decode(p.data_ptr(), nq, nkv, L["q_norm"].data_ptr(),
-                                               L["k_norm"].data_ptr(), self.eps, cfg.rotary_dim, cfg.rope_theta,
-                                               L["k_cache"].data_ptr(), L["v_cache"].data_ptr(), self.max_len,
-                                               self.pos.data_ptr(), out.data_ptr(),
-                                               _lib.DTYPE_CODES[torch.float16], _stream(self.dev)))
+        out = torch.empty(B, nq * hd, dtype=torch.float16, device=self.dev)
+        _lib.check(_lib.load().gsq_attn_decode_batch(p.data_ptr(), nq, nkv, L["q_norm"].data_ptr(),
+                                                     L["k_norm"].data_ptr(), self.eps, cfg.rotary_dim,
+                                                     cfg.rope_theta, L["k_cache"].data_ptr(),
+                                                     L["v_cache"].data_ptr(), self.max_len, self.pos.data_ptr(),
+                                                     out.data_ptr(), _lib.DTYPE_CODES[torch.float16], B,
+                                                     _stream(self.dev)))
         return out
 
     def _layers(self, x: torch.Tensor, pos0: int | None) -> torch.Tensor:
@@ -462,7 +503,7 @@ class Qwen35:
             h = rmsnorm(x, delta, L["attn_norm"], self.eps)
             if L["linear"]:
                 p = L["qkvz"](h)
-                d = L["out"](self._gdn(L, p, h))
+                d = L["out"](self._gdn(L, p, h, decode=pos0 is None))
             else:
                 p = L["qkv"](h)
                 o = self._attn_decode(L, p) if pos0 is None else self._attn_prefill(L, p, pos0)
@@ -487,31 +528,39 @@ class Qwen35:
         last = x[T - 1:].clone()
         hf = rmsnorm(last, delta[T - 1:].contiguous(), self.out_norm, self.eps)
         logits = self.lm_head(hf)[0]
-        self.cur_id.copy_(torch.argmax(logits).to(torch.int32).reshape(1))
+        self.cur_id[:1].copy_(torch.argmax(logits).to(torch.int32).reshape(1))
         self.pos.fill_(T)
         self.n_pos = T
         return logits
 
     def _decode_body(self) -> torch.Tensor:
-        cfg = self.cfg
-        x = packed_embedding(self.cur_id, self.embed.data, qtype=self.embed.quantization_type,
+        cfg, B = self.cfg, self.batch
+        ids = self.cur_id[:B]
+        x = packed_embedding(ids, self.embed.data, qtype=self.embed.quantization_type,
                              vocab_size=cfg.vocab_size, dimensions=cfg.hidden_size, dtype=torch.float32)
-        x = x.reshape(1, cfg.hidden_size)
+        x = x.reshape(B, cfg.hidden_size)
         delta = self._layers(x, None)
         hf = rmsnorm(x, delta, self.out_norm, self.eps)
         logits = self.lm_head(hf)
-        self.cur_id.copy_(torch.argmax(logits, dim=-1).to(torch.int32))
+        ids.copy_(torch.argmax(logits, dim=-1).to(torch.int32))
         self.pos.add_(1)
         return logits
 
-    def decode_step(self, token: int | None = None) -> torch.Tensor:
-        """One decode token, eagerly: feeds ``token`` (default: the argmax of
-        the previous step) at the current position; returns the logits
-        (1 x vocab, fp32)."""
+    def decode_step(self, token=None) -> torch.Tensor:
+        """One decode step, eagerly: feeds ``token`` (an int for every
+        sequence, or one int per sequence of the batch; default: the argmax
+        of the previous step) at the current position; returns the logits
+        (batch x vocab, fp32)."""
         if self.n_pos >= self.max_len:
             raise ValueError("cache full")
         if token is not None:
-            self.cur_id.fill_(int(token))
+            if isinstance(token, int):
+                self.cur_id[:self.batch].fill_(int(token))
+            else:
+                t = torch.as_tensor(token, dtype=torch.int32).reshape(-1)
+                if t.numel() != self.batch:
+                    raise ValueError(f"expected {self.batch} tokens")
+                self.cur_id[:self.batch].copy_(t.to(self.dev))
         logits = self._decode_body()
         self.n_pos += 1
         return logits
@@ -522,7 +571,8 @@ class Qwen35:
         st = torch.cuda.Stream(device=self.dev)
         st.wait_stream(torch.cuda.current_stream(self.dev))
         g = torch.cuda.CUDAGraph()
-        saved = [(L["conv_state"].clone(), L["state"].clone()) for L in self.layers if L["linear"]]
+        B = self.batch
+        saved = [(L["conv_state"][:B].clone(), L["state"][:B].clone()) for L in self.layers if L["linear"]]
         pos, cur = self.pos.clone(), self.cur_id.clone()
         with torch.cuda.stream(st):
             with torch.cuda.graph(g, stream=st):
@@ -533,8 +583,8 @@ class Qwen35:
         for L in self.layers:
             if L["linear"]:
                 cs, s = next(it)
-                L["conv_state"].copy_(cs)
-                L["state"].copy_(s)
+                L["conv_state"][:B].copy_(cs)
+                L["state"][:B].copy_(s)
         self.pos.copy_(pos)
         self.cur_id.copy_(cur)
         self._graph = g
@@ -549,14 +599,19 @@ class Qwen35:
             self._graph.replay()
         self.n_pos += n
 
+    def release_graph(self) -> None:
+        """Drops the captured decode graph (and the memory it holds)."""
+        self._graph = None
+
     @property
     def graph_logits(self) -> torch.Tensor:
         return self._graph_logits
 
 
 def build_qwen35(weights: dict, cfg: Qwen35Config | None = None, device="cuda", max_len: int = 2304,
-                 group=None) -> Qwen35:
+                 group=None, max_batch: int = 1) -> Qwen35:
     """The model from GGUF-named weights (``qwen35.py:104-152``): packed
     projections as ``PackedWeight`` on the device, plain tensors as arrays;
-    ``group``: split every packed projection over the group's ranks."""
-    return Qwen35(weights, cfg or Qwen35Config(), device, max_len=max_len, group=group)
+    ``group``: split every packed projection over the group's ranks;
+    ``max_batch``: sequences a batched decode can hold (``fork``)."""
+    return Qwen35(weights, cfg or Qwen35Config(), device, max_len=max_len, group=group, max_batch=max_batch)

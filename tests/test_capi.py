@@ -117,3 +117,29 @@ def test_gather_entry_points_validate_before_any_launch():
     assert lib.gsq_ipc_export(None, ctypes.create_string_buffer(64)) == _lib.GSQ_ERR_ARG
     assert lib.gsq_ipc_import(None, ctypes.byref(p)) == _lib.GSQ_ERR_ARG
     assert lib.gsq_ipc_close(None) == _lib.GSQ_OK
+
+
+def test_batched_decode_entry_points_validate_before_any_launch():
+    """gsq_gdn_batch / gsq_attn_decode_batch: a batch of 0 sequences is a
+    no-op, negative or oversized batches and bad shapes are rejected with
+    status codes before touching the GPU."""
+    lib = _lib.load()
+    fake = ctypes.c_void_p(1 << 20)
+
+    def gdn_batch(batch, nk=2, nv=6, proj_stride=2048):
+        return lib.gsq_gdn_batch(fake, proj_stride, fake, 12, None, 0, None, 0, batch, nk, nv, fake, fake, fake, fake,
+                                 fake, fake, 1e-6, fake, fake, 0, None)
+
+    assert gdn_batch(0) == _lib.GSQ_OK
+    assert gdn_batch(-1) == _lib.GSQ_ERR_SIZE
+    assert gdn_batch(70000) == _lib.GSQ_ERR_SIZE
+    assert gdn_batch(4, nv=5) == _lib.GSQ_ERR_SIZE           # value heads not a multiple of key heads
+    assert gdn_batch(4, proj_stride=100) == _lib.GSQ_ERR_SIZE  # row shorter than q|k|v|z
+
+    def attn_batch(batch, nkv=4):
+        return lib.gsq_attn_decode_batch(fake, 24, nkv, fake, fake, 1e-6, 64, 1e7, fake, fake, 256, fake, fake, 1,
+                                         batch, None)
+
+    assert attn_batch(0) == _lib.GSQ_OK
+    assert attn_batch(-3) == _lib.GSQ_ERR_SIZE
+    assert attn_batch(2, nkv=5) == _lib.GSQ_ERR_SIZE

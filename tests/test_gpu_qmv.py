@@ -95,8 +95,8 @@ def _outlier_activations(k: int, seed: int) -> torch.Tensor:
     g = torch.Generator().manual_seed(seed)
     x = torch.randn(k // 32, 32, generator=g, dtype=torch.float64)
     ch = torch.randint(0, 32, (k // 32,), generator=g)
-    sign = torch.where(torch.rand(k // 32, generator=g) < 0.5, -1.0, 1.0)
-    x[torch.arange(k // 32), ch] = sign * 1000.0 * (1.0 + torch.rand(k // 32, generator=g))
+    sign = torch.where(torch.rand(k // 32, generator=g, dtype=torch.float64) < 0.5, -1.0, 1.0)
+    x[torch.arange(k // 32), ch] = sign * 1000.0 * (1.0 + torch.rand(k // 32, generator=g, dtype=torch.float64))
     tiny = torch.randperm(k // 32, generator=g)[:8]
     x[tiny] = torch.randn(8, 32, generator=g, dtype=torch.float64) * 1e-3
     x[int(torch.randperm(k // 32, generator=g)[0])] = 0.0

@@ -169,8 +169,21 @@ def _model_worker(rank, world, port, q):
             one.replay_decode(1)
             ok = ok and rel(tp.graph_logits, one.graph_logits) <= 1e-3
             ok = ok and int(tp.cur_id.item()) == int(one.cur_id.item())
+        # batched decode (9 sequences: the projections run the matmul with
+        # the gather fused into its epilogue; the LM head an NCCL all-gather)
+        tp.release_graph()
+        one.release_graph()
+        tpb = build_qwen35(w, cfg, dev, max_len=64, max_batch=9, group=dist.group.WORLD)
+        oneb = build_qwen35(w, cfg, dev, max_len=64, max_batch=9)
+        toks = [(13 * b + 3) % cfg.vocab_size for b in range(9)]
+        for m in (tpb, oneb):
+            m.prefill(prompt)
+            m.fork(9)
+        ok = ok and rel(tpb.decode_step(toks), oneb.decode_step(toks)) <= 1e-3
+        ok = ok and rel(tpb.decode_step(toks), oneb.decode_step(toks)) <= 1e-3
         torch.cuda.synchronize()
         ok = ok and _lib.load().gsq_device_status(None) == 0
+        tpb.close()
         tp.close()
         q.put((rank, ok))
     finally:
