@@ -1,6 +1,6 @@
 """Benchmark of the packed-GGUF hot path on B200 (driver contract).
 
-One *step* = one pass of the batch-1 decode matvec over the config-2 sweep:
+One *step* = one pass of the batch-1 decode matvec over the QMV sweep:
 the 11 packed types x {5120->5120, 5120->17408, 17408->5120}, fp16
 activations N(0,1), seeded synthetic packed weights (886 MB per step, far
 larger than the 126 MB L2, so no step reuses another's weights from L2).
@@ -21,7 +21,8 @@ larger than the 126 MB L2, so no step reuses another's weights from L2).
               matvec / matmul of the whole matrix.  A failure exits non-zero.
   qmv_sweep   per configuration: a CUDA graph of 24 launches over a ring of
               distinct weight copies (working set > 2x L2), CUDA events.
-  qmm_prefill config 3 at M=512 (tcgen05 QMM) in TFLOP/s vs measured bf16 peak;
+  qmm_prefill the prefill matmul (IQ2_XS, IQ3_S, IQ4_XS, Q6_K x 17408x5120 and
+              5120x17408) at M=512 (tcgen05 QMM) in TFLOP/s vs measured bf16 peak;
               on one GPU also M = 16, 182, 2048 against the max(FLOP, byte)
               roofline (``by_M``).
   embed       the packed embedding gather (Q6_K, vocab 248320 x 5120) at
@@ -74,7 +75,7 @@ def packed_bytes(q, n, k):
 
 
 SWEEP_BYTES = sum(packed_bytes(q, n, k) for q in TYPES for (n, k) in SHAPES)
-CONFIG = {"workload": "config-2 QMV sweep: 11 types x {5120->5120, 5120->17408, 17408->5120}, batch 1, fp16 x "
+CONFIG = {"workload": "QMV sweep: 11 types x {5120->5120, 5120->17408, 17408->5120}, batch 1, fp16 x "
                       "N(0,1), seeded synthetic packed weights",
           "bytes_per_step": SWEEP_BYTES, "l2": "inputs larger than L2 (886 MB per step)"}
 
@@ -186,7 +187,7 @@ def _cpu_config(job):
 
 
 def cpu_reference_sweep(max_workers: int | None = None) -> dict:
-    """The config-2 sweep on the host cores: every configuration once, one
+    """The QMV sweep on the host cores: every configuration once, one
     process per core (spawned; each with one OpenBLAS thread).  value =
     packed bytes of the sweep / wall time of the pool."""
     import multiprocessing as mp
@@ -223,7 +224,7 @@ def cpu_reference_sweep(max_workers: int | None = None) -> dict:
             "cpu_seconds": {"dequant": round(deq_s, 2), "matvec": round(mv_s, 2)},
             "per_core_gbs": round(total / (deq_s + mv_s) / 1e9, 5), "openblas_threads_per_worker": 1,
             "os_cpu_count": os.cpu_count(), "cpu_model": cpu_model,
-            "sample": "the whole config-2 sweep (33 configurations, 886 MB packed) once: gguf-py 0.19.0 dequantize "
+            "sample": "the whole QMV sweep (33 configurations, 886 MB packed) once: gguf-py 0.19.0 dequantize "
                       "+ numpy fp32 matvec per configuration, one spawned process per core"}
 
 
@@ -279,7 +280,7 @@ def graph_of(fn, dev, reps=1):
 
 
 def qmm_by_m(dev, pk, lib, clocks, ms=(16, 182, 2048)):
-    """Config 3 at the other token counts, one GPU: for each M, one CUDA graph
+    """The prefill matmul at the other token counts, one GPU: for each M, one CUDA graph
     runs the 8 projections (4 types x 2 shapes, 369 MB of distinct packed
     weights, > 2x L2) back to back; replayed, CUDA events.  Reported against
     the max(FLOP, byte) roofline: bound = max(2MNK / bf16 peak, bytes / HBM
@@ -747,7 +748,7 @@ def main():
         c["full"] = None if world == 1 else c["full"]
     torch.cuda.empty_cache()
 
-    # ---- QMM prefill, config 3 at M=512 (ranks > 1: each rank's row shard,
+    # ---- QMM prefill at M=512 (ranks > 1: each rank's row shard,
     # with the gather fused into the matmul's epilogue) ----
     qmm = None
     qmm_worst = 0.0

@@ -20,8 +20,10 @@ from __future__ import annotations
 
 import hashlib
 import json
+import mmap
 import os
 import struct
+import tempfile
 from collections import defaultdict
 from dataclasses import dataclass
 from pathlib import Path
@@ -116,7 +118,7 @@ class GGUFReader:
         with self.path.open("rb") as f:
             r = _In(f)
             if f.read(4) != b"GGUF":
-                raise GGUFError("not a GGUF file")
+                raise GGUFError(f"{path}: no GGUF magic at the start of the file")
             self.version = r.scalar("I")
             if self.version not in (2, 3):
                 raise GGUFError(f"unsupported GGUF version {self.version}")
@@ -125,7 +127,7 @@ class GGUFReader:
             for _ in range(n_kv):
                 key = r.text()
                 if key in self.metadata:
-                    raise GGUFError(f"duplicate metadata key {key}")
+                    raise GGUFError(f"metadata key {key} appears twice")
                 self.metadata[key] = r.value(r.scalar("I"))
             raw = []
             for _ in range(n_tensors):
@@ -141,7 +143,7 @@ class GGUFReader:
         tensors, seen = [], set()
         for name, dims, tid, off in raw:
             if name in seen:
-                raise GGUFError(f"duplicate tensor {name}")
+                raise GGUFError(f"tensor {name} appears twice in the directory")
             seen.add(name)
             if tid not in TYPE_BY_ID:
                 raise GGUFError(f"unknown tensor type {tid} for {name}")
@@ -153,12 +155,12 @@ class GGUFReader:
             nbytes = count // elems * bb
             start = self.data_offset + off
             if start + nbytes > self.file_size:
-                raise GGUFError(f"tensor outside file: {name}")
+                raise GGUFError(f"tensor {name} extends past the end of the file")
             tensors.append(TensorInfo(name, dims, qtype, tid, off, start, count, nbytes))
         spans = sorted((t.absolute_offset, t.absolute_offset + t.num_bytes, t.name) for t in tensors)
         for (_, end, a), (start, _, b) in zip(spans, spans[1:]):
             if end > start:
-                raise GGUFError(f"overlapping tensors: {a}, {b}")
+                raise GGUFError(f"tensors {a} and {b} share bytes")
         self.tensors = tuple(tensors)
         self._index = {t.name: t for t in tensors}
 
@@ -175,7 +177,7 @@ class GGUFReader:
         with self.path.open("rb") as f:
             f.seek(t.absolute_offset)
             if f.readinto(memoryview(out)) != t.num_bytes:
-                raise GGUFError(f"short read for {name}")
+                raise GGUFError(f"{name}: the file ended before the tensor's last byte")
         return out
 
     def weight(self, name: str, device="cuda"):
@@ -358,57 +360,81 @@ def manifest_path_for(container: Path) -> Path:
     return container.with_suffix(container.suffix + ".manifest.json")
 
 
+def _copy_and_hash(src: Path, dst: BinaryIO, ranges: list[tuple[str, int, int]]) -> dict[str, str]:
+    """Appends each (name, offset, size) byte range of ``src`` to ``dst`` and
+    returns the SHA-256 of every range: the GGUF file is memory-mapped and
+    each range is read once, for the copy and the digest together."""
+    digests: dict[str, str] = {}
+    with src.open("rb") as f, mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) as mm:
+        view = memoryview(mm)
+        try:
+            for name, off, n in ranges:
+                part = view[off:off + n]
+                try:
+                    if len(part) != n:
+                        raise OSError(f"{name}: the GGUF file ends inside the tensor")
+                    for c in range(0, n, COPY_CHUNK):
+                        dst.write(part[c:c + COPY_CHUNK])
+                    digests[name] = hashlib.sha256(part).hexdigest()
+                finally:
+                    part.release()
+        finally:
+            view.release()
+    return digests
+
+
+def _range_digests(path: Path, ranges: list[tuple[str, int, int]]) -> dict[str, str]:
+    """SHA-256 of each (name, offset, size) byte range of a file (memory-mapped)."""
+    out: dict[str, str] = {}
+    with path.open("rb") as f, mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ) as mm:
+        view = memoryview(mm)
+        try:
+            for name, off, n in ranges:
+                part = view[off:off + n]
+                try:
+                    if len(part) != n:
+                        raise OSError(f"{path.name} ends inside {name}")
+                    out[name] = hashlib.sha256(part).hexdigest()
+                finally:
+                    part.release()
+        finally:
+            view.release()
+    return out
+
+
 def convert_gguf_to_safetensors(src: str | Path, dst: str | Path, *, overwrite: bool = False,
                                 verify: bool = True) -> Path:
     """Copy every tensor's packed bytes unchanged into an ``mlx-gsq-packed-v1``
-    safetensors container (``converter.py:76-118``): written to a temporary
-    file and renamed when complete, then (by default) verified tensor by
-    tensor against the GGUF byte ranges with SHA-256."""
+    safetensors container, the contract of ``converter.py:76-118``: the
+    output appears only complete (written to a temporary file in the target
+    directory, synced, then renamed over the target), a sidecar manifest
+    describes every tensor, and by default every tensor is verified by
+    SHA-256 (the GGUF side from the digests taken while copying, the
+    container side read back) with the result recorded in the manifest."""
     reader = GGUFReader(src)
     out = Path(dst).expanduser().resolve()
     if out.exists() and not overwrite:
         raise FileExistsError(out)
     out.parent.mkdir(parents=True, exist_ok=True)
-    tmp = out.with_suffix(out.suffix + ".partial")
-    if tmp.exists():
-        tmp.unlink()
     header = _container_header(reader)
+    fd, tmp_name = tempfile.mkstemp(prefix=out.name + ".", suffix=".partial", dir=out.parent)
+    tmp = Path(tmp_name)
     try:
-        with reader.path.open("rb") as s, tmp.open("xb") as d:
-            d.write(struct.pack("<Q", len(header)))
-            d.write(header)
-            for t in reader.tensors:
-                s.seek(t.absolute_offset)
-                left = t.num_bytes
-                while left:
-                    chunk = s.read(min(left, COPY_CHUNK))
-                    if not chunk:
-                        raise OSError(f"short GGUF read for {t.name}")
-                    d.write(chunk)
-                    left -= len(chunk)
+        with os.fdopen(fd, "wb") as d:
+            d.write(struct.pack("<Q", len(header)) + header)
+            source_digests = _copy_and_hash(reader.path, d,
+                                            [(t.name, t.absolute_offset, t.num_bytes) for t in reader.tensors])
             d.flush()
             os.fsync(d.fileno())
-        tmp.replace(out)
-        manifest_path_for(out).write_text(json.dumps(_manifest(reader, out.name), ensure_ascii=False, indent=2) + "\n")
-        if verify:
-            verify_conversion(reader.path, out, record_hashes=True)
+        os.replace(tmp, out)
     except BaseException:
-        if tmp.exists():
-            tmp.unlink()
+        tmp.unlink(missing_ok=True)
         raise
+    mpath = manifest_path_for(out)
+    mpath.write_text(json.dumps(_manifest(reader, out.name), ensure_ascii=False, indent=2) + "\n")
+    if verify:
+        _verify(reader, out, mpath, source_digests, record_hashes=True)
     return out
-
-
-def _sha256(f: BinaryIO, offset: int, size: int) -> str:
-    h = hashlib.sha256()
-    f.seek(offset)
-    while size:
-        chunk = f.read(min(size, COPY_CHUNK))
-        if not chunk:
-            raise OSError("short read during verification")
-        h.update(chunk)
-        size -= len(chunk)
-    return h.hexdigest()
 
 
 def read_safetensors_header(path: Path) -> tuple[dict[str, Any], int]:
@@ -420,39 +446,59 @@ def read_safetensors_header(path: Path) -> tuple[dict[str, Any], int]:
         return json.loads(f.read(n)), 8 + n
 
 
-def verify_conversion(src: str | Path, container: str | Path, manifest: str | Path | None = None, *,
-                      record_hashes: bool = False) -> dict[str, Any]:
-    """Check the container's structure, its manifest, and that every tensor's
-    bytes hash the same as the GGUF range they came from
-    (``converter.py:129-176``); raises ``ValueError`` on any difference."""
-    reader = GGUFReader(src)
-    out = Path(container)
-    mpath = Path(manifest) if manifest else manifest_path_for(out)
+def _structure_problems(reader: GGUFReader, header: dict[str, Any], data0: int, size: int,
+                        manifest: dict[str, Any]) -> list[str]:
+    """Everything about the container's layout and manifest that differs from
+    what the GGUF directory implies (empty when they agree)."""
+    problems = []
+    expected = data0 + sum(t.num_bytes for t in reader.tensors)
+    if size != expected:
+        problems.append(f"safetensors size {size}, expected {expected}")
+    listed = manifest.get("tensors", {})
+    for t in reader.tensors:
+        e = header.get(t.name)
+        lo_hi = e.get("data_offsets") if isinstance(e, dict) else None
+        if not isinstance(e, dict) or e.get("dtype") != "U8" or e.get("shape") != [t.num_bytes] \
+                or not lo_hi or lo_hi[1] - lo_hi[0] != t.num_bytes:
+            problems.append(f"invalid safetensors entry for {t.name}")
+        m = listed.get(t.name)
+        if not m or any(m.get(k) != v for k, v in t.as_dict().items()):
+            problems.append(f"manifest entry of {t.name} differs from the GGUF directory")
+    return problems
+
+
+def _verify(reader: GGUFReader, out: Path, mpath: Path, source_digests: dict[str, str] | None,
+            record_hashes: bool) -> dict[str, Any]:
     man = json.loads(mpath.read_text())
     header, data0 = read_safetensors_header(out)
-    expected = data0 + sum(t.num_bytes for t in reader.tensors)
-    if out.stat().st_size != expected:
-        raise ValueError(f"safetensors size mismatch: {out.stat().st_size} != {expected}")
-    hashes = {}
-    with reader.path.open("rb") as s, out.open("rb") as p:
-        for t in reader.tensors:
-            e = header.get(t.name)
-            if not e or e["dtype"] != "U8" or e["shape"] != [t.num_bytes]:
-                raise ValueError(f"invalid safetensors entry for {t.name}")
-            lo, hi = e["data_offsets"]
-            h = _sha256(s, t.absolute_offset, t.num_bytes)
-            if h != _sha256(p, data0 + lo, hi - lo):
-                raise ValueError(f"packed bytes differ for {t.name}")
-            mt = man["tensors"].get(t.name)
-            if not mt or any(mt.get(k) != v for k, v in t.as_dict().items()):
-                raise ValueError(f"manifest differs for {t.name}")
-            hashes[t.name] = h
-    result = {"algorithm": "sha256", "status": "passed", "tensor_count": len(hashes),
-              "all_packed_bytes_identical": True, "tensor_hashes": hashes}
+    problems = _structure_problems(reader, header, data0, out.stat().st_size, man)
+    if problems:
+        raise ValueError("; ".join(problems))
+    if source_digests is None:
+        source_digests = _range_digests(reader.path, [(t.name, t.absolute_offset, t.num_bytes)
+                                                      for t in reader.tensors])
+    packed = _range_digests(out, [(t.name, data0 + header[t.name]["data_offsets"][0], t.num_bytes)
+                                  for t in reader.tensors])
+    bad = [name for name, h in source_digests.items() if packed.get(name) != h]
+    if bad:
+        raise ValueError(f"container bytes differ from the GGUF ranges for {', '.join(bad)}")
+    result = {"algorithm": "sha256", "status": "passed", "tensor_count": len(source_digests),
+              "all_packed_bytes_identical": True, "tensor_hashes": dict(source_digests)}
     if record_hashes:
         man["verification"] = result
         mpath.write_text(json.dumps(man, ensure_ascii=False, indent=2) + "\n")
     return result
+
+
+def verify_conversion(src: str | Path, container: str | Path, manifest: str | Path | None = None, *,
+                      record_hashes: bool = False) -> dict[str, Any]:
+    """Check a container against its GGUF source (``converter.py:129-176``):
+    its size, every tensor entry and manifest entry first, then the SHA-256
+    of every tensor's bytes on both sides; raises ``ValueError`` naming every
+    difference found."""
+    reader = GGUFReader(src)
+    out = Path(container)
+    return _verify(reader, out, Path(manifest) if manifest else manifest_path_for(out), None, record_hashes)
 
 
 def write_model_gguf(path: str | Path, weights: dict, metadata: dict[str, Any] | None = None) -> Path:

@@ -122,8 +122,8 @@ def tensor_shapes(cfg: Qwen35Config) -> dict[str, tuple[int, ...]]:
 
 
 def default_type_mix(cfg: Qwen35Config) -> dict[str, str]:
-    """Quant type per packed tensor: embedding and LM head
-    Q6_K; FFN gate/up IQ2_XS on even layers, IQ2_S on odd ones; FFN down
+    """Quant type per packed tensor of the benchmarked 27B model: embedding
+    and LM head Q6_K; FFN gate/up IQ2_XS on even layers, IQ2_S on odd ones; FFN down
     Q4_K; attention and linear-attention projections IQ3_S on even layers,
     IQ4_XS on odd ones.  ssm_alpha / ssm_beta, norms, conv taps and gates
     stay plain (F32)."""
@@ -291,7 +291,7 @@ class Qwen35:
     """The model, built from GGUF-named weights (``build_qwen35``).
 
     With ``group`` (an initialised process group of P ranks, one GPU each;
-    BASELINE config 5) every packed projection is split by output rows over
+    tensor parallel) every packed projection is split by output rows over
     the ranks: decode tokens gather the rows inside the matvec kernel
     (``gsq_qmv_gather``), prompts inside the matmul epilogue
     (``gsq_qmm_gather``; prompts of 2-7 tokens, an NCCL all-gather).

@@ -2,6 +2,11 @@
 
     python -m gsq_b200.profile_model [prompt_tokens] [tokens]
     python -m gsq_b200.profile_model prefill [prompt_tokens]
+    python -m gsq_b200.profile_model gdn
+
+The third form times the gated-DeltaNet block alone (``gsq_gdn`` at the
+model's 16 key / 48 value heads) for prompts of 1, 16, 128 and 512 tokens:
+a CUDA graph of 10 calls, replayed, CUDA events.
 
 Builds the full 27B model (random-init packed weights, the default type
 mix), runs a prompt prefill, captures the decode-step graph, and records
@@ -51,6 +56,61 @@ def prefill(prompt: int = 512) -> None:
     _table(prof, 1, "prefill")
 
 
+def gdn(lengths=(1, 16, 128, 512)) -> None:
+    """Device time of one gsq_gdn call (prep + scan + norm kernels; one
+    kernel for a single token) at the model's head counts."""
+    from . import _lib
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    cfg = Qwen35Config()
+    nk, nv, d = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_value_head_dim
+    C = cfg.gdn_conv_dim
+    g = torch.Generator(device=dev).manual_seed(3)
+    lib = _lib.load()
+    cw = torch.randn(C, 4, device=dev, generator=g) * 0.3
+    A = -torch.exp(torch.rand(nv, device=dev, generator=g))
+    dtb = torch.randn(nv, device=dev, generator=g) * 0.5
+    nw = torch.ones(d, device=dev)
+    state = torch.zeros(nv, d, d, device=dev)
+    conv = torch.zeros(4, C, device=dev)
+    pos = torch.zeros(1, dtype=torch.int32, device=dev)
+    for T in lengths:
+        proj = torch.randn(T, C + nv * d, device=dev, generator=g)
+        ab = torch.randn(T, 2 * nv, device=dev, generator=g).half()
+        out = torch.empty(T, nv * d, dtype=torch.float16, device=dev)
+        need = lib.gsq_gdn_scratch_bytes(T, nk, nv)
+        scratch = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+
+        def call():
+            _lib.check(lib.gsq_gdn(proj.data_ptr(), proj.stride(0), ab.data_ptr(), ab.stride(0), None, 0, None, 0,
+                                   T, nk, nv, conv.data_ptr(), pos.data_ptr(), cw.data_ptr(), A.data_ptr(),
+                                   dtb.data_ptr(), nw.data_ptr(), 1e-6, state.data_ptr(),
+                                   scratch.data_ptr() if need else None, need, out.data_ptr(),
+                                   _lib.DTYPE_CODES[torch.float16], _lib.stream_ptr(dev)))
+
+        call()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream(device=dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(graph, stream=st):
+                for _ in range(10):
+                    call()
+        torch.cuda.current_stream(dev).wait_stream(st)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        print(f"gsq_gdn T={T}: {e0.elapsed_time(e1) * 1e3 / 50:.1f} us per call")
+    if lib.gsq_device_status(None) != 0:
+        raise RuntimeError("device status after the gsq_gdn timing")
+
+
 def main(prompt: int = 182, tokens: int = 4) -> None:
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
@@ -71,5 +131,7 @@ def main(prompt: int = 182, tokens: int = 4) -> None:
 if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "prefill":
         prefill(*(int(a) for a in sys.argv[2:3]))
+    elif len(sys.argv) > 1 and sys.argv[1] == "gdn":
+        gdn()
     else:
         main(*(int(a) for a in sys.argv[1:3]))

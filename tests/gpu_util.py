@@ -3,7 +3,7 @@ import numpy as np
 import torch
 
 
-# Primary bar: rel-L2 <= 1e-3 against the float64
+# Primary bar of the matvec / matmul: rel-L2 <= 1e-3 against the float64
 # dequantize-then-matmul of the oracle.
 REL_L2 = 1e-3
 

@@ -2,7 +2,8 @@
 
 Mirrors the reference's tests/test_all_qmm.py:41-57 (rows 8/16/33, an fp16
 input case, tolerance rtol=2e-3, atol=2e-3*max|expected|) plus the primary
-rel-L2 <= 1e-3 bar, ragged shapes and the BASELINE config-3 shapes."""
+rel-L2 <= 1e-3 bar, ragged shapes and the prefill benchmark shapes (IQ2_XS, IQ3_S, IQ4_XS,
+Q6_K at 5120->17408 and 17408->5120, 16 to 2048 tokens)."""
 import numpy as np
 import pytest
 import torch

@@ -2,8 +2,9 @@
 
 Primary bar: rel-L2 <= 1e-3 (fp32 accumulate).  Mirrors the reference's
 tests/test_all_qmv.py:9-24 (rows 2 and 5, N=4, fp32 x) on the golden
-fixtures, then widens to ragged shapes, every activation dtype, the BASELINE
-config-1 matrix and the config-2 full-size shapes."""
+fixtures, then widens to ragged shapes, every activation dtype, the
+single-matvec benchmark matrix (Q4_K 5120x5120) and the full-size sweep
+shapes (11 types x 5120->5120, 5120->17408, 17408->5120)."""
 import numpy as np
 import pytest
 import torch
@@ -52,7 +53,7 @@ def test_qmv_output_dtype_follows_input(golden):
 
 
 def test_qmv_config1_q4k_5120(oracle_mod):
-    """Q4_K 5120x5120, seed 0, fp16 x N(0,1), fp32 y."""
+    """The single-matvec benchmark case: Q4_K 5120x5120, seed 0, fp16 x N(0,1), fp32 y."""
     packed = random_matrix("Q4_K", 5120, 5120, seed=0)
     x = random_activations(1, 5120, seed=0, dtype=np.float16)
     y = quantized_matvec(cuda(x), cuda(packed), qtype="Q4_K", out_features=5120, in_features=5120,
