@@ -40,7 +40,7 @@ constexpr int QMM_THREADS = 32 * (QMM_DEC0 + QMM_DEC_WARPS);
 // Scratch: a fixed region of ticket counters (left zero-filled by every
 // call), then the partial tiles of split-K plans, then the fp16 activations.
 constexpr int QMM_TICKETS = 16384;
-constexpr int QMM_KSPLIT_MAX = 4;
+constexpr int QMM_KSPLIT_MAX = 8;
 constexpr size_t QMM_TICKET_BYTES = QMM_TICKETS * sizeof(unsigned);
 
 template <int T>
@@ -457,8 +457,13 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
       }
     } else {
       // Partial tile of this split -> scratch [tile][split][T][128] (rows
-      // contiguous: coalesced), then a ticket; the last split to arrive sums
-      // all splits in order.
+      // contiguous: coalesced).  The tile's ticket then counts the splits
+      // twice: the first ksplit arrivals say that every partial is written
+      // (each split waits, bounded, until all are: the plan keeps every
+      // split of a call resident at once), then every split sums its share
+      // of the tile's 8-column chunks over all splits, in split order
+      // (deterministic), and arrives again; the last of those arrivals
+      // resets the ticket to zero for the next call.
       float* mine = a.part + ((tile * a.ksplit + split) * ttok) * QMM_BM;
       if (ok) {
         for (int j0 = ehalf * cols; j0 < (ehalf + 1) * cols; j0 += 16) {
@@ -468,28 +473,43 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
           for (int jj = 0; jj < 16; jj++) mine[(int64_t)(j0 + jj) * QMM_BM + er] = __uint_as_float(vv[jj]);
         }
       }
+      unsigned* tk = a.tickets + tile;
       named_sync_decoders();
       if (warp == QMM_DEC0 && lane == 0) {
-        const unsigned prev = atom_add_acq_rel_gpu(a.tickets + tile, 1u);
-        *last_flag = (prev + 1u == (unsigned)a.ksplit) ? 1u : 0u;
-        if (prev + 1u == (unsigned)a.ksplit) a.tickets[tile] = 0u;
+        atom_add_acq_rel_gpu(tk, 1u);
+        bool all_in = true;
+        const long long t0 = clock64();
+        for (;;) {
+          unsigned v;
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(tk) : "memory");
+          if (v >= (unsigned)a.ksplit) break;
+          if (clock64() - t0 > (1ll << 31)) {
+            if (a.err) atomicExch(a.err, DEV_WAIT_TIMEOUT);
+            all_in = false;
+            break;
+          }
+          __nanosleep(64);
+        }
+        *last_flag = all_in ? 1u : 0u;
       }
       named_sync_decoders();
-      if (*last_flag && elive && ok) {
-        __threadfence();
-        // 16 columns x all splits (<= QMM_KSPLIT_MAX) of loads in flight per
-        // batch; sums in split order.
+      const bool reduce = ok && *last_flag != 0u;
+      if (reduce && elive) {
+        // This split's chunks of 8 columns in this warp's column half: 8
+        // columns x all splits (<= QMM_KSPLIT_MAX) of loads in flight.
         const float* base = a.part + (tile * a.ksplit * ttok) * QMM_BM;
-        for (int j0 = ehalf * cols; j0 < (ehalf + 1) * cols && m0 + j0 < a.M; j0 += 16) {
-          float v[QMM_KSPLIT_MAX][16];
+        for (int c = split; c < cols / 8; c += a.ksplit) {
+          const int j0 = ehalf * cols + 8 * c;
+          if (m0 + j0 >= a.M) break;
+          float v[QMM_KSPLIT_MAX][8];
 #pragma unroll
           for (int z = 0; z < QMM_KSPLIT_MAX; z++) {
 #pragma unroll
-            for (int jj = 0; jj < 16; jj++)
+            for (int jj = 0; jj < 8; jj++)
               v[z][jj] = z < a.ksplit ? __ldcg(base + ((int64_t)z * ttok + j0 + jj) * QMM_BM + er) : 0.f;
           }
 #pragma unroll
-          for (int jj = 0; jj < 16; jj++) {
+          for (int jj = 0; jj < 8; jj++) {
             float acc = v[0][jj];
 #pragma unroll
             for (int z = 1; z < QMM_KSPLIT_MAX; z++) acc += v[z][jj];  // zeros beyond ksplit
@@ -498,14 +518,24 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
           }
         }
       }
+      if constexpr (GATHER) {
+        if (reduce) __threadfence_system();  // this thread's stores into the peers' regions
+      }
+      named_sync_decoders();
+      if (warp == QMM_DEC0 && lane == 0) {
+        const unsigned prev = atom_add_acq_rel_gpu(tk, 1u);
+        const bool done = prev + 1u == 2u * (unsigned)a.ksplit;
+        if (done) *tk = 0u;
+        *last_flag = done && reduce ? 1u : 0u;  // the tile is complete: this split signals it
+      }
     }
   }
   if constexpr (GATHER) {
     if (warp >= QMM_DEC0) {
-      const bool stored = a.ksplit == 1 || *last_flag;
-      if (stored) __threadfence_system();  // this thread's stores into the peers' regions
+      if (a.ksplit == 1) __threadfence_system();  // this thread's stores into the peers' regions
       named_sync_decoders();
-      if (warp == QMM_DEC0 && lane == 0) qmm_gather_signal(a, stored);
+      const bool signal = a.ksplit == 1 || *last_flag;
+      if (warp == QMM_DEC0 && lane == 0) qmm_gather_signal(a, signal);
     }
   }
   tc_fence_before();
