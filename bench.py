@@ -684,42 +684,18 @@ def main():
                   c["rows"], c["k"], 1, dev_yb.data_ptr() + 4 * yo, _lib.DTYPE_CODES[torch.float32], wsp, wsn, stream)
                  for c, xo, yo in zip(cfgs, xoff, yoff)]
         qmv = lib.gsq_qmv
-        # The step's projections in four chunks: the activations of chunk
-        # i + 1 go up and the outputs of chunk i - 1 come down on a copy
-        # stream while chunk i's kernels run (events order each chunk's
-        # kernels after its copy in, and its copy out after its kernels).
-        main_st, copy_st = torch.cuda.current_stream(dev), torch.cuda.Stream(device=dev)
-        bounds = [round(i * len(cfgs) / 4) for i in range(5)]
-        chunks = []
-        for i in range(4):
-            a0, a1 = bounds[i], bounds[i + 1]
-            x_lo, x_hi = xoff[a0], (xoff[a1] if a1 < len(cfgs) else nx)
-            y_lo, y_hi = yoff[a0], (yoff[a1] if a1 < len(cfgs) else ny)
-            chunks.append((calls[a0:a1], (dev_xb[x_lo:x_hi], host_xb[x_lo:x_hi]),
-                           (host_yb[y_lo:y_hi], dev_yb[y_lo:y_hi]),
-                           torch.cuda.Event(), torch.cuda.Event()))
 
         def e2e_step():
-            copy_st.wait_stream(main_st)  # copies start after the timing event recorded on the main stream
-            for cs, (dx, hx), _, x_in, _ in chunks:
-                with torch.cuda.stream(copy_st):
-                    dx.copy_(hx, non_blocking=True)
-                    x_in.record(copy_st)
-            for cs, _, (hy, dy), x_in, y_done in chunks:
-                main_st.wait_event(x_in)
-                for args_ in cs:
-                    rc = qmv(*args_)
-                    if rc:
-                        _lib.check(rc)
-                y_done.record(main_st)
-                copy_st.wait_event(y_done)
-                with torch.cuda.stream(copy_st):
-                    hy.copy_(dy, non_blocking=True)
-            copy_st.synchronize()
-        e2e_path = ("activations of the step in one pinned host buffer -> copied to the device in four chunks on a "
-                    "copy stream, each chunk's gsq_qmv C-ABI calls (ctypes, device pointers prepared once) waiting "
-                    "for its chunk -> each chunk's outputs copied to pinned host memory as soon as its kernels are "
-                    "done; one synchronisation per step")
+            dev_xb.copy_(host_xb, non_blocking=True)
+            for args_ in calls:
+                rc = qmv(*args_)
+                if rc:
+                    _lib.check(rc)
+            host_yb.copy_(dev_yb, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        e2e_path = ("activations of the step in one pinned host buffer -> one copy to the device -> one gsq_qmv "
+                    "C-ABI call per projection (ctypes, device pointers prepared once) -> outputs in one copy to "
+                    "pinned host memory; one stream synchronisation per step")
     else:
         calls = [(type_id(c["q"]), dev_xb.data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16], c["packed"].data_ptr(),
                   c["rows"], c["k"], 1, c["region"].regions, world, rank, rank * c["rows"], c["n"], wsp, wsn, stream)
@@ -776,6 +752,7 @@ def main():
     # with the gather fused into the matmul's epilogue) ----
     qmm = None
     qmm_worst = 0.0
+    gather_path = None
     if not args.no_qmm:
         qres = []
         flops_total, t_qmm = 0.0, 0.0
@@ -821,6 +798,7 @@ def main():
                     tt = torch.tensor([t_ms], device=dev)
                     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
                     t_ms = float(tt.item())
+                    gather_path = "NVSwitch multicast stores" if region.mc else "peer stores to every rank"
                     region.close()
                 del g, full
                 fl = 2.0 * 512 * n * k
@@ -837,8 +815,8 @@ def main():
                "per_shape": qres,
                "note": "includes the bf16->fp16 activation pre-pass; weights decoded once per 128x128 tile; "
                        "CUDA graph of 8 launches, CUDA events" + (
-                           f"; {world} ranks: row shards, the gather fused into the matmul epilogue, max over ranks, "
-                           f"peak = {world} x the measured bf16 peak" if world > 1 else "")}
+                           f"; {world} ranks: row shards, the gather fused into the matmul epilogue ({gather_path}), "
+                           f"max over ranks, peak = {world} x the measured bf16 peak" if world > 1 else "")}
         if world > 1:
             t = torch.tensor([qmm_worst], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -159,6 +159,19 @@ GSQ_API int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t*
                            int64_t M, void* const* regions, int world, int rank, int64_t row0, int64_t ntot,
                            void* workspace, size_t workspace_bytes, gsq_stream_t stream);
 
+/* gsq_qmm_gather writing every output value once, through an NVSwitch
+ * multicast mapping of the ranks' regions (multimem stores: the switch
+ * delivers each value to every rank, this one included), instead of once per
+ * rank.  multicast_region maps all ranks' regions at the same byte offsets
+ * (e.g. torch symmetric memory's multicast_ptr for buffers holding the
+ * regions); regions[] are still each rank's unicast mapping (the tile counts
+ * go through them).  Same rules and bounded wait as gsq_qmm_gather.  No
+ * reference counterpart (the reference runs on one device). */
+GSQ_API int gsq_qmm_gather_mc(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
+                              int64_t M, void* const* regions, void* multicast_region, int world, int rank,
+                              int64_t row0, int64_t ntot, void* workspace, size_t workspace_bytes,
+                              gsq_stream_t stream);
+
 /* Synchronises `stream`, then returns and clears the device error word the
  * kernels of the current device write (0 = none; 1 = a bounded wait expired;
  * 2 = an embedding id was out of range).  On 1 it also synchronises the

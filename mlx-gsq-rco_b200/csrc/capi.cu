@@ -233,9 +233,11 @@ int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed,
   return e == cudaSuccess ? GSQ_OK : cuda_fail(e, "gsq_qmv_gather launch");
 }
 
-int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-                   void* const* regions, int world, int rank, int64_t row0, int64_t ntot, void* workspace,
-                   size_t workspace_bytes, gsq_stream_t stream) {
+}  // extern "C"
+
+static int qmm_gather_run(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
+                          int64_t M, void* const* regions, void* multicast, int world, int rank, int64_t row0,
+                          int64_t ntot, void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
   int rc = check_matrix(qtype, packed, N, K);
   if (rc) return rc;
   if (world < 2 || world > 8 || rank < 0 || rank >= world) return fail(GSQ_ERR_ARG, "world must be 2..8 and rank < world");
@@ -253,13 +255,31 @@ int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed,
   if (need > 0 && (!workspace || workspace_bytes < need || !aligned(workspace, 256)))
     return fail(GSQ_ERR_WORKSPACE, "gsq_qmm_gather needs %zu workspace bytes (256-byte aligned), got %zu", need,
                 workspace_bytes);
-  const QmmGather g = {regions, world, rank, row0, ntot};
+  if (multicast && !aligned(multicast, 256)) return fail(GSQ_ERR_ALIGN, "multicast region not 256-byte aligned");
+  const QmmGather g = {regions, world, rank, row0, ntot, multicast};
   float* own_y = reinterpret_cast<float*>(static_cast<uint8_t*>(regions[rank]) + 256);
   const char* why = "";
   cudaError_t e = qmm_launch(qtype, x, x_dtype, packed, N, K, M, own_y, workspace, device_error_word(),
                              (cudaStream_t)stream, &why, &g);
   if (e != cudaSuccess) return fail(GSQ_ERR_CUDA, "gsq_qmm_gather launch: %s (%s)", cudaGetErrorString(e), why);
   return GSQ_OK;
+}
+
+extern "C" {
+
+int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
+                   void* const* regions, int world, int rank, int64_t row0, int64_t ntot, void* workspace,
+                   size_t workspace_bytes, gsq_stream_t stream) {
+  return qmm_gather_run(qtype, x, x_dtype, packed, N, K, M, regions, nullptr, world, rank, row0, ntot, workspace,
+                        workspace_bytes, stream);
+}
+
+int gsq_qmm_gather_mc(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
+                      void* const* regions, void* multicast_region, int world, int rank, int64_t row0, int64_t ntot,
+                      void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
+  if (!multicast_region) return fail(GSQ_ERR_ARG, "null multicast region");
+  return qmm_gather_run(qtype, x, x_dtype, packed, N, K, M, regions, multicast_region, world, rank, row0, ntot,
+                        workspace, workspace_bytes, stream);
 }
 
 size_t gsq_qmm_workspace_size(int qtype, int64_t N, int64_t K, int64_t M, int x_dtype) {

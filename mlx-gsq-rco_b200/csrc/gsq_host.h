@@ -88,6 +88,7 @@ struct QmmGather {
   void* const* regions;
   int world, rank;
   int64_t row0, ntot;
+  void* multicast;  // NVSwitch multicast mapping of the regions, or nullptr
 };
 
 cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,

@@ -90,6 +90,7 @@ struct QmmArgs {
   // a 256-byte header whose word p counts the tiles rank p has delivered).
   float* gy[QMM_GATHER_MAX];
   unsigned* gflags[QMM_GATHER_MAX];
+  float* mcy;         // or: the fp32 output through the regions' NVSwitch multicast address
   int world, rank;
   int64_t row0, ntot;
 };
@@ -103,6 +104,12 @@ __device__ __forceinline__ void qmm_store(const QmmArgs& a, int64_t m, int64_t e
     return;
   }
   const int64_t off = m * a.ntot + a.row0 + erow;
+  if (a.mcy) {
+    // One store through the multicast address: the switch writes it into
+    // every rank's region (this rank's included).
+    asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(a.mcy + off), "f"(v) : "memory");
+    return;
+  }
 #pragma unroll
   for (int p = 0; p < QMM_GATHER_MAX; p++)
     if (p < a.world) a.gy[p][off] = v;
@@ -230,19 +237,13 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
   uint8_t* bstage = astage + (size_t)NS * QMM_BM * 128;       // NS x T*128
   uint8_t* pstage = bstage + (size_t)NS * bbytes;             // PST x PSTAGE
   uint8_t* tab = pstage + (size_t)PST * G::PSTAGE;            // decode tables
-  // The B (activation) part of a stage is one box per accumulator, each with
-  // its own full / empty barrier: the box of accumulator j is reloaded as
-  // soon as that accumulator's MMAs of the stage have completed, while the
-  // other accumulator's MMAs still run.  The A (weight) part is released when
-  // all of the stage's MMAs are done.
   uint64_t* bars = reinterpret_cast<uint64_t*>(tab + G::TAB);
-  uint64_t* full_a = bars;          // [NS]     count 8 (decoder warps)
-  uint64_t* full_b = bars + 4;      // [NS][2]  count 1 (TMA)
-  uint64_t* empty = bars + 12;      // [NS]     count 1 (tcgen05.commit): A part free
-  uint64_t* empty_b = bars + 16;    // [NS][2]  count 1 (tcgen05.commit): B box j free
-  uint64_t* accf = bars + 24;       // [1]      count 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 25);
-  unsigned* last_flag = reinterpret_cast<unsigned*>(bars + 26);
+  uint64_t* full_a = bars;          // [NS]  count 8 (decoder warps)
+  uint64_t* full_b = bars + 4;      // [NS]  count 1 (TMA)
+  uint64_t* empty = bars + 8;       // [NS]  count 1 (tcgen05.commit)
+  uint64_t* accf = bars + 20;       // [1]   count 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+  unsigned* last_flag = reinterpret_cast<unsigned*>(bars + 22);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n0 = (int64_t)blockIdx.x * QMM_BM;
@@ -256,11 +257,8 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; s++) {
       mbar_init(&full_a[s], QMM_DEC_WARPS);
+      mbar_init(&full_b[s], 1);
       mbar_init(&empty[s], 1);
-      for (int j = 0; j < 2; j++) {
-        mbar_init(&full_b[2 * s + j], 1);
-        mbar_init(&empty_b[2 * s + j], 1);
-      }
     }
     mbar_init(accf, 1);
     fence_mbar_init();
@@ -278,16 +276,15 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
     pdl_wait();  // the activations are written by the preceding kernel
     int s = 0, n = 0;  // stage and its use count, advanced without divisions
     for (int ks = 0; ks < nks && ok; ks++) {
-      for (int j = 0; j < nacc && ok; j++) {
-        if (n > 0) ok = mbar_wait_bounded(&empty_b[2 * s + j], (uint32_t)((n - 1) & 1), a.err);
-        if (!ok) break;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full_b[2 * s + j], (uint32_t)bn * 128u);
+      if (n > 0) ok = mbar_wait_bounded(&empty[s], (uint32_t)((n - 1) & 1), a.err);
+      if (!ok) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full_b[s], (uint32_t)bbytes);
+        for (int j = 0; j < nacc; j++)
           tma_load_2d(bstage + (size_t)s * bbytes + (size_t)j * bn * 128, &xmap, kb0 * QK + ks * QMM_BK, m0 + j * bn,
-                      &full_b[2 * s + j]);
-        }
-        __syncwarp();
+                      &full_b[s]);
       }
+      __syncwarp();
       if (++s == NS) { s = 0; n++; }
     }
   } else if (warp == 2) {
@@ -297,24 +294,21 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
     const uint32_t idesc = f16_idesc(bn);
     int s = 0, n = 0;
     for (int ks = 0; ks < nks && ok; ks++, (++s == NS ? (s = 0, n++) : 0)) {
-      ok = mbar_wait_bounded(&full_a[s], (uint32_t)(n & 1), a.err);
-      const uint32_t aaddr = smem_u32(astage + (size_t)s * QMM_BM * 128);
-      const uint32_t baddr = smem_u32(bstage + (size_t)s * bbytes);
-      for (int j = 0; j < nacc && ok; j++) {
-        ok = mbar_wait_bounded(&full_b[2 * s + j], (uint32_t)(n & 1), a.err);
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
+      ok = mbar_wait_bounded(&full_a[s], (uint32_t)(n & 1), a.err) &&
+           mbar_wait_bounded(&full_b[s], (uint32_t)(n & 1), a.err);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t aaddr = smem_u32(astage + (size_t)s * QMM_BM * 128);
+        const uint32_t baddr = smem_u32(bstage + (size_t)s * bbytes);
+        for (int j = 0; j < nacc; j++) {
 #pragma unroll
           for (int kk = 0; kk < QMM_BK / 16; kk++)
             tc_mma_f16(tmem_d + (uint32_t)(j * bn), sw128_desc(aaddr + kk * 32),
                        sw128_desc(baddr + (uint32_t)(j * bn * 128) + kk * 32), idesc, (ks | kk) != 0 ? 1u : 0u);
-          tc_commit(&empty_b[2 * s + j]);
         }
-        __syncwarp();
+        tc_commit(&empty[s]);
       }
-      if (!ok) break;
-      if (lane == 0) tc_commit(&empty[s]);
       __syncwarp();
     }
     if (lane == 0) tc_commit(accf);
@@ -687,6 +681,7 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
     a.gy[i] = nullptr;
     a.gflags[i] = nullptr;
   }
+  a.mcy = nullptr;
   if (gather && gather->world > 1) {
     if (gather->world > QMM_GATHER_MAX || gather->rank < 0 || gather->rank >= gather->world) {
       *why = "invalid gather world/rank";
@@ -701,6 +696,7 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
       a.gflags[i] = reinterpret_cast<unsigned*>(r);
       a.gy[i] = reinterpret_cast<float*>(r + 256);
     }
+    if (gather->multicast) a.mcy = reinterpret_cast<float*>(static_cast<uint8_t*>(gather->multicast) + 256);
   }
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};

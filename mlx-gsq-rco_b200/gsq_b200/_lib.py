@@ -47,6 +47,8 @@ SIGNATURES = {
     "gsq_ipc_close": (_I, [_P]),
     "gsq_qmv_gather": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _I, _I, _I64, _I64, _P, _SZ, _P]),
     "gsq_qmm_gather": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _I, _I, _I64, _I64, _P, _SZ, _P]),
+    "gsq_qmm_gather_mc": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _P, _I, _I, _I64, _I64, _P, _SZ,
+                               _P]),
     # include/gsq_model.h: decoder-glue kernels of the model harness
     "gsq_rmsnorm": (_I, [_P, _P, _I64, _I64, _P, ctypes.c_float, _P, _I, _P]),
     "gsq_silu_mul": (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),

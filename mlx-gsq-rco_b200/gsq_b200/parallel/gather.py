@@ -20,6 +20,7 @@ call site: its rows stay valid until the same site runs again.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 import torch.distributed as dist
@@ -43,7 +44,8 @@ class GatherRegion:
     region; ``gsq_qmv_gather`` fills all of it).
     """
 
-    def __init__(self, rows: int, ntot: int, group=None, device: torch.device | None = None):
+    def __init__(self, rows: int, ntot: int, group=None, device: torch.device | None = None,
+                 multicast: bool | None = None):
         if not dist.is_initialized():
             raise RuntimeError("GatherRegion needs an initialised process group")
         self.group = group
@@ -57,6 +59,13 @@ class GatherRegion:
         nbytes = lib.gsq_gather_region_bytes(self.rows, self.ntot)
         if nbytes == 0:
             raise ValueError("empty gather region")
+        self.mc = None       # NVSwitch multicast address of the regions (prefill regions), if any
+        self._symm = None
+        self._imported = []
+        if multicast is None:
+            multicast = self.rows >= 8 and os.environ.get("GSQ_MULTICAST", "1") != "0"
+        if multicast and self._symmetric(nbytes):
+            return
         with torch.cuda.device(self.device):
             own = ctypes.c_void_p()
             _lib.check(lib.gsq_gather_region_alloc(nbytes, ctypes.byref(own)))
@@ -77,12 +86,55 @@ class GatherRegion:
         self.regions = (ctypes.c_void_p * self.world)(*ptrs)
         self.y = torch.as_tensor(_DeviceArray(self._own + 256, (self.rows, self.ntot)), device=self.device)
 
+    def _symmetric(self, nbytes: int) -> bool:
+        """Regions in torch symmetric memory, mapped on every rank and, where
+        the GPUs share an NVSwitch multicast object, behind one multicast
+        address (``self.mc``) that the matmul's epilogue stores through once
+        per value.  Collective: every rank takes the same path (all ranks
+        must allocate, rendezvous and see a multicast address, or none uses
+        it).  Returns False (nothing kept) when symmetric memory is not
+        available on every rank."""
+        group = self.group if self.group is not None else dist.group.WORLD
+
+        def everyone(ok: bool) -> bool:
+            t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+            return bool(t.item())
+
+        buf = None
+        try:
+            import torch.distributed._symmetric_memory as symm
+            with torch.cuda.device(self.device):
+                buf = symm.empty(nbytes, dtype=torch.uint8, device=self.device)
+                buf.zero_()
+                torch.cuda.synchronize(self.device)
+        except Exception:
+            buf = None
+        if not everyone(buf is not None):
+            return False
+        hdl = symm.rendezvous(buf, group)
+        mc = int(getattr(hdl, "multicast_ptr", 0) or 0)
+        ptrs = [int(p) for p in hdl.buffer_ptrs]
+        if not everyone(mc != 0 and mc % 256 == 0 and all(p % 256 == 0 for p in ptrs)):
+            return False
+        dist.barrier(group=self.group)  # every rank's zero-filled region is in place
+        self._symm = (buf, hdl)
+        self.mc = mc
+        self._own = ptrs[self.rank]
+        self.regions = (ctypes.c_void_p * self.world)(*ptrs)
+        self.y = torch.as_tensor(_DeviceArray(self._own + 256, (self.rows, self.ntot)), device=self.device)
+        return True
+
     def close(self) -> None:
         """Unmap the peers' regions and free this rank's (collective: every rank calls it)."""
         if self._own is None:
             return
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)  # no peer still writes into this rank's region
+        if self._symm is not None:
+            self._symm, self.mc, self._own = None, None, None
+            dist.barrier(group=self.group)
+            return
         lib = _lib.load()
         with torch.cuda.device(self.device):
             for p in self._imported:
@@ -139,9 +191,14 @@ def quantized_matmul_gather(x: torch.Tensor, packed_shard: torch.Tensor, *, qtyp
     xcode = _lib.DTYPE_CODES[flat.dtype]
     need = lib.gsq_qmm_workspace_size(tid, out_features, in_features, rows, xcode)
     ws = _lib.workspaces.get(dev, need, "qmm")
-    code = lib.gsq_qmm_gather(tid, flat.data_ptr(), xcode, pk.data_ptr(), out_features, in_features, rows,
-                              region.regions, region.world, region.rank, row0, region.ntot,
-                              ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-                              _lib.stream_ptr(dev))
+    wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+    if region.mc:  # one multicast store per value through the NVSwitch
+        code = lib.gsq_qmm_gather_mc(tid, flat.data_ptr(), xcode, pk.data_ptr(), out_features, in_features, rows,
+                                     region.regions, region.mc, region.world, region.rank, row0, region.ntot, wsp, wsn,
+                                     _lib.stream_ptr(dev))
+    else:
+        code = lib.gsq_qmm_gather(tid, flat.data_ptr(), xcode, pk.data_ptr(), out_features, in_features, rows,
+                                  region.regions, region.world, region.rank, row0, region.ntot, wsp, wsn,
+                                  _lib.stream_ptr(dev))
     _lib.check(code)
     return region.y[:rows]

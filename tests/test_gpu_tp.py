@@ -91,19 +91,25 @@ def _worker(rank, world, port, q):
         # Tiled matmul with the gather fused into its epilogue (split-K and
         # whole-K shapes), repeated on one region.
         from gsq_b200.parallel import quantized_matmul_gather
-        for qtype, n2, k2 in (("IQ4_XS", 2048, 5120), ("Q6_K", 1024, 17408)):
-            packed2 = random_matrix_torch(qtype, n2, k2, seed=6, device=dev)
-            shard2 = shard_packed(packed2, qtype, n2, k2, world, rank)
-            region2 = GatherRegion(64, n2)
-            for it in range(3):
-                x2 = torch.randn(64, k2, device=dev, dtype=torch.bfloat16,
-                                 generator=torch.Generator(device=dev).manual_seed(10 + it))
-                ref2 = quantized_matmul(x2, packed2, qtype=qtype, out_features=n2, in_features=k2,
-                                        out_dtype=torch.float32)
-                y2 = quantized_matmul_gather(x2, shard2, qtype=qtype, out_features=n2 // world, in_features=k2,
-                                             region=region2, row0=rank * (n2 // world))
-                ok = ok and float((y2 - ref2).norm() / ref2.norm()) <= 1e-3
-            region2.close()
+        # Both ways of delivering the tiles: one multicast store per value
+        # through the NVSwitch (symmetric-memory regions, where the GPUs
+        # offer it) and one store per rank over NVLink.
+        for multicast in (True, False):
+            for qtype, n2, k2 in (("IQ4_XS", 2048, 5120), ("Q6_K", 1024, 17408)):
+                packed2 = random_matrix_torch(qtype, n2, k2, seed=6, device=dev)
+                shard2 = shard_packed(packed2, qtype, n2, k2, world, rank)
+                region2 = GatherRegion(64, n2, multicast=multicast)
+                if not multicast:
+                    ok = ok and region2.mc is None
+                for it in range(3):
+                    x2 = torch.randn(64, k2, device=dev, dtype=torch.bfloat16,
+                                     generator=torch.Generator(device=dev).manual_seed(10 + it))
+                    ref2 = quantized_matmul(x2, packed2, qtype=qtype, out_features=n2, in_features=k2,
+                                            out_dtype=torch.float32)
+                    y2 = quantized_matmul_gather(x2, shard2, qtype=qtype, out_features=n2 // world, in_features=k2,
+                                                 region=region2, row0=rank * (n2 // world))
+                    ok = ok and float((y2 - ref2).norm() / ref2.norm()) <= 1e-3
+                region2.close()
         ok = ok and _lib.load().gsq_device_status(None) == 0
         del g
         for r in regions:
