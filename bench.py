@@ -68,6 +68,13 @@ UNIT = "GB/s (packed weight bytes, QMV batch 1)"
 BLOCK_BYTES = {"IQ1_M": 56, "IQ1_S": 50, "IQ2_XXS": 66, "IQ2_XS": 74, "IQ2_S": 82, "IQ3_XXS": 98, "IQ3_S": 110,
                "IQ4_XS": 136, "Q2_K": 84, "Q4_K": 144, "Q6_K": 210}
 PARITY_REL_L2 = 1e-3
+_T0 = time.time()
+
+
+def log(msg: str) -> None:
+    """Progress on stderr (rank, seconds since start), so a slow or stuck
+    section of a run can be located."""
+    print(f"[bench rank {os.environ.get('RANK', '0')} +{time.time() - _T0:.1f}s] {msg}", file=sys.stderr, flush=True)
 
 
 def packed_bytes(q, n, k):
@@ -403,6 +410,7 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
                          group=dist.group.WORLD if world > 1 else None)
     del w
     torch.cuda.empty_cache()
+    log("model built")
     gen = torch.Generator(device=dev).manual_seed(1)
 
     def max_over_ranks(t):
@@ -435,6 +443,7 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
         model.prefill(ids)  # warm-up (workspaces, attention plans)
         torch.cuda.synchronize()
         t = timed(lambda: model.prefill(ids), 3, f"prefill {T}")
+        log(f"model prefill {T}: {t * 1e3:.1f} ms")
         out[f"prefill_{T}_ms"] = round(t * 1e3, 2)
         out[f"prefill_{T}_tok_s"] = round(T / t, 1)
 
@@ -448,6 +457,7 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
         model.capture_decode()
         model.replay_decode(3)  # warm-up replays
         t = timed(lambda: model.replay_decode(decode_tokens), 1, f"decode batch {B}") / decode_tokens
+        log(f"model decode batch {B}: {t * 1e3:.2f} ms/step")
         gbs = out["packed_bytes_per_token"] / t / 1e9
         decode.append({"batch": B, "ms_per_step": round(t * 1e3, 3), "tok_s": round(B / t, 1),
                        "packed_gbs": round(gbs, 1), "roofline_frac": round(gbs / (pk["hbm"] * world), 4)})
@@ -496,6 +506,7 @@ def main():
         return
 
     clocks = ClockSampler(local).start()  # before any barrier: no rank waits on nvidia-smi later
+    log("clock sampler started")
 
     import torch
     import torch.distributed as dist
@@ -513,6 +524,7 @@ def main():
     pk = peaks()
     lib = _lib.load()
     lib.gsq_device_status(None)
+    log("initialised")
 
     # ---- workload: every rank holds its row shard of every projection ----
     cfgs = []
@@ -531,6 +543,7 @@ def main():
     step_bytes = sum(c["bytes"] for c in cfgs)
     assert step_bytes == SWEEP_BYTES
     torch.cuda.synchronize()
+    log("QMV workload built")
 
     def matvec(c, x):
         """One projection: y, or (ranks > 1) every rank's rows gathered in c's region."""
@@ -553,10 +566,12 @@ def main():
     graph = graph_of(step, dev)
     torch.cuda.synchronize()
 
+    log("QMV step captured")
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
     device_ok(lib, dev, "warm-up")
+    log("QMV warm-up done")
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -580,6 +595,7 @@ def main():
         dist.barrier()
     ms_per_step = ms / args.steps
     value = step_bytes * args.steps / (ms / 1e3) / 1e9
+    log(f"QMV timed: {ms_per_step:.4f} ms/step")
 
     # ---- parity of the timed step's outputs ----
     worst, checked = 0.0, 0
@@ -603,6 +619,7 @@ def main():
               "against": ("the single-GPU matvec of the whole matrix on every rank (gathered rows vs it)"
                           if world > 1 else "float64 x @ bit-exact dequantized matrix (GPU dequant)")}
 
+    log(f"parity {worst:.2e}")
     # ---- roofline of the QMV kernel over the timed region ----
     alg_step = sum(c["alg"] for c in cfgs)
     achieved = alg_step / (ms_per_step / 1e3) / 1e9
@@ -716,11 +733,13 @@ def main():
                     "gsq_qmv_gather C-ABI call per projection (this rank's rows, every rank's rows gathered) -> "
                     "each gathered output copied to one pinned host buffer; one stream synchronisation per step")
 
+    log("per-configuration sweep done")
     for _ in range(2):
         e2e_step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    log("e2e warm-up done")
     e2e_steps = max(3, args.steps // 4)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -804,6 +823,7 @@ def main():
                 fl = 2.0 * 512 * n * k
                 flops_total += fl
                 t_qmm += t_ms / 1e3
+                log(f"qmm {q} {n}x{k}: {t_ms * 1e3:.1f} us")
                 qres.append({"type": q, "N": n, "K": k, "us": round(t_ms * 1e3, 1),
                              "TFLOPs": round(fl / (t_ms / 1e3) / 1e12, 1)})
                 del w
@@ -829,6 +849,7 @@ def main():
         c["full"] = None
     torch.cuda.empty_cache()
 
+    log("QMM done")
     embed = None
     if world == 1 and not args.no_embed:
         embed = embed_bench(dev, pk, lib, clocks)
@@ -840,6 +861,7 @@ def main():
         except Exception as e:  # recorded in the line; the QMV and QMM results above still stand
             model = {"error": f"{type(e).__name__}: {e}"[:300]}
 
+    log("model done")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = dict(cpu_reference_sweep(), kind="reference")
