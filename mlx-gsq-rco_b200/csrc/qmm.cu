@@ -116,13 +116,14 @@ __device__ __forceinline__ void qmm_store(const QmmArgs& a, int64_t m, int64_t e
 }
 
 // End of a gathering call, one thread per CTA, after the decoder warps'
-// barrier.  A CTA that stored an output tile (every CTA without split-K, the
-// last split otherwise) adds 1 to this rank's word in every peer's region
-// (release, system scope; the storing threads fenced their peer stores at
-// system scope before the barrier).  The last CTA of the grid (gpu-scope
-// ticket) then waits, bounded, until every peer's word in the own region
-// reaches this call's total (calls x tiles per rank, acquire): when the
-// kernel completes, every rank's tiles of this call are in every region.
+// barrier.  A CTA that completed an output tile (every CTA without split-K,
+// the split that finishes the tile's reduction otherwise) adds 1 to this
+// rank's word in every peer's region (release, system scope; the storing
+// threads fenced their peer stores at system scope before the barrier).  The
+// last CTA of the grid (gpu-scope ticket) then waits, bounded, until every
+// peer's word in the own region reaches the running total of tiles of all
+// calls on the region so far, this one included (acquire): when the kernel
+// completes, every rank's tiles of this call are in every region.
 // Every rank must make the same sequence of calls on a region.
 __device__ void qmm_gather_signal(const QmmArgs& a, bool stored) {
   unsigned* own = a.gflags[a.rank];
@@ -135,9 +136,12 @@ __device__ void qmm_gather_signal(const QmmArgs& a, bool stored) {
   const unsigned ctas = gridDim.x * gridDim.y * gridDim.z;
   if (atomicAdd(own + QMM_GFLAG_TICKET, 1u) != ctas - 1u) return;
   own[QMM_GFLAG_TICKET] = 0u;
-  const unsigned calls = own[QMM_GFLAG_COUNT] + 1u;
-  own[QMM_GFLAG_COUNT] = calls;
-  const unsigned expected = calls * (gridDim.x * gridDim.y);
+  // Running total of the tiles every peer has delivered into this region
+  // once this call is done: calls on a region may differ in token count (a
+  // shared prefill region sees prompts of any length), so the total grows
+  // by this call's tile count, which every rank computes the same way.
+  const unsigned expected = own[QMM_GFLAG_COUNT] + gridDim.x * gridDim.y;
+  own[QMM_GFLAG_COUNT] = expected;
   const long long t0 = clock64();
   for (int p = 0; p < a.world; p++) {
     if (p == a.rank) continue;

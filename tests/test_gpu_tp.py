@@ -110,6 +110,21 @@ def _worker(rank, world, port, q):
                                                  region=region2, row0=rank * (n2 // world))
                     ok = ok and float((y2 - ref2).norm() / ref2.norm()) <= 1e-3
                 region2.close()
+            # One region shared by calls of different token counts (one and
+            # several 512-token groups, as a model's prefill region sees).
+            n3, k3 = 1024, 5120
+            packed3 = random_matrix_torch("IQ3_S", n3, k3, seed=8, device=dev)
+            shard3 = shard_packed(packed3, "IQ3_S", n3, k3, world, rank)
+            region3 = GatherRegion(1300, n3, multicast=multicast)
+            for it, m3 in enumerate((64, 1300, 182, 600, 64)):
+                x3 = torch.randn(m3, k3, device=dev, dtype=torch.bfloat16,
+                                 generator=torch.Generator(device=dev).manual_seed(20 + it))
+                ref3 = quantized_matmul(x3, packed3, qtype="IQ3_S", out_features=n3, in_features=k3,
+                                        out_dtype=torch.float32)
+                y3 = quantized_matmul_gather(x3, shard3, qtype="IQ3_S", out_features=n3 // world, in_features=k3,
+                                             region=region3, row0=rank * (n3 // world))
+                ok = ok and float((y3 - ref3).norm() / ref3.norm()) <= 1e-3
+            region3.close()
         ok = ok and _lib.load().gsq_device_status(None) == 0
         del g
         for r in regions:
@@ -165,7 +180,10 @@ def _model_worker(rank, world, port, q):
 
         ok = True
         prompt = (torch.arange(12, dtype=torch.int32, device=dev) * 41) % cfg.vocab_size
-        ok = ok and rel(tp.prefill(prompt), one.prefill(prompt)) <= 1e-3  # matmul + NCCL all-gather
+        ok = ok and rel(tp.prefill(prompt), one.prefill(prompt)) <= 1e-3  # matmul, gather in the epilogue
+        long_prompt = (torch.arange(40, dtype=torch.int32, device=dev) * 17) % cfg.vocab_size
+        ok = ok and rel(tp.prefill(long_prompt), one.prefill(long_prompt)) <= 1e-3  # the same regions, more tokens
+        ok = ok and rel(tp.prefill(prompt), one.prefill(prompt)) <= 1e-3
         for t in (5, 77, 300):  # eager decode: the fused-gather matvec
             ok = ok and rel(tp.decode_step(t), one.decode_step(t)) <= 1e-3
         tp.capture_decode()
