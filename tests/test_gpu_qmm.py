@@ -77,3 +77,19 @@ def test_qmm_split_k_deterministic():
     b = quantized_matmul(x, w, qtype="IQ4_XS", out_features=640, in_features=17408, out_dtype=torch.float32)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("qtype", ["IQ2_XS", "IQ3_S", "Q6_K"])
+@pytest.mark.parametrize("m", [257, 300, 600, 1300])
+@pytest.mark.parametrize("nk", [(1024, 5120), (512, 2048), (4096, 2048)])
+def test_qmm_two_accumulators(qtype, m, nk):
+    """Token tiles of two accumulators narrower than 256 columns each (M
+    above 256 and not a multiple of 512: 2x160 columns at M=600, 2x224 at
+    M=1300), with several token groups, with K split over up to 8 CTAs (few
+    row tiles) and without."""
+    n, k = nk
+    packed = random_packed_gpu(qtype, n, k, seed=m + n)
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    y = quantized_matmul(x, packed, qtype=qtype, out_features=n, in_features=k, out_dtype=torch.float32)
+    exp = x.double() @ dense_gpu(packed, qtype, n, k).T
+    assert rel_l2(y.cpu(), exp.cpu()) <= REL_L2

@@ -33,6 +33,14 @@ def _worker(rank, world, port, q):
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    fails = []
+
+    def check(label, a, b, tol=1e-3):
+        e = float((a.float() - b.float()).norm() / b.float().norm())
+        if not (a.shape == b.shape and e <= tol):
+            fails.append(f"{label}: {e:.3g}")
+        return True
+
     try:
         ok = True
         for qtype, n, k in (("IQ3_S", 1024, 2048), ("Q4_K", 512, 5120)):
@@ -49,8 +57,7 @@ def _worker(rank, world, port, q):
                 else:
                     ref = quantized_matmul(x, packed, qtype=qtype, out_features=n, in_features=k,
                                            out_dtype=torch.float32)
-                err = float((y - ref).norm() / ref.norm())
-                ok = ok and y.shape == ref.shape and err <= 1e-3
+                check(f"RowParallelLinear {qtype} rows {rows}", y, ref)
         # Matvec with the gather fused in: against the NCCL path and one GPU,
         # repeated on two alternating regions (flag counts advance per call),
         # then replayed from a CUDA graph.
@@ -68,8 +75,7 @@ def _worker(rank, world, port, q):
             i = it % 2
             y = quantized_matvec_gather(xs[i], shard, qtype="IQ2_XS", out_features=n // world, in_features=k,
                                         region=regions[i], row0=rank * (n // world))
-            err = float((y - refs[i]).norm() / refs[i].norm())
-            ok = ok and err <= 1e-3
+            check(f"matvec gather call {it}", y, refs[i])
         g = torch.cuda.CUDAGraph()
         st = torch.cuda.Stream(device=dev)
         st.wait_stream(torch.cuda.current_stream(dev))
@@ -87,7 +93,7 @@ def _worker(rank, world, port, q):
             g.replay()
             torch.cuda.synchronize()
             for i in range(2):
-                ok = ok and float((regions[i].y - refs[i]).norm() / refs[i].norm()) <= 1e-3
+                check(f"matvec gather graph {i}", regions[i].y, refs[i])
         # Tiled matmul with the gather fused into its epilogue (split-K and
         # whole-K shapes), repeated on one region.
         from gsq_b200.parallel import quantized_matmul_gather
@@ -99,8 +105,8 @@ def _worker(rank, world, port, q):
                 packed2 = random_matrix_torch(qtype, n2, k2, seed=6, device=dev)
                 shard2 = shard_packed(packed2, qtype, n2, k2, world, rank)
                 region2 = GatherRegion(64, n2, multicast=multicast)
-                if not multicast:
-                    ok = ok and region2.mc is None
+                if not multicast and region2.mc is not None:
+                    fails.append("multicast region without asking")
                 for it in range(3):
                     x2 = torch.randn(64, k2, device=dev, dtype=torch.bfloat16,
                                      generator=torch.Generator(device=dev).manual_seed(10 + it))
@@ -108,7 +114,7 @@ def _worker(rank, world, port, q):
                                             out_dtype=torch.float32)
                     y2 = quantized_matmul_gather(x2, shard2, qtype=qtype, out_features=n2 // world, in_features=k2,
                                                  region=region2, row0=rank * (n2 // world))
-                    ok = ok and float((y2 - ref2).norm() / ref2.norm()) <= 1e-3
+                    check(f"matmul gather mc={multicast} {qtype} it {it}", y2, ref2)
                 region2.close()
             # One region shared by calls of different token counts (one and
             # several 512-token groups, as a model's prefill region sees).
@@ -123,15 +129,17 @@ def _worker(rank, world, port, q):
                                         out_dtype=torch.float32)
                 y3 = quantized_matmul_gather(x3, shard3, qtype="IQ3_S", out_features=n3 // world, in_features=k3,
                                              region=region3, row0=rank * (n3 // world))
-                ok = ok and float((y3 - ref3).norm() / ref3.norm()) <= 1e-3
+                check(f"shared region mc={multicast} M={m3}", y3, ref3)
             region3.close()
-        ok = ok and _lib.load().gsq_device_status(None) == 0
+        status = _lib.load().gsq_device_status(None)
+        if status:
+            fails.append(f"device status {status}")
         del g
         for r in regions:
             r.close()
         layer.close()
         torch.cuda.synchronize()
-        q.put((rank, ok))
+        q.put((rank, not fails, fails))
     finally:
         dist.destroy_process_group()
 
@@ -148,7 +156,7 @@ def _spawn(target, world):
     for p in procs:
         p.join(timeout=300)
     results = sorted(q.get(timeout=5) for _ in range(world))
-    assert results == [(r, True) for r in range(world)]
+    assert [r[:2] for r in results] == [(r, True) for r in range(world)], results
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
@@ -209,7 +217,7 @@ def _model_worker(rank, world, port, q):
         ok = ok and _lib.load().gsq_device_status(None) == 0
         tpb.close()
         tp.close()
-        q.put((rank, ok))
+        q.put((rank, ok, []))
     finally:
         dist.destroy_process_group()
 
