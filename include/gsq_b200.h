@@ -141,8 +141,10 @@ GSQ_API int gsq_ipc_close(void* peer);
  * and ends with the exchange of the rows through the regions' inboxes, so
  * that once the call has completed on `stream` every rank's region holds all
  * ntot rows of this call.  Every rank must make the same sequence of calls on a region; a
- * region must serve one call site (its rows stay valid until that site runs
- * again).  The flag wait is bounded: a rank that never arrives makes the
+ * region must serve one call site.  Its rows stay valid until any rank calls
+ * the region again: that call stores into every rank's copy, so a rank must
+ * not issue it before every rank has consumed the previous rows (another
+ * gathered call in between orders them, as does a barrier).  The flag wait is bounded: a rank that never arrives makes the
  * others return with gsq_device_status() == 1.  Output is fp32. */
 GSQ_API int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
                            int64_t rows, void* const* regions, int world, int rank, int64_t row0, int64_t ntot,

@@ -15,7 +15,10 @@ allocates ``gsq_gather_region_bytes(rows, ntot)`` bytes (256 bytes of control
 words, then fp32 ``rows x ntot``, then for fewer than 8 rows the matvec's
 inbox), exports a CUDA IPC handle, and maps its peers' regions.  Every rank
 must make the same sequence of calls on a region, and a region serves one
-call site: its rows stay valid until the same site runs again.
+call site: its rows stay valid until any rank runs the same site again (that
+call stores into every rank's copy, so it must not start on one rank before
+every rank has consumed the previous rows: another gathered call in between,
+or a barrier, orders them).
 """
 from __future__ import annotations
 

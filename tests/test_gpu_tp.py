@@ -115,6 +115,9 @@ def _worker(rank, world, port, q):
                     y2 = quantized_matmul_gather(x2, shard2, qtype=qtype, out_features=n2 // world, in_features=k2,
                                                  region=region2, row0=rank * (n2 // world))
                     check(f"matmul gather mc={multicast} {qtype} it {it}", y2, ref2)
+                    # The next call on this region stores into every rank's copy: no rank
+                    # may start it before every rank has read this call's rows.
+                    dist.barrier()
                 region2.close()
             # One region shared by calls of different token counts (one and
             # several 512-token groups, as a model's prefill region sees).
@@ -130,6 +133,7 @@ def _worker(rank, world, port, q):
                 y3 = quantized_matmul_gather(x3, shard3, qtype="IQ3_S", out_features=n3 // world, in_features=k3,
                                              region=region3, row0=rank * (n3 // world))
                 check(f"shared region mc={multicast} M={m3}", y3, ref3)
+                dist.barrier()
             region3.close()
         status = _lib.load().gsq_device_status(None)
         if status:
