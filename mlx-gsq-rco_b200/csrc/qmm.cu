@@ -91,6 +91,7 @@ struct QmmArgs {
   float* gy[QMM_GATHER_MAX];
   unsigned* gflags[QMM_GATHER_MAX];
   float* mcy;         // or: the fp32 output through the regions' NVSwitch multicast address
+  int gvec;           // rows of a token are 16-byte aligned in the regions (row0, ntot multiples of 4)
   int world, rank;
   int64_t row0, ntot;
 };
@@ -113,6 +114,48 @@ __device__ __forceinline__ void qmm_store(const QmmArgs& a, int64_t m, int64_t e
 #pragma unroll
   for (int p = 0; p < QMM_GATHER_MAX; p++)
     if (p < a.world) a.gy[p][off] = v;
+}
+
+// Four consecutive output rows [erow, erow + 4) of token m (16-byte
+// aligned: a.gvec): one 16-byte store per rank, or one multicast store.
+__device__ __forceinline__ void qmm_store_v4(const QmmArgs& a, int64_t m, int64_t erow, float4 v) {
+  const int64_t off = m * a.ntot + a.row0 + erow;
+  if (a.mcy) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(a.mcy + off), "f"(v.x),
+                 "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+    return;
+  }
+#pragma unroll
+  for (int p = 0; p < QMM_GATHER_MAX; p++)
+    if (p < a.world) *reinterpret_cast<float4*>(a.gy[p] + off) = v;
+}
+
+// A warp's 32 rows (lanes) x NJ tokens of a gathering epilogue: staged in
+// shared memory (token-major), then written as 16-byte stores of 4
+// consecutive rows -- remote and multicast stores move whole 16-byte pieces
+// instead of 4-byte ones.  `stage`: 32 * NJ floats of this warp.
+template <int NJ>
+__device__ __forceinline__ void gather_store_rows(const QmmArgs& a, float* stage, const float (&v)[NJ], int lane,
+                                                  int64_t m_first, int64_t row_first) {
+#pragma unroll
+  for (int j = 0; j < NJ; j++) stage[j * 32 + lane] = v[j];
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < NJ / 4; i++) {
+    const int idx = lane + 32 * i;         // (token, 4-row group) pairs
+    const int t = idx >> 3, r4 = (idx & 7) * 4;
+    const int64_t m = m_first + t, row = row_first + r4;
+    if (m >= a.M || row >= a.N) continue;
+    const float4 q = *reinterpret_cast<const float4*>(stage + t * 32 + r4);
+    if (row + 3 < a.N) {
+      qmm_store_v4(a, m, row, q);
+    } else {
+      const float e[4] = {q.x, q.y, q.z, q.w};
+      for (int k = 0; k < 4 && row + k < a.N; k++) qmm_store<true>(a, m, row + k, e[k]);
+    }
+  }
+  __syncwarp();
 }
 
 // End of a gathering call, one thread per CTA, after the decoder warps'
@@ -437,6 +480,9 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
     if (ok) ok = mbar_wait_bounded(accf, 0u, a.err);
     tc_fence_after();
     const uint32_t lane_base = (uint32_t)(32 * sub) << 16;
+    // Gathering epilogue staging: 2 KB per decoder warp in the A stages,
+    // which no MMA reads any more (accf completed).
+    float* gstage = reinterpret_cast<float*>(astage) + dw * 32 * 16;
     const int cols = ttok / 2;
     const int64_t tile = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
     if (a.ksplit == 1) {
@@ -444,6 +490,15 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
         for (int j0 = ehalf * cols; j0 < (ehalf + 1) * cols; j0 += 16) {
           uint32_t vv[16];
           tmem_ld16(tmem_d + lane_base + (uint32_t)j0, vv);
+          if constexpr (GATHER) {
+            if (a.gvec) {  // whole warp: the staging needs every lane
+              float f[16];
+#pragma unroll
+              for (int jj = 0; jj < 16; jj++) f[jj] = __uint_as_float(vv[jj]);
+              gather_store_rows<16>(a, gstage, f, lane, (int64_t)m0 + j0, n0 + 32 * sub);
+              continue;
+            }
+          }
           if (elive) {
 #pragma unroll
             for (int jj = 0; jj < 16; jj++) {
@@ -492,7 +547,7 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
       }
       named_sync_decoders();
       const bool reduce = ok && *last_flag != 0u;
-      if (reduce && elive) {
+      if (reduce) {
         // This split's chunks of 8 columns in this warp's column half: 8
         // columns x all splits (<= QMM_KSPLIT_MAX) of loads in flight.
         const float* base = a.part + (tile * a.ksplit * ttok) * QMM_BM;
@@ -506,13 +561,26 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
             for (int jj = 0; jj < 8; jj++)
               v[z][jj] = z < a.ksplit ? __ldcg(base + ((int64_t)z * ttok + j0 + jj) * QMM_BM + er) : 0.f;
           }
+          float accs[8];
 #pragma unroll
           for (int jj = 0; jj < 8; jj++) {
             float acc = v[0][jj];
 #pragma unroll
             for (int z = 1; z < QMM_KSPLIT_MAX; z++) acc += v[z][jj];  // zeros beyond ksplit
-            const int64_t m = (int64_t)m0 + j0 + jj;
-            if (m < a.M) qmm_store<GATHER>(a, m, erow, acc);
+            accs[jj] = acc;
+          }
+          if constexpr (GATHER) {
+            if (a.gvec) {  // whole warp (the loop bounds are uniform over the warp)
+              gather_store_rows<8>(a, gstage, accs, lane, (int64_t)m0 + j0, n0 + 32 * sub);
+              continue;
+            }
+          }
+          if (elive) {
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+              const int64_t m = (int64_t)m0 + j0 + jj;
+              if (m < a.M) qmm_store<GATHER>(a, m, erow, accs[jj]);
+            }
           }
         }
       }
@@ -686,6 +754,7 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
     a.gflags[i] = nullptr;
   }
   a.mcy = nullptr;
+  a.gvec = 0;
   if (gather && gather->world > 1) {
     if (gather->world > QMM_GATHER_MAX || gather->rank < 0 || gather->rank >= gather->world) {
       *why = "invalid gather world/rank";
@@ -701,6 +770,7 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
       a.gy[i] = reinterpret_cast<float*>(r + 256);
     }
     if (gather->multicast) a.mcy = reinterpret_cast<float*>(static_cast<uint8_t*>(gather->multicast) + 256);
+    a.gvec = (gather->row0 % 4 == 0 && gather->ntot % 4 == 0) ? 1 : 0;
   }
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
