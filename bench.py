@@ -774,7 +774,7 @@ def main():
     gather_path = None
     if not args.no_qmm:
         qres = []
-        flops_total, t_qmm = 0.0, 0.0
+        flops_total, t_qmm, t_qmm16 = 0.0, 0.0, 0.0
         for q in QMM_TYPES:
             for (n, k) in QMM_SHAPES:
                 rows = n // world
@@ -783,49 +783,70 @@ def main():
                 w = full[rank * rows * rb:(rank + 1) * rows * rb].clone()
                 x = torch.randn(512, k, device=dev, dtype=torch.bfloat16,
                                 generator=torch.Generator(device=dev).manual_seed(11))
-                region = GatherRegion(512, n) if world > 1 else None
 
-                def prefill():
-                    if world > 1:
-                        return quantized_matmul_gather(x, w, qtype=q, out_features=rows, in_features=k, region=region,
-                                                       row0=rank * rows)
-                    return quantized_matmul(x, w, qtype=q, out_features=rows, in_features=k, out_dtype=torch.float32)
+                def timed(region):
+                    """us per call (max over ranks) of a graph of 8 calls, replayed 3 times."""
+                    def prefill():
+                        if world > 1:
+                            return quantized_matmul_gather(x, w, qtype=q, out_features=rows, in_features=k,
+                                                           region=region, row0=rank * rows)
+                        return quantized_matmul(x, w, qtype=q, out_features=rows, in_features=k,
+                                                out_dtype=torch.float32)
 
-                for _ in range(2):
-                    prefill()
-                torch.cuda.synchronize()
-                g = graph_of(prefill, dev, reps=8)
-                g.replay()
-                torch.cuda.synchronize()
-                if world > 1:
-                    dist.barrier()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                clocks.mark_start()
-                e0.record()
-                for _ in range(3):
+                    for _ in range(2):
+                        prefill()
+                    torch.cuda.synchronize()
+                    g = graph_of(prefill, dev, reps=8)
                     g.replay()
-                e1.record()
-                torch.cuda.synchronize()
-                clocks.mark_end()
-                device_ok(lib, dev, f"qmm {q} {n}x{k}")
-                t_ms = e0.elapsed_time(e1) / 24
-                if world > 1:
-                    # the gathered output of the last replay against the single-GPU matmul of the whole matrix
+                    torch.cuda.synchronize()
+                    if world > 1:
+                        dist.barrier()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    clocks.mark_start()
+                    e0.record()
+                    for _ in range(3):
+                        g.replay()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    clocks.mark_end()
+                    device_ok(lib, dev, f"qmm {q} {n}x{k}")
+                    del g
+                    t = e0.elapsed_time(e1) / 24
+                    if world > 1:
+                        tt = torch.tensor([t], device=dev)
+                        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                        t = float(tt.item())
+                    return t
+
+                entry = {"type": q, "N": n, "K": k}
+                if world == 1:
+                    t_ms = timed(None)
+                else:
+                    # fp32 regions (the single-GPU output type), then fp16
+                    # regions (half the NVLink bytes); each gathered output
+                    # of the last replay against the single-GPU matmul of the
+                    # whole matrix
                     ref = quantized_matmul(x, full, qtype=q, out_features=n, in_features=k, out_dtype=torch.float32)
+                    region = GatherRegion(512, n)
+                    t_ms = timed(region)
                     qmm_worst = max(qmm_worst, rel_l2(region.y[:512], ref))
-                    del ref
-                    tt = torch.tensor([t_ms], device=dev)
-                    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-                    t_ms = float(tt.item())
                     gather_path = "NVSwitch multicast stores" if region.mc else "peer stores to every rank"
                     region.close()
-                del g, full
+                    region = GatherRegion(512, n, dtype=torch.float16)
+                    t16 = timed(region)
+                    qmm_worst = max(qmm_worst, rel_l2(region.y[:512].float(), ref))
+                    region.close()
+                    del ref
+                    entry["us_fp16_gather"] = round(t16 * 1e3, 1)
+                    t_qmm16 += t16 / 1e3
+                del full
                 fl = 2.0 * 512 * n * k
                 flops_total += fl
                 t_qmm += t_ms / 1e3
-                log(f"qmm {q} {n}x{k}: {t_ms * 1e3:.1f} us")
-                qres.append({"type": q, "N": n, "K": k, "us": round(t_ms * 1e3, 1),
-                             "TFLOPs": round(fl / (t_ms / 1e3) / 1e12, 1)})
+                log(f"qmm {q} {n}x{k}: {t_ms * 1e3:.1f} us" + (
+                    f" (fp16 gather {entry['us_fp16_gather']} us)" if world > 1 else ""))
+                entry.update(us=round(t_ms * 1e3, 1), TFLOPs=round(fl / (t_ms / 1e3) / 1e12, 1))
+                qres.append(entry)
                 del w
         tf = flops_total / t_qmm / 1e12
         qmm = {"M": 512, "tflops": round(tf, 1), "peak": round(pk["bf16"] * world, 1),
@@ -836,13 +857,15 @@ def main():
                "note": "includes the bf16->fp16 activation pre-pass; weights decoded once per 128x128 tile; "
                        "CUDA graph of 8 launches, CUDA events" + (
                            f"; {world} ranks: row shards, the gather fused into the matmul epilogue ({gather_path}), "
-                           f"max over ranks, peak = {world} x the measured bf16 peak" if world > 1 else "")}
+                           f"max over ranks, peak = {world} x the measured bf16 peak; us / tflops: fp32 regions, "
+                           f"us_fp16_gather / tflops_fp16_gather: fp16 regions" if world > 1 else "")}
         if world > 1:
+            qmm["tflops_fp16_gather"] = round(flops_total / t_qmm16 / 1e12, 1)
             t = torch.tensor([qmm_worst], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             qmm_worst = float(t.item())
             parity["qmm_max_rel_l2"] = qmm_worst
-            parity["qmm_n_checked"] = len(qres)
+            parity["qmm_n_checked"] = 2 * len(qres)
     if qmm is not None and world == 1:
         qmm["by_M"] = qmm_by_m(dev, pk, lib, clocks)
     for c in cfgs:

@@ -87,11 +87,13 @@ GSQ_API int gsq_qmv(int qtype, const void* x, int x_dtype, const uint8_t* packed
 GSQ_API size_t gsq_qmm_workspace_size(int qtype, int64_t N, int64_t K, int64_t M, int x_dtype);
 
 /* Tiled dequantize + matmul on tcgen05 tensor cores (prefill):
- *   y[m, n] = sum_k x[m, k] * deq(W)[n, k],  fp32 output, M x N row-major.
+ *   y[m, n] = sum_k x[m, k] * deq(W)[n, k],  M x N row-major in y_dtype
+ *   (fp32, or fp16 / bf16 rounded once to nearest even from the fp32 sum).
  * x: M x K (x_dtype), 16-byte aligned; weights decoded to fp16, fp32 accumulation.
- * Replaces quantized_matmul (mlx_gsq/runtime/kernels/qmm.py:559-594). */
+ * Replaces quantized_matmul (mlx_gsq/runtime/kernels/qmm.py:559-594), whose
+ * output has x's dtype. */
 GSQ_API int gsq_qmm(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-            float* y, void* workspace, size_t workspace_bytes, gsq_stream_t stream);
+                    void* y, int y_dtype, void* workspace, size_t workspace_bytes, gsq_stream_t stream);
 
 /* Packed embedding gather: out[t, :] = deq(W)[ids[t], :] rounded once to
  * out_dtype; W is vocab x dim packed rows.  Out-of-range ids leave their row
@@ -152,14 +154,17 @@ GSQ_API int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t*
 
 /* gsq_qmm for rank `rank` of `world` (2..8) holding output rows
  * [row0, row0 + N) of ntot (prefill): every output tile is stored into every
- * rank's region (fp32 M x ntot at byte 256) over NVLink as the epilogue
- * writes it, and each rank counts the tiles its peers delivered, so that once
- * the call has completed on `stream` every rank's region holds all ntot rows.
- * Same region rules and bounded wait as gsq_qmv_gather (a region for M >= 8
- * rows has no inbox: gsq_gather_region_bytes(M, ntot) bytes). */
+ * rank's region (M x ntot values at byte 256: fp32 for y_dtype 0, fp16
+ * rounded to nearest even for y_dtype 1, which halves the bytes that cross
+ * NVLink) over NVLink as the epilogue writes it, and each rank counts the
+ * tiles its peers delivered, so that once the call has completed on `stream`
+ * every rank's region holds all ntot rows.  Every call on a region uses the
+ * same y_dtype.  Same region rules and bounded wait as gsq_qmv_gather (a
+ * region for M >= 8 rows has no inbox: gsq_gather_region_bytes(M, ntot)
+ * bytes, enough for either value type). */
 GSQ_API int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
                            int64_t M, void* const* regions, int world, int rank, int64_t row0, int64_t ntot,
-                           void* workspace, size_t workspace_bytes, gsq_stream_t stream);
+                           int y_dtype, void* workspace, size_t workspace_bytes, gsq_stream_t stream);
 
 /* gsq_qmm_gather writing every output value once, through an NVSwitch
  * multicast mapping of the ranks' regions (multimem stores: the switch
@@ -171,7 +176,7 @@ GSQ_API int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t*
  * reference counterpart (the reference runs on one device). */
 GSQ_API int gsq_qmm_gather_mc(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
                               int64_t M, void* const* regions, void* multicast_region, int world, int rank,
-                              int64_t row0, int64_t ntot, void* workspace, size_t workspace_bytes,
+                              int64_t row0, int64_t ntot, int y_dtype, void* workspace, size_t workspace_bytes,
                               gsq_stream_t stream);
 
 /* Synchronises `stream`, then returns and clears the device error word the

@@ -31,12 +31,13 @@ extern "C" {
 GSQ_API int gsq_rmsnorm(float* resid, const float* delta, int64_t rows, int64_t dim, const float* weight, float eps,
                         void* out, int out_dtype, gsq_stream_t stream);
 
-/* out[r,i] = silu(gate[r,i]) * up[r,i] from a [rows, 2n] fp32 input: with
- * group == 0 the gate projection's n outputs then the up projection's; with
- * group g > 0 (n % g == 0) interleaved groups of g gate then g up outputs
- * (the layout of an interleaved gate|up matrix, see gsq_qmv_swiglu). */
-GSQ_API int gsq_silu_mul(const float* gu, int64_t rows, int64_t n, int64_t group, void* out, int out_dtype,
-                         gsq_stream_t stream);
+/* out[r,i] = silu(gate[r,i]) * up[r,i] from a [rows, 2n] input of gu_dtype
+ * (fp32, fp16 or bf16; computed in fp32): with group == 0 the gate
+ * projection's n outputs then the up projection's; with group g > 0
+ * (n % g == 0) interleaved groups of g gate then g up outputs (the layout of
+ * an interleaved gate|up matrix, see gsq_qmv_swiglu). */
+GSQ_API int gsq_silu_mul(const void* gu, int gu_dtype, int64_t rows, int64_t n, int64_t group, void* out,
+                         int out_dtype, gsq_stream_t stream);
 
 /* The FFN's gate and up projections and their SwiGLU product in one fused
  * matvec (decode, 0 < rows < 8): `packed` is a packed matrix of 2*n_out rows

@@ -237,13 +237,15 @@ int gsq_qmv_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed,
 
 static int qmm_gather_run(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K,
                           int64_t M, void* const* regions, void* multicast, int world, int rank, int64_t row0,
-                          int64_t ntot, void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
+                          int64_t ntot, int y_dtype, void* workspace, size_t workspace_bytes,
+                          gsq_stream_t stream) {
   int rc = check_matrix(qtype, packed, N, K);
   if (rc) return rc;
   if (world < 2 || world > 8 || rank < 0 || rank >= world) return fail(GSQ_ERR_ARG, "world must be 2..8 and rank < world");
   if (!regions) return fail(GSQ_ERR_ARG, "null region list");
   for (int i = 0; i < world; i++)
     if (!regions[i] || !aligned(regions[i], 256)) return fail(GSQ_ERR_ALIGN, "region %d missing or not 256-byte aligned", i);
+  if (y_dtype != DT_F32 && y_dtype != DT_F16) return fail(GSQ_ERR_ARG, "gathered values must be fp32 or fp16");
   if (M <= 0 || M > (1ll << 31)) return fail(GSQ_ERR_SIZE, "invalid row count %lld", (long long)M);
   if (row0 < 0 || N <= 0 || row0 + N > ntot)
     return fail(GSQ_ERR_SIZE, "rows [%lld, %lld) outside the %lld gathered rows", (long long)row0,
@@ -257,9 +259,9 @@ static int qmm_gather_run(int qtype, const void* x, int x_dtype, const uint8_t* 
                 workspace_bytes);
   if (multicast && !aligned(multicast, 256)) return fail(GSQ_ERR_ALIGN, "multicast region not 256-byte aligned");
   const QmmGather g = {regions, world, rank, row0, ntot, multicast};
-  float* own_y = reinterpret_cast<float*>(static_cast<uint8_t*>(regions[rank]) + 256);
+  void* own_y = static_cast<uint8_t*>(regions[rank]) + 256;
   const char* why = "";
-  cudaError_t e = qmm_launch(qtype, x, x_dtype, packed, N, K, M, own_y, workspace, device_error_word(),
+  cudaError_t e = qmm_launch(qtype, x, x_dtype, packed, N, K, M, own_y, y_dtype, workspace, device_error_word(),
                              (cudaStream_t)stream, &why, &g);
   if (e != cudaSuccess) return fail(GSQ_ERR_CUDA, "gsq_qmm_gather launch: %s (%s)", cudaGetErrorString(e), why);
   return GSQ_OK;
@@ -268,18 +270,18 @@ static int qmm_gather_run(int qtype, const void* x, int x_dtype, const uint8_t* 
 extern "C" {
 
 int gsq_qmm_gather(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-                   void* const* regions, int world, int rank, int64_t row0, int64_t ntot, void* workspace,
-                   size_t workspace_bytes, gsq_stream_t stream) {
-  return qmm_gather_run(qtype, x, x_dtype, packed, N, K, M, regions, nullptr, world, rank, row0, ntot, workspace,
-                        workspace_bytes, stream);
+                   void* const* regions, int world, int rank, int64_t row0, int64_t ntot, int y_dtype,
+                   void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
+  return qmm_gather_run(qtype, x, x_dtype, packed, N, K, M, regions, nullptr, world, rank, row0, ntot, y_dtype,
+                        workspace, workspace_bytes, stream);
 }
 
 int gsq_qmm_gather_mc(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
                       void* const* regions, void* multicast_region, int world, int rank, int64_t row0, int64_t ntot,
-                      void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
+                      int y_dtype, void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
   if (!multicast_region) return fail(GSQ_ERR_ARG, "null multicast region");
   return qmm_gather_run(qtype, x, x_dtype, packed, N, K, M, regions, multicast_region, world, rank, row0, ntot,
-                        workspace, workspace_bytes, stream);
+                        y_dtype, workspace, workspace_bytes, stream);
 }
 
 size_t gsq_qmm_workspace_size(int qtype, int64_t N, int64_t K, int64_t M, int x_dtype) {
@@ -288,20 +290,22 @@ size_t gsq_qmm_workspace_size(int qtype, int64_t N, int64_t K, int64_t M, int x_
 }
 
 int gsq_qmm(int qtype, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-            float* y, void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
+            void* y, int y_dtype, void* workspace, size_t workspace_bytes, gsq_stream_t stream) {
   int rc = check_matrix(qtype, packed, N, K);
   if (rc) return rc;
   if (M < 0 || M > (1ll << 31)) return fail(GSQ_ERR_SIZE, "invalid row count %lld", (long long)M);
   if (M == 0 || N == 0) return GSQ_OK;
   if (!x || !y) return fail(GSQ_ERR_ARG, "null x or y");
   if (!dtype_ok(x_dtype)) return fail(GSQ_ERR_ARG, "unsupported x dtype");
-  if (!aligned(x, 16) || !aligned(y, 4)) return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned");
+  if (!dtype_ok(y_dtype)) return fail(GSQ_ERR_ARG, "unsupported y dtype");
+  if (!aligned(x, 16) || !aligned(y, y_dtype == DT_F32 ? 4 : 2))
+    return fail(GSQ_ERR_ALIGN, "x must be 16-byte aligned, y aligned to its type");
   const size_t need = qmm_workspace_bytes(qtype, N, K, M, x_dtype);
   if (need > 0 && (!workspace || workspace_bytes < need || !aligned(workspace, 256)))
     return fail(GSQ_ERR_WORKSPACE, "gsq_qmm needs %zu workspace bytes (256-byte aligned), got %zu", need,
                 workspace_bytes);
   const char* why = "launch";
-  cudaError_t e = qmm_launch(qtype, x, x_dtype, packed, N, K, M, y, workspace, device_error_word(),
+  cudaError_t e = qmm_launch(qtype, x, x_dtype, packed, N, K, M, y, y_dtype, workspace, device_error_word(),
                              (cudaStream_t)stream, &why);
   return e == cudaSuccess ? GSQ_OK : cuda_fail(e, why);
 }

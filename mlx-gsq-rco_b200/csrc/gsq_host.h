@@ -91,8 +91,10 @@ struct QmmGather {
   void* multicast;  // NVSwitch multicast mapping of the regions, or nullptr
 };
 
+// y: M x N values of y_dtype (DT_F32 / DT_F16 / DT_BF16), or with `gather`
+// this rank's region values (DT_F32 / DT_F16).
 cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-                       float* y, void* ws, int* err, cudaStream_t st, const char** why,
+                       void* y, int y_dtype, void* ws, int* err, cudaStream_t st, const char** why,
                        const struct QmmGather* gather = nullptr);
 
 // Device address of the library's error word on the current device (the

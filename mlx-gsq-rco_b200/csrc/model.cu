@@ -168,8 +168,10 @@ __global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(float* resid, cons
 }
 
 // group 0: gu = [gate | up] halves; group g > 0: gate and up interleaved in
-// groups of g columns (g gate columns, then the same g up columns).
-__global__ void silu_mul_kernel(const float* gu, int64_t rows, int64_t n, int64_t group, void* out, int dt) {
+// groups of g columns (g gate columns, then the same g up columns).  gu is
+// fp32, fp16 or bf16 (gu_dt).
+__global__ void silu_mul_kernel(const void* gu, int gu_dt, int64_t rows, int64_t n, int64_t group, void* out,
+                                int dt) {
   pdl_launch_dependents();
   pdl_wait();
   const int64_t total = rows * n;
@@ -181,7 +183,59 @@ __global__ void silu_mul_kernel(const float* gu, int64_t rows, int64_t n, int64_
       gcol = c + q * group;
       ucol = gcol + group;
     }
-    store_out(out, dt, i, silu(gu[r * 2 * n + gcol]) * gu[r * 2 * n + ucol]);
+    store_out(out, dt, i, silu(load_act(gu, gu_dt, r * 2 * n + gcol)) * load_act(gu, gu_dt, r * 2 * n + ucol));
+  }
+}
+
+// Eight outputs per thread: the gate values at gu[row][g0 .. g0+7] and the
+// up values at gu[row][u0 .. u0+7] (16-byte loads of fp16 / bf16, two of
+// fp32), out[row][8c .. 8c+7] as one 16-byte store (fp16 / bf16) or two
+// (fp32).  grid.y = rows; group 8: g0 = 16c, u0 = 16c + 8; group 0: g0 = 8c,
+// u0 = n + 8c.
+template <typename IT>
+__device__ __forceinline__ void load8(const IT* p, float (&f)[8]) {
+  if constexpr (sizeof(IT) == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    const IT* e = reinterpret_cast<const IT*>(&v);
+#pragma unroll
+    for (int i = 0; i < 8; i++) f[i] = to_f32(e[i]);
+  }
+}
+
+template <typename IT>
+__global__ void silu_mul8_kernel(const IT* gu, int64_t n, int64_t group, void* out, int dt) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n / 8) return;
+  const int64_t row = blockIdx.y;
+  const IT* base = gu + row * 2 * n;
+  float g[8], u[8], y[8];
+  load8(base + (group ? 16 * c : 8 * c), g);
+  load8(base + (group ? 16 * c + 8 : n + 8 * c), u);
+#pragma unroll
+  for (int i = 0; i < 8; i++) y[i] = silu(g[i]) * u[i];
+  const int64_t o = row * n + 8 * c;
+  if (dt == DT_F32) {
+    float4* p = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + o);
+    p[0] = make_float4(y[0], y[1], y[2], y[3]);
+    p[1] = make_float4(y[4], y[5], y[6], y[7]);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      if (dt == DT_F16) {
+        const __half2 h = __floats2half2_rn(y[2 * i], y[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      } else {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + o) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -626,15 +680,33 @@ int gsq_rmsnorm(float* resid, const float* delta, int64_t rows, int64_t dim, con
   return launched("gsq_rmsnorm");
 }
 
-int gsq_silu_mul(const float* gu, int64_t rows, int64_t n, int64_t group, void* out, int out_dtype,
+int gsq_silu_mul(const void* gu, int gu_dtype, int64_t rows, int64_t n, int64_t group, void* out, int out_dtype,
                  gsq_stream_t stream) {
   if (!gu || !out) return fail(GSQ_ERR_ARG, "gsq_silu_mul: null pointer");
   if (rows < 0 || n <= 0 || group < 0 || (group > 0 && n % group)) return fail(GSQ_ERR_SIZE, "gsq_silu_mul: bad shape");
-  if (!dt_ok(out_dtype)) return fail(GSQ_ERR_ARG, "gsq_silu_mul: bad output dtype");
+  if (!dt_ok(out_dtype) || !dt_ok(gu_dtype)) return fail(GSQ_ERR_ARG, "gsq_silu_mul: bad dtype");
   if (rows == 0) return GSQ_OK;
+  // Eight outputs per thread where every 8-value piece is 16-byte aligned.
+  const size_t isz = gu_dtype == DT_F32 ? 4 : 2;
+  if ((group == 0 || group == 8) && n % 8 == 0 && rows <= 65535 && (2 * n * isz) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(gu) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0) {
+    const dim3 grid((unsigned)((n / 8 + 255) / 256), (unsigned)rows);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (gu_dtype == DT_F16)
+      launch_pdl(silu_mul8_kernel<__half>, grid, dim3(256), 0, st, static_cast<const __half*>(gu), n, group, out,
+                 out_dtype);
+    else if (gu_dtype == DT_BF16)
+      launch_pdl(silu_mul8_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, static_cast<const __nv_bfloat16*>(gu), n,
+                 group, out, out_dtype);
+    else
+      launch_pdl(silu_mul8_kernel<float>, grid, dim3(256), 0, st, static_cast<const float*>(gu), n, group, out,
+                 out_dtype);
+    return launched("gsq_silu_mul");
+  }
   const int64_t total = rows * n;
   const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 16);
-  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, (cudaStream_t)stream, gu, rows, n, group, out, out_dtype);
+  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, (cudaStream_t)stream, gu, gu_dtype, rows, n, group, out,
+             out_dtype);
   return launched("gsq_silu_mul");
 }
 

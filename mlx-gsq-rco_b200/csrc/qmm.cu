@@ -79,19 +79,22 @@ constexpr int QMM_GFLAG_TICKET = 62, QMM_GFLAG_COUNT = 63;  // owner's words of 
 struct QmmArgs {
   const uint8_t* packed;
   int64_t N, K, M, row_bytes, packed_bytes;
-  float* y;
+  void* y;            // M x N, ydt (without the gather)
+  int ydt;            // DT_F32 / DT_F16 / DT_BF16 (rounded to nearest even)
   float* part;        // [row tiles x token groups][ksplit][T][128] partial tiles (ksplit > 1)
   unsigned* tickets;  // [row tiles x token groups] (ksplit > 1)
   int bn, nacc;       // MMA N per accumulator, accumulators per CTA
   int ksplit, kbs;    // K splits, 256-blocks per split
   int* err;
   // Fused row gather (world > 1, gsq_qmm_gather): output rows
-  // [row0, row0 + N) of ntot go to every rank's region (fp32 [M][ntot] after
-  // a 256-byte header whose word p counts the tiles rank p has delivered).
+  // [row0, row0 + N) of ntot go to every rank's region ([M][ntot] fp32, or
+  // fp16 with yh, after a 256-byte header whose word p counts the tiles rank
+  // p has delivered).
   float* gy[QMM_GATHER_MAX];
   unsigned* gflags[QMM_GATHER_MAX];
-  float* mcy;         // or: the fp32 output through the regions' NVSwitch multicast address
-  int gvec;           // rows of a token are 16-byte aligned in the regions (row0, ntot multiples of 4)
+  float* mcy;         // or: the output through the regions' NVSwitch multicast address
+  int yh;             // the regions hold fp16 values (round to nearest even)
+  int gvec;           // 16-byte pieces of 4 (fp32) or 8 (fp16) consecutive rows are aligned in the regions
   int world, rank;
   int64_t row0, ntot;
 };
@@ -101,10 +104,19 @@ struct QmmArgs {
 template <bool GATHER>
 __device__ __forceinline__ void qmm_store(const QmmArgs& a, int64_t m, int64_t erow, float v) {
   if constexpr (!GATHER) {
-    a.y[m * a.N + erow] = v;
+    store_out(a.y, a.ydt, m * a.N + erow, v);
     return;
   }
   const int64_t off = m * a.ntot + a.row0 + erow;
+  if (a.yh) {
+    // (multimem stores have no single-fp16 form: one store per rank through
+    // the unicast mappings, which a multicast call also holds)
+    const __half h = __float2half_rn(v);
+#pragma unroll
+    for (int p = 0; p < QMM_GATHER_MAX; p++)
+      if (p < a.world) reinterpret_cast<__half*>(a.gy[p])[off] = h;
+    return;
+  }
   if (a.mcy) {
     // One store through the multicast address: the switch writes it into
     // every rank's region (this rank's included).
@@ -131,16 +143,57 @@ __device__ __forceinline__ void qmm_store_v4(const QmmArgs& a, int64_t m, int64_
     if (p < a.world) *reinterpret_cast<float4*>(a.gy[p] + off) = v;
 }
 
+// Eight consecutive output rows [erow, erow + 8) of token m as fp16 (16-byte
+// aligned: a.gvec with a.yh).
+__device__ __forceinline__ void qmm_store_h8(const QmmArgs& a, int64_t m, int64_t erow, uint4 v) {
+  const int64_t off = m * a.ntot + a.row0 + erow;
+  __half* mc = reinterpret_cast<__half*>(a.mcy);
+  if (mc) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc + off), "r"(v.x),
+                 "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+    return;
+  }
+#pragma unroll
+  for (int p = 0; p < QMM_GATHER_MAX; p++)
+    if (p < a.world) *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(a.gy[p]) + off) = v;
+}
+
 // A warp's 32 rows (lanes) x NJ tokens of a gathering epilogue: staged in
-// shared memory (token-major), then written as 16-byte stores of 4
-// consecutive rows -- remote and multicast stores move whole 16-byte pieces
-// instead of 4-byte ones.  `stage`: 32 * NJ floats of this warp.
+// shared memory (token-major), then written as 16-byte stores of 4 (fp32)
+// or 8 (fp16) consecutive rows -- remote and multicast stores move whole
+// 16-byte pieces instead of 4- or 2-byte ones.  `stage`: 32 * NJ floats of
+// this warp.
 template <int NJ>
 __device__ __forceinline__ void gather_store_rows(const QmmArgs& a, float* stage, const float (&v)[NJ], int lane,
                                                   int64_t m_first, int64_t row_first) {
+  static_assert(NJ % 8 == 0, "whole 8-row pieces per lane");
 #pragma unroll
   for (int j = 0; j < NJ; j++) stage[j * 32 + lane] = v[j];
   __syncwarp();
+  if (a.yh) {
+#pragma unroll
+    for (int i = 0; i < NJ / 8; i++) {
+      const int idx = lane + 32 * i;         // (token, 8-row group) pairs
+      const int t = idx >> 2, r8 = (idx & 3) * 8;
+      const int64_t m = m_first + t, row = row_first + r8;
+      if (m >= a.M || row >= a.N) continue;
+      const float4 q0 = *reinterpret_cast<const float4*>(stage + t * 32 + r8);
+      const float4 q1 = *reinterpret_cast<const float4*>(stage + t * 32 + r8 + 4);
+      if (row + 7 < a.N) {
+        const __half2 h0 = __floats2half2_rn(q0.x, q0.y), h1 = __floats2half2_rn(q0.z, q0.w);
+        const __half2 h2 = __floats2half2_rn(q1.x, q1.y), h3 = __floats2half2_rn(q1.z, q1.w);
+        qmm_store_h8(a, m, row,
+                     make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                                *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3)));
+      } else {
+        const float e[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        for (int k = 0; k < 8 && row + k < a.N; k++) qmm_store<true>(a, m, row + k, e[k]);
+      }
+    }
+    __syncwarp();
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < NJ / 4; i++) {
     const int idx = lane + 32 * i;         // (token, 4-row group) pairs
@@ -610,11 +663,48 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
 }
 
 // Activations -> fp16 (row-major [M, K]); the tensor map reads this copy.
-__global__ void to_f16_kernel(const void* x, int dtype, int64_t n, __half* out) {
+// Eight values per thread and step (one 16-byte fp16 store; one 16-byte
+// bf16 or two fp32 loads), four steps' loads issued before their stores;
+// each value rounds to nearest even.  n8 = M*K/8 (K is a multiple of 256,
+// x is 16-byte aligned).
+__device__ __forceinline__ uint4 to_f16_8(const void* x, int dtype, int64_t i) {
+  float f[8];
+  if (dtype == DT_BF16) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(x) + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      f[2 * j] = __uint_as_float(w[j] << 16);
+      f[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  } else {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(x) + 2 * i);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(x) + 2 * i + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+  uint32_t h[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const __half2 p = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+    h[j] = *reinterpret_cast<const uint32_t*>(&p);
+  }
+  return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+__global__ void __launch_bounds__(256) to_f16_kernel(const void* x, int dtype, int64_t n8, uint4* out) {
   pdl_launch_dependents();
-  pdl_wait();
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = __float2half_rn(load_act(x, dtype, i));
+  pdl_wait();  // x is written by the preceding kernel; out may still be read by the previous matmul
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n8; i += 4 * stride) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) v[u] = to_f16_8(x, dtype, i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; u++) out[i + u * stride] = v[u];
+  }
+  for (; i < n8; i += stride) out[i] = to_f16_8(x, dtype, i);
 }
 
 // --------------------------------------------------------------------------
@@ -722,17 +812,19 @@ static cudaError_t qmm_launch_t(const QmmArgs& a, const QmmPlan& p, const CUtens
 // ws holds the plan's scratch (zero-filled once by the caller; the ticket
 // region is left zero-filled by every call).
 cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed, int64_t N, int64_t K, int64_t M,
-                       float* y, void* ws, int* err, cudaStream_t st, const char** why, const QmmGather* gather) {
+                       void* y, int y_dtype, void* ws, int* err, cudaStream_t st, const char** why,
+                       const QmmGather* gather) {
   const QmmPlan p = qmm_plan(t, N, K, M, x_dtype);
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   __half* x16 = reinterpret_cast<__half*>(wsb + p.off_x16);
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) { *why = "cuTensorMapEncodeTiled unavailable"; return cudaErrorNotSupported; }
   if (x_dtype != DT_F16) {
-    const int64_t n = M * K;
-    const int grid = (int)std::min<int64_t>((n + 255) / 256, 148 * 32);
-    to_f16_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, x16);
-    cudaError_t e = cudaGetLastError();
+    // about four 8-value steps per thread, at most 8 CTAs of 256 per SM
+    const int64_t n8 = M * K / 8;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n8 + 1023) / 1024, (int64_t)qmm_sm_count() * 8));
+    cudaError_t e = launch_pdl(to_f16_kernel, dim3((unsigned)grid), dim3(256), 0, st, x, x_dtype, n8,
+                               reinterpret_cast<uint4*>(x16));
     if (e != cudaSuccess) return e;
   } else {
     x16 = reinterpret_cast<__half*>(const_cast<void*>(x));
@@ -741,7 +833,7 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
   a.packed = packed; a.N = N; a.K = K; a.M = M;
   a.row_bytes = (K / QK) * block_bytes(t);
   a.packed_bytes = N * a.row_bytes;
-  a.y = y; a.err = err;
+  a.y = y; a.ydt = y_dtype; a.err = err;
   a.bn = p.bn; a.nacc = p.nacc; a.ksplit = p.ksplit; a.kbs = p.kbs;
   a.tickets = p.ksplit > 1 ? reinterpret_cast<unsigned*>(wsb) : nullptr;
   a.part = p.ksplit > 1 ? reinterpret_cast<float*>(wsb + p.off_part) : nullptr;
@@ -754,6 +846,7 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
     a.gflags[i] = nullptr;
   }
   a.mcy = nullptr;
+  a.yh = 0;
   a.gvec = 0;
   if (gather && gather->world > 1) {
     if (gather->world > QMM_GATHER_MAX || gather->rank < 0 || gather->rank >= gather->world) {
@@ -770,7 +863,9 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
       a.gy[i] = reinterpret_cast<float*>(r + 256);
     }
     if (gather->multicast) a.mcy = reinterpret_cast<float*>(static_cast<uint8_t*>(gather->multicast) + 256);
-    a.gvec = (gather->row0 % 4 == 0 && gather->ntot % 4 == 0) ? 1 : 0;
+    a.yh = y_dtype == DT_F16 ? 1 : 0;
+    const int piece = a.yh ? 8 : 4;  // rows per 16-byte piece
+    a.gvec = (gather->row0 % piece == 0 && gather->ntot % piece == 0) ? 1 : 0;
   }
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};

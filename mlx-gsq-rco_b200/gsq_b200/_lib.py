@@ -35,7 +35,7 @@ SIGNATURES = {
     "gsq_qmv_workspace_size": (_SZ, [_I, _I64, _I64, _I64]),
     "gsq_qmv": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, _P, _I, _P, _SZ, _P]),
     "gsq_qmm_workspace_size": (_SZ, [_I, _I64, _I64, _I64, _I]),
-    "gsq_qmm": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, _P, _P, _SZ, _P]),
+    "gsq_qmm": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, _P, _I, _P, _SZ, _P]),
     "gsq_embed": (_I, [_I, _P, _I64, _P, _I64, _I64, _P, _I, _P]),
     "gsq_device_status": (_I, [_P]),
     "gsq_qmv_noalloc": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, _P, _I, _P]),
@@ -46,12 +46,13 @@ SIGNATURES = {
     "gsq_ipc_import": (_I, [ctypes.c_char_p, ctypes.POINTER(_P)]),
     "gsq_ipc_close": (_I, [_P]),
     "gsq_qmv_gather": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _I, _I, _I64, _I64, _P, _SZ, _P]),
-    "gsq_qmm_gather": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _I, _I, _I64, _I64, _P, _SZ, _P]),
-    "gsq_qmm_gather_mc": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _P, _I, _I, _I64, _I64, _P, _SZ,
-                               _P]),
+    "gsq_qmm_gather": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _I, _I, _I64, _I64, _I, _P, _SZ,
+                            _P]),
+    "gsq_qmm_gather_mc": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, ctypes.POINTER(_P), _P, _I, _I, _I64, _I64, _I, _P,
+                               _SZ, _P]),
     # include/gsq_model.h: decoder-glue kernels of the model harness
     "gsq_rmsnorm": (_I, [_P, _P, _I64, _I64, _P, ctypes.c_float, _P, _I, _P]),
-    "gsq_silu_mul": (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),
+    "gsq_silu_mul": (_I, [_P, _I, _I64, _I64, _I64, _P, _I, _P]),
     "gsq_qmv_swiglu": (_I, [_I, _P, _I, _P, _I64, _I64, _I64, _P, _I, _P, _SZ, _P]),
     "gsq_gdn_scratch_bytes": (_SZ, [_I64, _I64, _I64]),
     "gsq_gdn": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P,

@@ -224,10 +224,13 @@ class _Packed:
             self.region.close()
             self.region = None
 
-    def __call__(self, x16: torch.Tensor) -> torch.Tensor:
+    def __call__(self, x16: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
+        """x16 @ W.T as fp32 rows (``out_dtype`` fp16: rounded once from the
+        fp32 sums, for prompts of 8 tokens and more; the tensor-parallel
+        prompt path then returns the type of the projection's region)."""
         if self.world == 1:
             return quantized_matvec(x16, self.data, qtype=self.qtype, out_features=self.n, in_features=self.k,
-                                    out_dtype=torch.float32)
+                                    out_dtype=out_dtype)
         if x16.shape[0] == 1:  # decode: the gather is fused into the matvec (every rank's rows, over NVLink)
             from ..parallel import quantized_matvec_gather
             return quantized_matvec_gather(x16, self.data, qtype=self.qtype, out_features=self.n_local,
@@ -239,7 +242,7 @@ class _Packed:
                                            in_features=self.k, region=reg, row0=self.row0)
         from ..parallel import gather_rows
         y = quantized_matvec(x16, self.data, qtype=self.qtype, out_features=self.n_local, in_features=self.k,
-                             out_dtype=torch.float32)
+                             out_dtype=out_dtype)
         return gather_rows(y, self.group)
 
     def swiglu(self, x16: torch.Tensor, out_dtype=torch.float16) -> torch.Tensor:
@@ -249,7 +252,10 @@ class _Packed:
             raise ValueError("swiglu needs the gate|up join interleaved in groups of 8")
         rows = x16.shape[0]
         if rows >= 8 or self.world > 1:
-            return silu_mul(self(x16), out_dtype, group=8)
+            # prompts: the gate|up values as fp16 (also what the gathered
+            # tensor-parallel matmul delivers), then the SwiGLU kernel in fp32
+            gu = self(x16, out_dtype=torch.float16 if rows >= 8 else torch.float32)
+            return silu_mul(gu, out_dtype, group=8)
         from ..quant.layouts import type_id
         dev = x16.device
         lib = _lib.load()
@@ -281,9 +287,11 @@ def rmsnorm(resid: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tenso
 
 def silu_mul(gu: torch.Tensor, out_dtype=torch.float16, group: int = 0) -> torch.Tensor:
     rows, n2 = gu.shape
+    if gu.stride(1) != 1 or gu.stride(0) != n2:
+        gu = gu.contiguous()
     out = torch.empty((rows, n2 // 2), dtype=out_dtype, device=gu.device)
-    _lib.check(_lib.load().gsq_silu_mul(gu.data_ptr(), rows, n2 // 2, group, out.data_ptr(),
-                                        _lib.DTYPE_CODES[out_dtype], _stream(gu.device)))
+    _lib.check(_lib.load().gsq_silu_mul(gu.data_ptr(), _lib.DTYPE_CODES[gu.dtype], rows, n2 // 2, group,
+                                        out.data_ptr(), _lib.DTYPE_CODES[out_dtype], _stream(gu.device)))
     return out
 
 
@@ -346,19 +354,29 @@ class Qwen35:
             for pk in self._projections():
                 pk.shard(group)
             # Prompts gather inside the matmul epilogue into one region per
-            # output width, shared by every projection of that width (the LM
-            # head only ever sees one row).  Sharing is safe because two calls
-            # of the same width always have another gathered call between
-            # them: no rank finishes that call before every rank's matmul has
-            # started storing, which each does only after the kernel that
-            # consumed the previous output of the width has completed.
+            # output width and value type, shared by every projection of that
+            # kind (the LM head only ever sees one row).  Sharing is safe
+            # because two calls on a region always have another gathered call
+            # between them: no rank finishes that call before every rank's
+            # matmul has started storing, which each does only after the
+            # kernel that consumed the previous output of the region has
+            # completed.  The FFN's gate|up outputs (the widest, read only by
+            # the SwiGLU kernel, which computes in fp32 from any input type)
+            # gather as fp16: half the NVLink bytes of the largest gather;
+            # every other projection's output stays fp32 (a gate|up width may
+            # equal another projection's, so the type is part of the key).
             from ..parallel import GatherRegion
-            widths = sorted({pk.n for pk in self._projections() if pk is not self.lm_head})
-            for n in widths:
-                self._prefill_regions[n] = GatherRegion(max_len, n, group=group, device=self.dev)
+
+            def kind(pk):
+                fp16 = any(pk is L["gate_up"] for L in self.layers)
+                return pk.n, torch.float16 if fp16 else torch.float32
+
+            for key in sorted({kind(pk) for pk in self._projections() if pk is not self.lm_head}, key=str):
+                self._prefill_regions[key] = GatherRegion(max_len, key[0], group=group, device=self.dev,
+                                                          dtype=key[1])
             for pk in self._projections():
                 if pk is not self.lm_head:
-                    pk.prefill_region = self._prefill_regions[pk.n]
+                    pk.prefill_region = self._prefill_regions[kind(pk)]
         self.pos = torch.zeros(1, dtype=torch.int32, device=self.dev)   # next position (decode)
         self.cur_id = torch.zeros(max_batch, dtype=torch.int32, device=self.dev)  # tokens to feed next (decode)
         self.n_pos = 0  # host copy of the position (prefill bookkeeping)

@@ -12,7 +12,8 @@ other's delivered tiles.
 
 A :class:`GatherRegion` is the per-call-site buffer behind both: every rank
 allocates ``gsq_gather_region_bytes(rows, ntot)`` bytes (256 bytes of control
-words, then fp32 ``rows x ntot``, then for fewer than 8 rows the matvec's
+words, then ``rows x ntot`` values -- fp32, or fp16 for a matmul region made
+with ``dtype=torch.float16`` -- then for fewer than 8 rows the matvec's
 inbox), exports a CUDA IPC handle, and maps its peers' regions.  Every rank
 must make the same sequence of calls on a region, and a region serves one
 call site: its rows stay valid until any rank runs the same site again (that
@@ -35,20 +36,29 @@ from ..quant.layouts import type_id as _type_id
 class _DeviceArray:
     """__cuda_array_interface__ view of library-owned device memory."""
 
-    def __init__(self, ptr: int, shape: tuple[int, ...]):
-        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (ptr, False), "version": 3,
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3,
                                          "strides": None}
 
 
 class GatherRegion:
     """One projection call site's gathered output on every rank of ``group``.
 
-    ``y`` is this rank's copy, a ``rows x ntot`` fp32 tensor (a view of the
-    region; ``gsq_qmv_gather`` fills all of it).
+    ``y`` is this rank's copy, a ``rows x ntot`` tensor of ``dtype`` (a view
+    of the region; ``gsq_qmv_gather`` fills all of it).  ``dtype`` is fp32, or
+    fp16 for a matmul (prefill) region: the epilogue rounds each value to
+    nearest even and half the bytes cross NVLink.  ``multicast`` places a
+    region of 8 rows and more in symmetric memory behind an NVSwitch multicast
+    address when every rank has one (one store per value, delivered to every
+    rank by the switch, this one included).  Off by default (``GSQ_MULTICAST=1``
+    turns it on): a multicast store also comes back over this GPU's own link,
+    so every rank receives all of the output instead of the (P-1)/P that
+    peer stores deliver; on 2 GPUs the peer stores were 20-25 us faster per
+    17408 x 512 output.
     """
 
     def __init__(self, rows: int, ntot: int, group=None, device: torch.device | None = None,
-                 multicast: bool | None = None):
+                 multicast: bool | None = None, dtype: torch.dtype = torch.float32):
         if not dist.is_initialized():
             raise RuntimeError("GatherRegion needs an initialised process group")
         self.group = group
@@ -57,6 +67,12 @@ class GatherRegion:
         if not 2 <= self.world <= 8:
             raise ValueError("the fused gather supports 2 to 8 ranks")
         self.rows, self.ntot = int(rows), int(ntot)
+        if dtype not in (torch.float32, torch.float16):
+            raise ValueError("a gather region holds fp32 or fp16 values")
+        if dtype != torch.float32 and self.rows < 8:
+            raise ValueError("fp16 regions serve the matmul gather (8 rows and more)")
+        self.dtype = dtype
+        self._typestr = "<f4" if dtype == torch.float32 else "<f2"
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         lib = _lib.load()
         nbytes = lib.gsq_gather_region_bytes(self.rows, self.ntot)
@@ -66,7 +82,7 @@ class GatherRegion:
         self._symm = None
         self._imported = []
         if multicast is None:
-            multicast = self.rows >= 8 and os.environ.get("GSQ_MULTICAST", "1") != "0"
+            multicast = self.rows >= 8 and os.environ.get("GSQ_MULTICAST", "0") == "1"
         if multicast and self._symmetric(nbytes):
             return
         with torch.cuda.device(self.device):
@@ -87,7 +103,8 @@ class GatherRegion:
                 ptrs.append(peer.value)
                 self._imported.append(peer.value)
         self.regions = (ctypes.c_void_p * self.world)(*ptrs)
-        self.y = torch.as_tensor(_DeviceArray(self._own + 256, (self.rows, self.ntot)), device=self.device)
+        self.y = torch.as_tensor(_DeviceArray(self._own + 256, (self.rows, self.ntot), self._typestr),
+                                 device=self.device)
 
     def _symmetric(self, nbytes: int) -> bool:
         """Regions in torch symmetric memory, mapped on every rank and, where
@@ -125,7 +142,8 @@ class GatherRegion:
         self.mc = mc
         self._own = ptrs[self.rank]
         self.regions = (ctypes.c_void_p * self.world)(*ptrs)
-        self.y = torch.as_tensor(_DeviceArray(self._own + 256, (self.rows, self.ntot)), device=self.device)
+        self.y = torch.as_tensor(_DeviceArray(self._own + 256, (self.rows, self.ntot), self._typestr),
+                                 device=self.device)
         return True
 
     def close(self) -> None:
@@ -158,6 +176,8 @@ def quantized_matvec_gather(x: torch.Tensor, packed_shard: torch.Tensor, *, qtyp
     rows = x.numel() // in_features
     if rows != region.rows:
         raise ValueError(f"x has {rows} rows, the region {region.rows}")
+    if region.dtype != torch.float32:
+        raise ValueError("the matvec gathers into fp32 regions")
     flat = x.reshape(rows, in_features).contiguous()
     if flat.data_ptr() % 16:
         flat = flat.clone()
@@ -179,8 +199,9 @@ def quantized_matmul_gather(x: torch.Tensor, packed_shard: torch.Tensor, *, qtyp
     of a row-split projection with the gather fused into its epilogue
     (``gsq_qmm_gather``): every output tile goes into every rank's region over
     NVLink as it is written.  Returns the first ``rows`` rows of the region's
-    fp32 output (a region of R rows serves calls of up to R rows), complete
-    once the call finishes on the current stream."""
+    output (fp32 or fp16, the region's dtype; a region of R rows serves calls
+    of up to R rows), complete once the call finishes on the current
+    stream."""
     tid = _type_id(qtype)
     dev = _lib.require_cuda(x, packed_shard)
     rows = x.numel() // in_features
@@ -195,13 +216,14 @@ def quantized_matmul_gather(x: torch.Tensor, packed_shard: torch.Tensor, *, qtyp
     need = lib.gsq_qmm_workspace_size(tid, out_features, in_features, rows, xcode)
     ws = _lib.workspaces.get(dev, need, "qmm")
     wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+    ycode = _lib.DTYPE_CODES[region.dtype]
     if region.mc:  # one multicast store per value through the NVSwitch
         code = lib.gsq_qmm_gather_mc(tid, flat.data_ptr(), xcode, pk.data_ptr(), out_features, in_features, rows,
-                                     region.regions, region.mc, region.world, region.rank, row0, region.ntot, wsp, wsn,
-                                     _lib.stream_ptr(dev))
+                                     region.regions, region.mc, region.world, region.rank, row0, region.ntot, ycode,
+                                     wsp, wsn, _lib.stream_ptr(dev))
     else:
         code = lib.gsq_qmm_gather(tid, flat.data_ptr(), xcode, pk.data_ptr(), out_features, in_features, rows,
-                                  region.regions, region.world, region.rank, row0, region.ntot, wsp, wsn,
+                                  region.regions, region.world, region.rank, row0, region.ntot, ycode, wsp, wsn,
                                   _lib.stream_ptr(dev))
     _lib.check(code)
     return region.y[:rows]

@@ -41,16 +41,16 @@ def quantized_matmul(x: torch.Tensor, packed: torch.Tensor, *, qtype: str, out_f
     if flat.data_ptr() % 16:
         flat = flat.clone()  # TMA / vector loads need 16-byte alignment
     pk = packed.reshape(-1).contiguous()
-    y = torch.empty((rows, out_features), dtype=torch.float32, device=dev)
+    out_dtype = out_dtype or x.dtype
+    if out_dtype not in _lib.DTYPE_CODES:
+        raise TypeError(f"unsupported output dtype {out_dtype}")
+    y = torch.empty((rows, out_features), dtype=out_dtype, device=dev)  # rounded once from the fp32 sums
     lib = _lib.load()
     xcode = _lib.DTYPE_CODES[flat.dtype]
     need = lib.gsq_qmm_workspace_size(type_id, out_features, in_features, rows, xcode)
     ws = _lib.workspaces.get(dev, need, "qmm")
     code = lib.gsq_qmm(type_id, flat.data_ptr(), xcode, pk.data_ptr(), out_features, in_features, rows,
-                       y.data_ptr(), ws.data_ptr() if ws is not None else None,
+                       y.data_ptr(), _lib.DTYPE_CODES[out_dtype], ws.data_ptr() if ws is not None else None,
                        ws.numel() if ws is not None else 0, _lib.stream_ptr(dev))
     _lib.check(code)
-    out_dtype = out_dtype or x.dtype
-    if out_dtype != torch.float32:
-        y = y.to(out_dtype)
     return y.reshape(*original, out_features)

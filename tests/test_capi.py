@@ -60,8 +60,9 @@ def test_validation_errors_before_any_launch():
     need = lib.gsq_qmv_workspace_size(q4k, 5120, 5120, 1)
     assert need > 0
     assert lib.gsq_qmv(q4k, fake, 1, fake, 5120, 5120, 1, fake, 0, None, 0, None) == _lib.GSQ_ERR_WORKSPACE
-    assert lib.gsq_qmm(q4k, fake, 2, fake, 16, 256, 4, fake, None, 0, None) == _lib.GSQ_ERR_WORKSPACE
-    assert lib.gsq_qmm(q4k, ctypes.c_void_p((1 << 20) + 4), 1, fake, 16, 256, 4, fake, None, 0, None) \
+    assert lib.gsq_qmm(q4k, fake, 2, fake, 16, 256, 4, fake, 0, None, 0, None) == _lib.GSQ_ERR_WORKSPACE
+    assert lib.gsq_qmm(q4k, fake, 2, fake, 16, 256, 4, fake, 7, None, 0, None) == _lib.GSQ_ERR_ARG  # y dtype
+    assert lib.gsq_qmm(q4k, ctypes.c_void_p((1 << 20) + 4), 1, fake, 16, 256, 4, fake, 0, None, 0, None) \
         == _lib.GSQ_ERR_ALIGN
     assert lib.gsq_embed(q4k, fake, 3, fake, 10, 100, fake, 1, None) == _lib.GSQ_ERR_SIZE
     assert lib.gsq_dequant(99, fake, 1, fake, None) == _lib.GSQ_ERR_QTYPE
@@ -101,10 +102,14 @@ def test_gather_entry_points_validate_before_any_launch():
     assert qmv_gather(two, 2, 1, row0=384) == _lib.GSQ_ERR_SIZE  # rows [384, 640) outside 512
     assert qmv_gather(two, 2, 0, xdt=7) == _lib.GSQ_ERR_ARG
 
-    def qmm_gather(regions, world, rank, m=64, row0=0, ntot=512):
-        return lib.gsq_qmm_gather(q4k, fake, 1, fake, 256, 256, m, regions, world, rank, row0, ntot, None, 0, None)
+    def qmm_gather(regions, world, rank, m=64, row0=0, ntot=512, ydt=0):
+        return lib.gsq_qmm_gather(q4k, fake, 1, fake, 256, 256, m, regions, world, rank, row0, ntot, ydt, None, 0,
+                                  None)
 
     assert qmm_gather(two, 9, 0) == _lib.GSQ_ERR_ARG
+    assert qmm_gather(two, 2, 0, ydt=2) == _lib.GSQ_ERR_ARG  # gathered values are fp32 or fp16
+    assert lib.gsq_qmm_gather_mc(q4k, fake, 1, fake, 256, 256, 64, two, None, 2, 0, 0, 512, 0, None, 0,
+                                 None) == _lib.GSQ_ERR_ARG  # no multicast address
     assert qmm_gather(odd, 2, 0) == _lib.GSQ_ERR_ALIGN
     assert qmm_gather(two, 2, 0, m=0) == _lib.GSQ_ERR_SIZE
     assert qmm_gather(two, 2, 0, ntot=128) == _lib.GSQ_ERR_SIZE

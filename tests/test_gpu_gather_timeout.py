@@ -60,10 +60,13 @@ def _run(kind):
         need = lib.gsq_qmm_workspace_size(tid, n // 2, k, rows, xcode)
     ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=dev)
     lib.gsq_device_status(None)  # clear any earlier status
-    fn = lib.gsq_qmv_gather if kind == "qmv" else lib.gsq_qmm_gather
     t0 = time.time()
-    code = fn(tid, x.data_ptr(), xcode, shard.data_ptr(), n // 2, k, rows, regions, 2, 0, 0, n, ws.data_ptr(),
-              ws.numel(), None)
+    if kind == "qmv":
+        code = lib.gsq_qmv_gather(tid, x.data_ptr(), xcode, shard.data_ptr(), n // 2, k, rows, regions, 2, 0, 0, n,
+                                  ws.data_ptr(), ws.numel(), None)
+    else:
+        code = lib.gsq_qmm_gather(tid, x.data_ptr(), xcode, shard.data_ptr(), n // 2, k, rows, regions, 2, 0, 0, n,
+                                  _lib.DTYPE_CODES[torch.float32], ws.data_ptr(), ws.numel(), None)
     assert code == _lib.GSQ_OK, _lib.last_error()
     status = lib.gsq_device_status(None)
     elapsed = time.time() - t0

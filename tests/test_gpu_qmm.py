@@ -68,6 +68,22 @@ def test_qmm_config3(qtype, nk, m):
     assert rel_l2(y.cpu(), exp.cpu()) <= REL_L2
 
 
+@pytest.mark.parametrize("m,nk", [(40, (640, 17408)), (600, (2048, 5120)), (12, (1000, 2048))])
+def test_qmm_output_types_round_the_fp32_sums(m, nk):
+    """fp16 and bf16 outputs are the fp32 result rounded once to nearest even
+    (split-K and whole-K tiles, a ragged last row tile); by default the
+    output has x's dtype, as the reference's quantized_matmul returns."""
+    n, k = nk
+    w = random_matrix_torch("IQ4_XS", n, k, seed=n)
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    y32 = quantized_matmul(x, w, qtype="IQ4_XS", out_features=n, in_features=k, out_dtype=torch.float32)
+    for dt in (torch.float16, torch.bfloat16):
+        y = quantized_matmul(x, w, qtype="IQ4_XS", out_features=n, in_features=k, out_dtype=dt)
+        assert y.dtype == dt
+        assert torch.equal(y, y32.to(dt))
+    assert quantized_matmul(x, w, qtype="IQ4_XS", out_features=n, in_features=k).dtype == torch.bfloat16
+
+
 def test_qmm_split_k_deterministic():
     """Shapes with few row tiles split K over several CTAs; the partial tiles
     are summed in split order, so repeated calls agree bit for bit."""

@@ -100,11 +100,15 @@ def _worker(rank, world, port, q):
         # Both ways of delivering the tiles: one multicast store per value
         # through the NVSwitch (symmetric-memory regions, where the GPUs
         # offer it) and one store per rank over NVLink.
+        # fp16 regions too (16-byte pieces of 8 rows; 1000 rows: shards whose
+        # first row is not a multiple of 8 take the per-value path).
         for multicast in (True, False):
-            for qtype, n2, k2 in (("IQ4_XS", 2048, 5120), ("Q6_K", 1024, 17408)):
+            for qtype, n2, k2, ydt in (("IQ4_XS", 2048, 5120, torch.float32), ("IQ4_XS", 2048, 5120, torch.float16),
+                                       ("Q6_K", 1024, 17408, torch.float32), ("Q6_K", 1024, 17408, torch.float16),
+                                       ("Q4_K", 1000, 2048, torch.float16)):
                 packed2 = random_matrix_torch(qtype, n2, k2, seed=6, device=dev)
                 shard2 = shard_packed(packed2, qtype, n2, k2, world, rank)
-                region2 = GatherRegion(64, n2, multicast=multicast)
+                region2 = GatherRegion(64, n2, multicast=multicast, dtype=ydt)
                 if not multicast and region2.mc is not None:
                     fails.append("multicast region without asking")
                 for it in range(3):
@@ -114,7 +118,9 @@ def _worker(rank, world, port, q):
                                             out_dtype=torch.float32)
                     y2 = quantized_matmul_gather(x2, shard2, qtype=qtype, out_features=n2 // world, in_features=k2,
                                                  region=region2, row0=rank * (n2 // world))
-                    check(f"matmul gather mc={multicast} {qtype} it {it}", y2, ref2)
+                    if y2.dtype != ydt:
+                        fails.append(f"region dtype {y2.dtype}")
+                    check(f"matmul gather mc={multicast} {qtype} {ydt} N={n2} it {it}", y2, ref2)
                     # The next call on this region stores into every rank's copy: no rank
                     # may start it before every rank has read this call's rows.
                     dist.barrier()
@@ -187,24 +193,29 @@ def _model_worker(rank, world, port, q):
         one = build_qwen35(w, cfg, dev, max_len=64)
         tp = build_qwen35(w, cfg, dev, max_len=64, group=dist.group.WORLD)
 
-        def rel(a, b):
-            return float((a.float() - b.float()).norm() / b.float().norm())
+        fails = []
 
-        ok = True
+        def check(label, a, b, tol=1e-3):
+            """Every check runs on every rank (the calls inside are collective)."""
+            e = float((a.float() - b.float()).norm() / b.float().norm())
+            if not e <= tol:
+                fails.append(f"{label}: {e:.3g}")
+
         prompt = (torch.arange(12, dtype=torch.int32, device=dev) * 41) % cfg.vocab_size
-        ok = ok and rel(tp.prefill(prompt), one.prefill(prompt)) <= 1e-3  # matmul, gather in the epilogue
+        check("prefill 12", tp.prefill(prompt), one.prefill(prompt))  # matmul, gather in the epilogue
         long_prompt = (torch.arange(40, dtype=torch.int32, device=dev) * 17) % cfg.vocab_size
-        ok = ok and rel(tp.prefill(long_prompt), one.prefill(long_prompt)) <= 1e-3  # the same regions, more tokens
-        ok = ok and rel(tp.prefill(prompt), one.prefill(prompt)) <= 1e-3
+        check("prefill 40", tp.prefill(long_prompt), one.prefill(long_prompt))  # the same regions, more tokens
+        check("prefill 12 again", tp.prefill(prompt), one.prefill(prompt))
         for t in (5, 77, 300):  # eager decode: the fused-gather matvec
-            ok = ok and rel(tp.decode_step(t), one.decode_step(t)) <= 1e-3
+            check(f"decode {t}", tp.decode_step(t), one.decode_step(t))
         tp.capture_decode()
         one.capture_decode()
-        for _ in range(3):  # graph decode, greedy: both must follow the same tokens
+        for i in range(3):  # graph decode, greedy: both must follow the same tokens
             tp.replay_decode(1)
             one.replay_decode(1)
-            ok = ok and rel(tp.graph_logits, one.graph_logits) <= 1e-3
-            ok = ok and int(tp.cur_id.item()) == int(one.cur_id.item())
+            check(f"graph step {i}", tp.graph_logits, one.graph_logits)
+            if int(tp.cur_id.item()) != int(one.cur_id.item()):
+                fails.append(f"graph step {i}: tokens differ")
         # batched decode (9 sequences: the projections run the matmul with
         # the gather fused into its epilogue; the LM head an NCCL all-gather)
         tp.release_graph()
@@ -215,13 +226,15 @@ def _model_worker(rank, world, port, q):
         for m in (tpb, oneb):
             m.prefill(prompt)
             m.fork(9)
-        ok = ok and rel(tpb.decode_step(toks), oneb.decode_step(toks)) <= 1e-3
-        ok = ok and rel(tpb.decode_step(toks), oneb.decode_step(toks)) <= 1e-3
+        check("batched decode 1", tpb.decode_step(toks), oneb.decode_step(toks))
+        check("batched decode 2", tpb.decode_step(toks), oneb.decode_step(toks))
         torch.cuda.synchronize()
-        ok = ok and _lib.load().gsq_device_status(None) == 0
+        status = _lib.load().gsq_device_status(None)
+        if status:
+            fails.append(f"device status {status}")
         tpb.close()
         tp.close()
-        q.put((rank, ok, []))
+        q.put((rank, not fails, fails))
     finally:
         dist.destroy_process_group()
 

@@ -74,8 +74,9 @@ def test_glue_abi_validation():
     fake = 1 << 20  # never dereferenced: every call fails validation first
     assert lib.gsq_rmsnorm(None, None, 1, 16, fake, 1e-6, fake, 1, None) == _lib.GSQ_ERR_ARG
     assert lib.gsq_rmsnorm(fake, None, 1, 16, fake, 1e-6, fake, 9, None) == _lib.GSQ_ERR_ARG
-    assert lib.gsq_silu_mul(fake, 1, 0, 0, fake, 1, None) == _lib.GSQ_ERR_SIZE
-    assert lib.gsq_silu_mul(fake, 1, 12, 8, fake, 1, None) == _lib.GSQ_ERR_SIZE  # n not a multiple of the group
+    assert lib.gsq_silu_mul(fake, 0, 1, 0, 0, fake, 1, None) == _lib.GSQ_ERR_SIZE
+    assert lib.gsq_silu_mul(fake, 0, 1, 12, 8, fake, 1, None) == _lib.GSQ_ERR_SIZE  # n not a multiple of the group
+    assert lib.gsq_silu_mul(fake, 5, 1, 16, 8, fake, 1, None) == _lib.GSQ_ERR_ARG   # input dtype
     q4k = 12
     assert lib.gsq_qmv_swiglu(q4k, fake, 1, fake, 12, 256, 1, fake, 1, None, 0, None) == _lib.GSQ_ERR_SIZE
     assert lib.gsq_qmv_swiglu(q4k, fake, 1, fake, 16, 256, 8, fake, 1, None, 0, None) == _lib.GSQ_ERR_SIZE
