@@ -73,8 +73,10 @@ cudaError_t embed_launch(int t, const int32_t* ids, int64_t n, const uint8_t* pa
 // token groups x K splits, and the scratch layout.
 struct QmmPlan {
   int bn, nacc;              // MMA N per accumulator (<= 256), accumulators per CTA (1 or 2)
-  int ksplit, kbs;           // K splits, 256-blocks per split
+  int ksplit, kbs;           // K splits, 256-blocks per split (of the split launch)
   int64_t row_tiles, token_groups;
+  int64_t whole_tiles;       // > 0: a first launch of whole-K tiles [0, whole_tiles) in full waves,
+                             // then the remaining tiles with K split ksplit ways
   size_t off_part, off_x16;  // scratch layout: tickets at 0, partial tiles, fp16 activations
   size_t workspace;          // scratch bytes
 };

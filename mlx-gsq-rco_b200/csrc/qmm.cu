@@ -85,6 +85,8 @@ struct QmmArgs {
   unsigned* tickets;  // [row tiles x token groups] (ksplit > 1)
   int bn, nacc;       // MMA N per accumulator, accumulators per CTA
   int ksplit, kbs;    // K splits, 256-blocks per split
+  int64_t tile0;      // tile of CTA (0, 0): tiles are numbered row tile fastest
+  int64_t row_tiles;
   int* err;
   // Fused row gather (world > 1, gsq_qmm_gather): output rows
   // [row0, row0 + N) of ntot go to every rank's region ([M][ntot] fp32, or
@@ -346,8 +348,11 @@ __global__ void __launch_bounds__(QMM_THREADS, 1) qmm_kernel(const QmmArgs a, co
   unsigned* last_flag = reinterpret_cast<unsigned*>(bars + 22);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n0 = (int64_t)blockIdx.x * QMM_BM;
-  const int m0 = blockIdx.y * ttok;
+  // This CTA's output tile: row tile fastest over the whole call; a launch
+  // covers tiles [tile0, tile0 + gridDim.x * gridDim.y).
+  const int64_t tile_id = a.tile0 + (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+  const int64_t n0 = (tile_id % a.row_tiles) * QMM_BM;
+  const int m0 = (int)(tile_id / a.row_tiles) * ttok;
   const int split = blockIdx.z;
   const int kb0 = split * a.kbs;                                  // this CTA's 256-blocks
   const int nkb = min(a.kbs, (int)(a.K / QK) - kb0);
@@ -765,16 +770,29 @@ QmmPlan qmm_plan(int t, int64_t N, int64_t K, int64_t M, int x_dtype) {
   const int nkb = (int)(K / QK);
   const int sms = qmm_sm_count();
   p.ksplit = 1;
-  if (ctas * 4 < (int64_t)sms * 3 && ctas <= QMM_TICKETS)
+  p.whole_tiles = 0;
+  int64_t split_tiles = ctas;  // tiles whose K is split (their partials live in the scratch)
+  if (ctas * 4 < (int64_t)sms * 3 && ctas <= QMM_TICKETS) {
     p.ksplit = (int)std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(nkb, QMM_KSPLIT_MAX), sms / ctas));
+  } else if (ctas > sms && ctas % sms != 0 && (ctas % sms) * 2 <= sms) {
+    // A last wave at most half full: its tiles split K over the idle SMs.
+    const int64_t tail = ctas % sms;
+    const int s = (int)std::min<int64_t>(std::min<int64_t>(nkb, QMM_KSPLIT_MAX), sms / tail);
+    if (s >= 2) {
+      p.whole_tiles = ctas - tail;
+      p.ksplit = s;
+      split_tiles = tail;
+    }
+  }
   p.kbs = (nkb + p.ksplit - 1) / p.ksplit;
   p.ksplit = (nkb + p.kbs - 1) / p.kbs;
+  if (p.ksplit == 1) p.whole_tiles = 0;
   // Nothing but tickets is ever written to [0, QMM_TICKET_BYTES), whatever
   // the shape, so a workspace zero-filled once keeps zero tickets.
   size_t off = QMM_TICKET_BYTES;
   if (p.ksplit > 1) {
     p.off_part = off;
-    off += align256((size_t)ctas * p.ksplit * ttok * QMM_BM * sizeof(float));
+    off += align256((size_t)split_tiles * p.ksplit * ttok * QMM_BM * sizeof(float));
   }
   p.off_x16 = off;
   if (x_dtype != DT_F16) off += align256((size_t)M * K * 2);
@@ -798,8 +816,24 @@ static cudaError_t qmm_launch_g(const QmmArgs& a, const QmmPlan& p, const CUtens
     if (e != cudaSuccess) return e;
     configured[dev] = (int)smem;
   }
-  dim3 grid((unsigned)p.row_tiles, (unsigned)p.token_groups, (unsigned)p.ksplit);
-  return launch_pdl(qmm_kernel<T, GATHER>, grid, dim3(QMM_THREADS), smem, st, a, map);
+  if (p.whole_tiles == 0) {
+    const dim3 grid((unsigned)p.row_tiles, (unsigned)p.token_groups, (unsigned)p.ksplit);
+    return launch_pdl(qmm_kernel<T, GATHER>, grid, dim3(QMM_THREADS), smem, st, a, map);
+  }
+  // Full waves of whole-K tiles, then the last wave's tiles split along K
+  // (every split CTA of that launch fits on the GPU at once).
+  QmmArgs w = a;
+  w.ksplit = 1;
+  w.kbs = (int)(a.K / QK);
+  w.tile0 = 0;
+  cudaError_t e = launch_pdl(qmm_kernel<T, GATHER>, dim3((unsigned)p.whole_tiles, 1, 1), dim3(QMM_THREADS), smem,
+                             st, w, map);
+  if (e != cudaSuccess) return e;
+  QmmArgs s = a;
+  s.tile0 = p.whole_tiles;
+  const int64_t rest = p.row_tiles * p.token_groups - p.whole_tiles;
+  return launch_pdl(qmm_kernel<T, GATHER>, dim3((unsigned)rest, 1, (unsigned)p.ksplit), dim3(QMM_THREADS), smem, st,
+                    s, map);
 }
 
 template <int T>
@@ -836,6 +870,8 @@ cudaError_t qmm_launch(int t, const void* x, int x_dtype, const uint8_t* packed,
   a.y = y; a.ydt = y_dtype; a.err = err;
   a.bn = p.bn; a.nacc = p.nacc; a.ksplit = p.ksplit; a.kbs = p.kbs;
   a.tickets = p.ksplit > 1 ? reinterpret_cast<unsigned*>(wsb) : nullptr;
+  a.tile0 = 0;
+  a.row_tiles = p.row_tiles;
   a.part = p.ksplit > 1 ? reinterpret_cast<float*>(wsb + p.off_part) : nullptr;
   a.world = 0;
   a.rank = 0;

@@ -84,6 +84,23 @@ def test_qmm_output_types_round_the_fp32_sums(m, nk):
     assert quantized_matmul(x, w, qtype="IQ4_XS", out_features=n, in_features=k).dtype == torch.bfloat16
 
 
+@pytest.mark.parametrize("n,k,m", [(5120, 2048, 2048), (2560, 5120, 4096), (17408, 512, 2048)])
+def test_qmm_last_wave_split(n, k, m):
+    """More tiles than SMs with a last wave at most half full (160 tiles of
+    128 rows x 512 tokens on 148 SMs): full waves of whole-K tiles, then the
+    remaining tiles with K split over the idle SMs; 17408 x 2048 tokens (544
+    tiles, a last wave of 100) stays one launch.  Against float64, and
+    repeated calls agree bit for bit."""
+    packed = random_packed_gpu("IQ4_XS", n, k, seed=n + m)
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16, generator=torch.Generator(device="cuda").manual_seed(4))
+    y = quantized_matmul(x, packed, qtype="IQ4_XS", out_features=n, in_features=k, out_dtype=torch.float32)
+    y2 = quantized_matmul(x, packed, qtype="IQ4_XS", out_features=n, in_features=k, out_dtype=torch.float32)
+    exp = x.double() @ dense_gpu(packed, "IQ4_XS", n, k).T
+    assert rel_l2(y.cpu(), exp.cpu()) <= REL_L2
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+
+
 def test_qmm_split_k_deterministic():
     """Shapes with few row tiles split K over several CTAs; the partial tiles
     are summed in split order, so repeated calls agree bit for bit."""

@@ -125,6 +125,23 @@ def _worker(rank, world, port, q):
                     # may start it before every rank has read this call's rows.
                     dist.barrier()
                 region2.close()
+            # A 2048-token call whose shard has more tiles than SMs (2 ranks:
+            # 5120 rows x 4 token groups = 160 tiles): full waves, then the last
+            # wave's tiles with K split, each launch gathering its tiles.
+            if world == 2:
+                n4, k4 = 10240, 512
+                packed4 = random_matrix_torch("IQ4_XS", n4, k4, seed=9, device=dev)
+                shard4 = shard_packed(packed4, "IQ4_XS", n4, k4, world, rank)
+                region4 = GatherRegion(2048, n4, multicast=multicast, dtype=torch.float16)
+                x4 = torch.randn(2048, k4, device=dev, dtype=torch.bfloat16,
+                                 generator=torch.Generator(device=dev).manual_seed(30))
+                ref4 = quantized_matmul(x4, packed4, qtype="IQ4_XS", out_features=n4, in_features=k4,
+                                        out_dtype=torch.float32)
+                y4 = quantized_matmul_gather(x4, shard4, qtype="IQ4_XS", out_features=n4 // world, in_features=k4,
+                                             region=region4, row0=rank * (n4 // world))
+                check(f"last-wave split mc={multicast}", y4, ref4)
+                dist.barrier()
+                region4.close()
             # One region shared by calls of different token counts (one and
             # several 512-token groups, as a model's prefill region sees).
             n3, k3 = 1024, 5120
