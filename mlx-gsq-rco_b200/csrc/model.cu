@@ -64,6 +64,21 @@ __device__ float block_sum(float v, float* red) {
   return s;
 }
 
+// Thread-block cluster barrier (all threads of every CTA of the cluster;
+// release / acquire order the shared-memory writes before it).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// A float in the shared memory of CTA `rank` of this cluster, at the address
+// `p` has in this CTA.
+__device__ __forceinline__ float ld_shared_cluster_f32(const float* p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
 __device__ float block_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -416,20 +431,29 @@ __global__ void __launch_bounds__(GDN_D) gdn_scan_kernel(GdnArgs a) {
   }
 }
 
-// One token (T == 1) of the whole block in one launch: CTA = value head h,
-// 256 threads.  Threads 0..127 take the q channels of key head h % nk and
-// the v channels of h, threads 128..255 the k channels; all 256 form the
-// gate dot products; then thread (j = tid / 2, r = tid % 2) applies the
-// recurrence to column j, key indices 64r..64r+63, held in registers; the
-// gated norm closes the head.  The conv window slot of this position is
-// written by the CTAs that own the channels (q/k: h < nk) and is not read by
-// any CTA at this position.  Batched decode: blockIdx.y is the sequence b of
-// the batch, whose token is row b of proj / x / ab, whose conv ring and
-// state follow the previous sequence's (4*C and nv*128*128 floats), and whose
-// output is row b of out; every sequence is at position *pos.
+// One token (T == 1) of the whole block in one launch: a cluster of
+// GDN_DEC_SPLIT CTAs per value head h, 256 threads each.  Every CTA of the
+// cluster forms the q and k channels of key head h % nk (threads 0..127 q,
+// 128..255 k: conv, then the rms norms) and the two gate dot products; CTA
+// rank c owns value columns 32c .. 32c + 31: thread (col = tid / 8,
+// seg = tid % 8) holds column 32c + col at key indices seg, seg + 8, ...,
+// seg + 120 in registers and applies the recurrence (8-lane shuffle
+// reductions).  The gated norm needs the sum of y^2 over the head's 128
+// columns: each CTA posts its columns' sum in shared memory and reads the
+// others' through the cluster's distributed shared memory.  The conv window
+// slot of this position is written by rank 0 of the clusters that own the
+// channels (q/k: h < nk) and is not read by any CTA at this position.
+// Batched decode: blockIdx.y is the sequence b of the batch, whose token is
+// row b of proj / x / ab, whose conv ring and state follow the previous
+// sequence's (4*C and nv*128*128 floats), and whose output is row b of out;
+// every sequence is at position *pos.
+constexpr int GDN_DEC_SPLIT = 4;
+constexpr int GDN_DEC_COLS = GDN_D / GDN_DEC_SPLIT;
+
 __global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(const GdnArgs a0) {
   __shared__ float red[32];
-  __shared__ float qs[GDN_D], ks[GDN_D], vs[GDN_D];
+  __shared__ float qs[GDN_D], ks[GDN_D], vs[GDN_DEC_COLS];
+  __shared__ float part_ss;
   pdl_launch_dependents();
   pdl_wait();
   const int64_t seq = blockIdx.y;
@@ -440,13 +464,15 @@ __global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(const GdnArgs a0)
   a.conv_state = a0.conv_state + seq * 4 * a0.C;
   a.state = a0.state + seq * a0.nv * GDN_D * GDN_D;
   const int64_t obase = seq * a0.nv * GDN_D;
-  const int h = blockIdx.x, kh = h % a.nk, tid = threadIdx.x, warp = tid >> 5;
+  const int crank = blockIdx.x % GDN_DEC_SPLIT;  // == %cluster_ctarank (cluster dims GDN_DEC_SPLIT x 1 x 1)
+  const int h = blockIdx.x / GDN_DEC_SPLIT, kh = h % a.nk, tid = threadIdx.x, warp = tid >> 5;
   const int pos = *a.pos;
   const int i = tid & (GDN_D - 1);
   const int cqk = (tid < GDN_D ? 0 : a.nk * GDN_D) + kh * GDN_D + i;
-  const int cv = 2 * a.nk * GDN_D + h * GDN_D + i;
+  const int col0 = crank * GDN_DEC_COLS;
+  const int cv = 2 * a.nk * GDN_D + h * GDN_D + col0 + tid;  // threads 0..31: this CTA's v channels
   const float c = gdn_conv(a, pos, 0, cqk);
-  const float v = tid < GDN_D ? gdn_conv(a, pos, 0, cv) : 0.f;
+  const float v = tid < GDN_DEC_COLS ? gdn_conv(a, pos, 0, cv) : 0.f;
   float av = 0.f, bv = 0.f;
   if (a.ab) {
     av = __half2float(a.ab[h]);
@@ -464,47 +490,56 @@ __global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(const GdnArgs a0)
   if ((tid & 31) == 0) red[warp] = sq;
   __syncthreads();
   const float part = tid < GDN_D ? red[0] + red[1] + red[2] + red[3] : red[4] + red[5] + red[6] + red[7];
-  if (tid < GDN_D) {
-    qs[i] = c * rsqrtf(part / GDN_D + 1e-6f) * (1.f / GDN_D);
-    vs[i] = v;
-  } else {
-    ks[i] = c * rsqrtf(part / GDN_D + 1e-6f) * rsqrtf((float)GDN_D);
-  }
+  if (tid < GDN_D) qs[i] = c * rsqrtf(part / GDN_D + 1e-6f) * (1.f / GDN_D);
+  else ks[i] = c * rsqrtf(part / GDN_D + 1e-6f) * rsqrtf((float)GDN_D);
+  if (tid < GDN_DEC_COLS) vs[tid] = v;
   const int slot = pos & 3;
-  if (h < a.nk) a.conv_state[(int64_t)slot * a.C + cqk] = a.proj[cqk];
-  if (tid < GDN_D) a.conv_state[(int64_t)slot * a.C + cv] = a.proj[cv];
+  if (crank == 0 && h < a.nk) a.conv_state[(int64_t)slot * a.C + cqk] = a.proj[cqk];
+  if (tid < GDN_DEC_COLS) a.conv_state[(int64_t)slot * a.C + cv] = a.proj[cv];
   __syncthreads();
 
-  const int j = tid >> 1, r = tid & 1;
-  float4* sp = reinterpret_cast<float4*>(a.state + ((int64_t)h * GDN_D + j) * GDN_D + 64 * r);
-  float S[64];
+  const int col = tid >> 3, seg = tid & 7;
+  const int j = col0 + col;
+  float* sp = a.state + ((int64_t)h * GDN_D + j) * GDN_D + seg;
+  float S[16];
 #pragma unroll
-  for (int m = 0; m < 16; m++) {
-    const float4 t4 = sp[m];
-    S[4 * m] = t4.x;
-    S[4 * m + 1] = t4.y;
-    S[4 * m + 2] = t4.z;
-    S[4 * m + 3] = t4.w;
-  }
-  float kv = 0.f;
+  for (int r = 0; r < 16; r++) S[r] = sp[8 * r];
+  float kv0 = 0.f, kv1 = 0.f;
 #pragma unroll
-  for (int m = 0; m < 64; m++) {
-    S[m] *= g;
-    kv = fmaf(S[m], ks[64 * r + m], kv);
+  for (int r = 0; r < 16; r += 2) {
+    S[r] *= g;
+    S[r + 1] *= g;
+    kv0 = fmaf(S[r], ks[seg + 8 * r], kv0);
+    kv1 = fmaf(S[r + 1], ks[seg + 8 * r + 8], kv1);
   }
+  float kv = kv0 + kv1;
   kv += __shfl_xor_sync(0xffffffffu, kv, 1);
-  const float u = (vs[j] - kv) * beta;
-  float y = 0.f;
+  kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+  kv += __shfl_xor_sync(0xffffffffu, kv, 4);
+  const float u = (vs[col] - kv) * beta;
+  float y0 = 0.f, y1 = 0.f;
 #pragma unroll
-  for (int m = 0; m < 64; m++) {
-    S[m] = fmaf(ks[64 * r + m], u, S[m]);
-    y = fmaf(S[m], qs[64 * r + m], y);
+  for (int r = 0; r < 16; r += 2) {
+    S[r] = fmaf(ks[seg + 8 * r], u, S[r]);
+    S[r + 1] = fmaf(ks[seg + 8 * r + 8], u, S[r + 1]);
+    y0 = fmaf(S[r], qs[seg + 8 * r], y0);
+    y1 = fmaf(S[r + 1], qs[seg + 8 * r + 8], y1);
   }
+  float y = y0 + y1;
   y += __shfl_xor_sync(0xffffffffu, y, 1);
+  y += __shfl_xor_sync(0xffffffffu, y, 2);
+  y += __shfl_xor_sync(0xffffffffu, y, 4);
 #pragma unroll
-  for (int m = 0; m < 16; m++) sp[m] = make_float4(S[4 * m], S[4 * m + 1], S[4 * m + 2], S[4 * m + 3]);
-  const float ss = block_sum(r == 0 ? y * y : 0.f, red);
-  if (r == 0) {
+  for (int r = 0; r < 16; r++) sp[8 * r] = S[r];
+  // sum of y^2 over this CTA's columns, then over the cluster's CTAs
+  const float ss_cta = block_sum(seg == 0 ? y * y : 0.f, red);
+  if (tid == 0) part_ss = ss_cta;
+  cluster_sync_all();
+  float ss = 0.f;
+#pragma unroll
+  for (int q = 0; q < GDN_DEC_SPLIT; q++) ss += ld_shared_cluster_f32(&part_ss, (uint32_t)q);
+  cluster_sync_all();  // no CTA leaves while a peer may still read its part_ss
+  if (seg == 0) {
     const float z = a.proj[a.C + h * GDN_D + j];
     store_out(a.out, a.dt, obase + (int64_t)h * GDN_D + j, y * rsqrtf(ss / GDN_D + a.eps) * a.norm_w[j] * silu(z));
   }
@@ -772,7 +807,8 @@ int gdn_run(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t 
   a.dt = out_dtype;
   cudaStream_t st = (cudaStream_t)stream;
   if (T == 1) {
-    launch_pdl(gdn_decode_kernel, dim3((unsigned)nv, (unsigned)batch), dim3(2 * GDN_D), 0, st, a);
+    launch_pdl_cluster(gdn_decode_kernel, dim3((unsigned)(nv * GDN_DEC_SPLIT), (unsigned)batch), dim3(2 * GDN_D),
+                       GDN_DEC_SPLIT, st, a);
     return launched("gsq_gdn (one token)");
   }
   uint8_t* p = static_cast<uint8_t*>(scratch);
