@@ -48,6 +48,7 @@ constexpr int QMV_PRODUCER = QMV_CWARPS;               // warp streaming packed 
 constexpr int QMV_COMBINER = QMV_CWARPS + 1;           // warp combining tiles split between CTAs
 constexpr int QMV_THREADS = QMV_CTHREADS + 64;
 constexpr int QMV_NS_MAX = 4;                          // ring stages at most
+constexpr int QMV_MIN_UNITS = 8;                       // (tile, block) units per CTA at least
 constexpr int QMV_CTA_SMEM = 112 * 1024;               // two CTAs per SM
 constexpr int QMV_XBYTES_PER_BLOCK = 2 * QK + 8 * 4 + 16 * 4;  // per activation row: levels, scales, half sums
 constexpr int QMV_RED_BUFS = QMV_NS_MAX + 1;          // per-warp row-sum buffers (ring depth + 1)
@@ -1132,6 +1133,12 @@ static QmvPlan qmv_plan_compute(int t, int64_t N, int64_t K, int rows, bool one_
   const int64_t slots = std::max<int64_t>(1, (int64_t)occ * qmv_sm_count() / p.btiles);
   int64_t ctas = std::max<int64_t>(1, slots / p.slices);
   ctas = std::min<int64_t>(ctas, p.tiles * w_min);
+  // At least QMV_MIN_UNITS (tile, block) units per CTA: a CTA quantises the
+  // whole activation slice whatever its share, so small matrices (the row
+  // shards of 4-8 ranks) ran faster on fewer CTAs (the 33-configuration
+  // sweep at 1/8 of the rows: 268 -> 246 us; at 1/4: 287 -> 278 us; full
+  // and half matrices keep one CTA per resident slot).
+  ctas = std::min<int64_t>(ctas, std::max<int64_t>(1, p.tiles * w_min / QMV_MIN_UNITS));
   // Single-slice piece slots must fit the always-zero fixed region.
   ctas = std::min<int64_t>(ctas, (int64_t)(QMV_TICKET_BYTES / ((size_t)p.btiles * nb * 16 * sizeof(float))));
   p.aligned = 0;

@@ -68,7 +68,7 @@ def _check_pair(lib, qtype, w, n, k, rows, seed):
     ("Q4_K", 5120, 5120, 1, True),      # tiles shared between CTAs: published pieces in the scratch
     ("IQ2_XS", 17408, 5120, 1, True),
     ("IQ3_S", 5120, 17408, 2, True),
-    ("Q6_K", 1000, 2048, 3, True),
+    ("Q6_K", 1000, 8192, 3, True),
     ("IQ4_XS", 4736, 5120, 1, False),   # whole tiles per CTA on 148 SMs: no scratch at all
 ])
 def test_noalloc_matches_workspace_entry_point(qtype, n, k, rows, split):
