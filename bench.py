@@ -717,7 +717,8 @@ def main():
         calls = [(type_id(c["q"]), dev_xb.data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16], c["packed"].data_ptr(),
                   c["rows"], c["k"], 1, c["region"].regions, world, rank, rank * c["rows"], c["n"], wsp, wsn, stream)
                  for c, xo in zip(cfgs, xoff)]
-        outs = [(host_yb[yo:yo + c["n"]], c["region"].y.reshape(-1)) for c, yo in zip(cfgs, yoff)]
+        ys = [c["region"].y.reshape(-1) for c in cfgs]
+        dev_yb = torch.empty(ny, dtype=torch.float32, device=dev)
         qmvg = lib.gsq_qmv_gather
 
         def e2e_step():
@@ -726,12 +727,13 @@ def main():
                 rc = qmvg(*args_)
                 if rc:
                     _lib.check(rc)
-            for hy, y in outs:
-                hy.copy_(y, non_blocking=True)
+            torch.cat(ys, out=dev_yb)  # one kernel: the gathered outputs side by side
+            host_yb.copy_(dev_yb, non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
         e2e_path = ("activations of the step in one pinned host buffer -> one copy to the device -> one "
                     "gsq_qmv_gather C-ABI call per projection (this rank's rows, every rank's rows gathered) -> "
-                    "each gathered output copied to one pinned host buffer; one stream synchronisation per step")
+                    "the gathered outputs concatenated on the device (one kernel) and copied to one pinned host "
+                    "buffer; one stream synchronisation per step")
 
     log("per-configuration sweep done")
     for _ in range(2):
