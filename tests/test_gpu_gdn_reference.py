@@ -151,7 +151,9 @@ def test_gdn_matches_reference_override():
         got = out.cpu().numpy()
         return rel_l2(got, exp), rel_l2(state.cpu().numpy(), ref.state)
 
-    for T, with_ab in ((9, True), (1, False), (1, False), (3, False), (12, True), (1, False)):
+    # longer prompts too (100 and 70 tokens, the state carried in)
+    for T, with_ab in ((9, True), (1, False), (1, False), (3, False), (12, True), (1, False), (100, True),
+                       (1, False), (70, False), (1, False)):
         e_out, e_state = run(T, with_ab)
         assert e_out <= TOL, (T, with_ab, e_out)
         assert e_state <= TOL, (T, with_ab, e_state)
