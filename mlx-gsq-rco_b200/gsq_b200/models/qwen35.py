@@ -442,14 +442,18 @@ class Qwen35:
         """The gated-DeltaNet block on the q|k|v|z projection p of input h:
         a prompt of p.shape[0] tokens of sequence 0, or (``decode``) one token
         of each of the batch's p.shape[0] sequences.  The 2 x 48 gate rows
-        (plain fp16) are a cuBLAS GEMM for prompts and are computed inside the
-        block's first kernel for decode tokens."""
+        (plain fp16) are a cuBLAS GEMM for prompts and for decode batches of 8
+        sequences and more, and are computed inside the block's kernel for
+        smaller decode batches (there every CTA of a head recomputes them, a
+        cost that grows with the batch)."""
         cfg, T = self.cfg, p.shape[0]
         nk, nv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
         lib = _lib.load()
         if decode:
             out = torch.empty(T, nv * cfg.linear_value_head_dim, dtype=torch.float16, device=self.dev)
-            _lib.check(lib.gsq_gdn_batch(p.data_ptr(), p.stride(0), None, 0, h.data_ptr(), h.stride(0),
+            ab = F.linear(h, L["ab"]) if T >= 8 else None
+            _lib.check(lib.gsq_gdn_batch(p.data_ptr(), p.stride(0), ab.data_ptr() if ab is not None else None,
+                                         ab.stride(0) if ab is not None else 0, h.data_ptr(), h.stride(0),
                                          L["ab"].data_ptr(), cfg.hidden_size, T, nk, nv, L["conv_state"].data_ptr(),
                                          self.pos.data_ptr(), L["conv_w"].data_ptr(), L["A"].data_ptr(),
                                          L["dt_bias"].data_ptr(), L["norm"].data_ptr(), self.eps,
