@@ -431,26 +431,29 @@ __global__ void __launch_bounds__(GDN_D) gdn_scan_kernel(GdnArgs a) {
   }
 }
 
-// One token (T == 1) of the whole block in one launch: a cluster of
-// GDN_DEC_SPLIT CTAs per value head h, 256 threads each.  Every CTA of the
-// cluster forms the q and k channels of key head h % nk (threads 0..127 q,
-// 128..255 k: conv, then the rms norms) and the two gate dot products; CTA
-// rank c owns value columns 32c .. 32c + 31: thread (col = tid / 8,
-// seg = tid % 8) holds column 32c + col at key indices seg, seg + 8, ...,
-// seg + 120 in registers and applies the recurrence (8-lane shuffle
-// reductions).  The gated norm needs the sum of y^2 over the head's 128
-// columns: each CTA posts its columns' sum in shared memory and reads the
-// others' through the cluster's distributed shared memory.  The conv window
-// slot of this position is written by rank 0 of the clusters that own the
-// channels (q/k: h < nk) and is not read by any CTA at this position.
+// One token (T == 1) of the whole block in one launch, SPLIT CTAs per value
+// head h (SPLIT = 4: a thread-block cluster, for few heads x sequences;
+// SPLIT = 1: one CTA of 1024 threads per head, for batches that fill the
+// GPU anyway -- every CTA of a cluster repeats the head's q/k conv and norms
+// and gate dot products, which a large batch pays 4 times).  Every CTA forms
+// the q and k channels of key head h % nk (threads 0..127 q, 128..255 k:
+// conv, then the rms norms) and the two gate dot products; CTA rank c owns
+// value columns COLS c .. COLS c + COLS - 1 (COLS = 128 / SPLIT): thread
+// (col = tid / 8, seg = tid % 8) holds column COLS c + col at key indices
+// seg, seg + 8, ..., seg + 120 in registers and applies the recurrence
+// (8-lane shuffle reductions).  The gated norm needs the sum of y^2 over the
+// head's 128 columns: with SPLIT > 1 each CTA posts its columns' sum in
+// shared memory and reads the others' through the cluster's distributed
+// shared memory.  The conv window slot of this position is written by rank 0
+// of the CTAs that own the channels (q/k: h < nk) and is not read by any CTA
+// at this position.
 // Batched decode: blockIdx.y is the sequence b of the batch, whose token is
 // row b of proj / x / ab, whose conv ring and state follow the previous
 // sequence's (4*C and nv*128*128 floats), and whose output is row b of out;
 // every sequence is at position *pos.
-constexpr int GDN_DEC_SPLIT = 4;
-constexpr int GDN_DEC_COLS = GDN_D / GDN_DEC_SPLIT;
-
-__global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(const GdnArgs a0) {
+template <int SPLIT>
+__global__ void __launch_bounds__(8 * GDN_D / SPLIT) gdn_decode_kernel(const GdnArgs a0) {
+  constexpr int GDN_DEC_SPLIT = SPLIT, GDN_DEC_COLS = GDN_D / SPLIT;
   __shared__ float red[32];
   __shared__ float qs[GDN_D], ks[GDN_D], vs[GDN_DEC_COLS];
   __shared__ float part_ss;
@@ -464,14 +467,21 @@ __global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(const GdnArgs a0)
   a.conv_state = a0.conv_state + seq * 4 * a0.C;
   a.state = a0.state + seq * a0.nv * GDN_D * GDN_D;
   const int64_t obase = seq * a0.nv * GDN_D;
-  const int crank = blockIdx.x % GDN_DEC_SPLIT;  // == %cluster_ctarank (cluster dims GDN_DEC_SPLIT x 1 x 1)
+  const int crank = blockIdx.x % GDN_DEC_SPLIT;  // == %cluster_ctarank (cluster dims SPLIT x 1 x 1)
   const int h = blockIdx.x / GDN_DEC_SPLIT, kh = h % a.nk, tid = threadIdx.x, warp = tid >> 5;
   const int pos = *a.pos;
   const int i = tid & (GDN_D - 1);
   const int cqk = (tid < GDN_D ? 0 : a.nk * GDN_D) + kh * GDN_D + i;
   const int col0 = crank * GDN_DEC_COLS;
   const int cv = 2 * a.nk * GDN_D + h * GDN_D + col0 + tid;  // threads 0..31: this CTA's v channels
-  const float c = gdn_conv(a, pos, 0, cqk);
+  // this thread's state entries first: their loads overlap the conv, norms and gates below
+  const int col = tid >> 3, seg = tid & 7;
+  const int j = col0 + col;
+  float* sp = a.state + ((int64_t)h * GDN_D + j) * GDN_D + seg;
+  float S[16];
+#pragma unroll
+  for (int r = 0; r < 16; r++) S[r] = sp[8 * r];
+  const float c = tid < 2 * GDN_D ? gdn_conv(a, pos, 0, cqk) : 0.f;  // threads past 255: state columns only
   const float v = tid < GDN_DEC_COLS ? gdn_conv(a, pos, 0, cv) : 0.f;
   float av = 0.f, bv = 0.f;
   if (a.ab) {
@@ -491,19 +501,13 @@ __global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(const GdnArgs a0)
   __syncthreads();
   const float part = tid < GDN_D ? red[0] + red[1] + red[2] + red[3] : red[4] + red[5] + red[6] + red[7];
   if (tid < GDN_D) qs[i] = c * rsqrtf(part / GDN_D + 1e-6f) * (1.f / GDN_D);
-  else ks[i] = c * rsqrtf(part / GDN_D + 1e-6f) * rsqrtf((float)GDN_D);
+  else if (tid < 2 * GDN_D) ks[i] = c * rsqrtf(part / GDN_D + 1e-6f) * rsqrtf((float)GDN_D);
   if (tid < GDN_DEC_COLS) vs[tid] = v;
   const int slot = pos & 3;
-  if (crank == 0 && h < a.nk) a.conv_state[(int64_t)slot * a.C + cqk] = a.proj[cqk];
+  if (crank == 0 && h < a.nk && tid < 2 * GDN_D) a.conv_state[(int64_t)slot * a.C + cqk] = a.proj[cqk];
   if (tid < GDN_DEC_COLS) a.conv_state[(int64_t)slot * a.C + cv] = a.proj[cv];
   __syncthreads();
 
-  const int col = tid >> 3, seg = tid & 7;
-  const int j = col0 + col;
-  float* sp = a.state + ((int64_t)h * GDN_D + j) * GDN_D + seg;
-  float S[16];
-#pragma unroll
-  for (int r = 0; r < 16; r++) S[r] = sp[8 * r];
   float kv0 = 0.f, kv1 = 0.f;
 #pragma unroll
   for (int r = 0; r < 16; r += 2) {
@@ -533,12 +537,15 @@ __global__ void __launch_bounds__(2 * GDN_D) gdn_decode_kernel(const GdnArgs a0)
   for (int r = 0; r < 16; r++) sp[8 * r] = S[r];
   // sum of y^2 over this CTA's columns, then over the cluster's CTAs
   const float ss_cta = block_sum(seg == 0 ? y * y : 0.f, red);
-  if (tid == 0) part_ss = ss_cta;
-  cluster_sync_all();
-  float ss = 0.f;
+  float ss = ss_cta;
+  if constexpr (SPLIT > 1) {
+    if (tid == 0) part_ss = ss_cta;
+    cluster_sync_all();
+    ss = 0.f;
 #pragma unroll
-  for (int q = 0; q < GDN_DEC_SPLIT; q++) ss += ld_shared_cluster_f32(&part_ss, (uint32_t)q);
-  cluster_sync_all();  // no CTA leaves while a peer may still read its part_ss
+    for (int q = 0; q < GDN_DEC_SPLIT; q++) ss += ld_shared_cluster_f32(&part_ss, (uint32_t)q);
+    cluster_sync_all();  // no CTA leaves while a peer may still read its part_ss
+  }
   if (seg == 0) {
     const float z = a.proj[a.C + h * GDN_D + j];
     store_out(a.out, a.dt, obase + (int64_t)h * GDN_D + j, y * rsqrtf(ss / GDN_D + a.eps) * a.norm_w[j] * silu(z));
@@ -807,8 +814,10 @@ int gdn_run(const float* proj, int64_t proj_stride, const uint16_t* ab, int64_t 
   a.dt = out_dtype;
   cudaStream_t st = (cudaStream_t)stream;
   if (T == 1) {
-    launch_pdl_cluster(gdn_decode_kernel, dim3((unsigned)(nv * GDN_DEC_SPLIT), (unsigned)batch), dim3(2 * GDN_D),
-                       GDN_DEC_SPLIT, st, a);
+    if (nv * batch < 2 * 148)  // few heads x sequences: 4 CTAs (a cluster) per head
+      launch_pdl_cluster(gdn_decode_kernel<4>, dim3((unsigned)(nv * 4), (unsigned)batch), dim3(2 * GDN_D), 4, st, a);
+    else
+      launch_pdl(gdn_decode_kernel<1>, dim3((unsigned)nv, (unsigned)batch), dim3(8 * GDN_D), 0, st, a);
     return launched("gsq_gdn (one token)");
   }
   uint8_t* p = static_cast<uint8_t*>(scratch);

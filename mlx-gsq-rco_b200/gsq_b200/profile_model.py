@@ -3,6 +3,11 @@
     python -m gsq_b200.profile_model [prompt_tokens] [tokens]
     python -m gsq_b200.profile_model prefill [prompt_tokens]
     python -m gsq_b200.profile_model gdn
+    python -m gsq_b200.profile_model batch [B] [prompt_tokens] [steps]
+
+The fourth form is the first one for a decode batch: the prompt's state is
+forked into B sequences (``fork``) and the batch's decode-step graph is
+profiled per step.
 
 The third form times the gated-DeltaNet block alone (``gsq_gdn`` at the
 model's 16 key / 48 value heads) for prompts of 1, 16, 128 and 512 tokens:
@@ -111,21 +116,23 @@ def gdn(lengths=(1, 16, 128, 512)) -> None:
         raise RuntimeError("device status after the gsq_gdn timing")
 
 
-def main(prompt: int = 182, tokens: int = 4) -> None:
+def main(prompt: int = 182, tokens: int = 4, batch: int = 1) -> None:
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
     cfg = Qwen35Config()
-    model = build_qwen35(random_weights(cfg, dev, seed=0), cfg, dev, max_len=prompt + tokens + 16)
+    model = build_qwen35(random_weights(cfg, dev, seed=0), cfg, dev, max_len=prompt + tokens + 16, max_batch=batch)
     ids = torch.randint(0, cfg.vocab_size, (prompt,), device=dev, dtype=torch.int32)
     model.prefill(ids)
-    model.decode_step()
+    if batch > 1:
+        model.fork(batch)
+    model.decode_step([int(t) for t in torch.randint(0, cfg.vocab_size, (batch,))] if batch > 1 else None)
     model.capture_decode()
     model.replay_decode(3)
     torch.cuda.synchronize()
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         model.replay_decode(tokens)
         torch.cuda.synchronize()
-    _table(prof, tokens, "token")
+    _table(prof, tokens, "token" if batch == 1 else f"step of {batch}")
 
 
 if __name__ == "__main__":
@@ -133,5 +140,8 @@ if __name__ == "__main__":
         prefill(*(int(a) for a in sys.argv[2:3]))
     elif len(sys.argv) > 1 and sys.argv[1] == "gdn":
         gdn()
+    elif len(sys.argv) > 1 and sys.argv[1] == "batch":
+        rest = [int(v) for v in sys.argv[2:5]]
+        main(*rest[1:], batch=rest[0] if rest else 8)
     else:
         main(*(int(a) for a in sys.argv[1:3]))
