@@ -677,7 +677,10 @@ def main():
     # As a C-ABI host drives it: the step's activations sit in one pinned
     # host buffer and go to the device in one copy; one call per projection
     # (device pointers prepared once); the outputs come back to one pinned
-    # host buffer; one synchronisation per step.
+    # host buffer in one copy.  Steps are pipelined: each step's upload and
+    # readback run on copy streams with two device / host buffers, so they
+    # overlap the neighbouring steps' kernels, and the host waits for a
+    # step's outputs on the host one step later.
     xoff, yoff = [], []
     nx = ny = 0
     for c in cfgs:
@@ -688,76 +691,100 @@ def main():
     host_xb = torch.zeros(nx, dtype=torch.float16).pin_memory()
     for c, o in zip(cfgs, xoff):
         host_xb[o:o + c["k"]] = c["x"].reshape(-1).cpu()
-    host_yb = torch.empty(ny, dtype=torch.float32).pin_memory()
-    dev_xb = torch.empty(nx, dtype=torch.float16, device=dev)
+    host_yb = [torch.empty(ny, dtype=torch.float32).pin_memory() for _ in range(2)]
+    dev_xb = [torch.empty(nx, dtype=torch.float16, device=dev) for _ in range(2)]
+    dev_yb = [torch.empty(ny, dtype=torch.float32, device=dev) for _ in range(2)]
     need = max(lib.gsq_qmv_workspace_size(type_id(c["q"]), c["rows"], c["k"], 1) for c in cfgs)
     ws = _lib.workspaces.get(dev, need, "qmv")
     wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
     stream = _lib.stream_ptr(dev)
+    main_st = torch.cuda.current_stream(dev)
+    up_st, down_st = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_up, ev_done, ev_down = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
     h2d, d2h = nx * 2, ny * 4
     if world == 1:
-        dev_yb = torch.empty(ny, dtype=torch.float32, device=dev)
-        calls = [(type_id(c["q"]), dev_xb.data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16], c["packed"].data_ptr(),
-                  c["rows"], c["k"], 1, dev_yb.data_ptr() + 4 * yo, _lib.DTYPE_CODES[torch.float32], wsp, wsn, stream)
-                 for c, xo, yo in zip(cfgs, xoff, yoff)]
-        qmv = lib.gsq_qmv
+        calls = [[(type_id(c["q"]), dev_xb[b].data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16],
+                   c["packed"].data_ptr(), c["rows"], c["k"], 1, dev_yb[b].data_ptr() + 4 * yo,
+                   _lib.DTYPE_CODES[torch.float32], wsp, wsn, stream)
+                  for c, xo, yo in zip(cfgs, xoff, yoff)] for b in range(2)]
+        fn = lib.gsq_qmv
 
-        def e2e_step():
-            dev_xb.copy_(host_xb, non_blocking=True)
-            for args_ in calls:
-                rc = qmv(*args_)
+        def kernels(b):
+            for args_ in calls[b]:
+                rc = fn(*args_)
                 if rc:
                     _lib.check(rc)
-            host_yb.copy_(dev_yb, non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()
         e2e_path = ("activations of the step in one pinned host buffer -> one copy to the device -> one gsq_qmv "
                     "C-ABI call per projection (ctypes, device pointers prepared once) -> outputs in one copy to "
-                    "pinned host memory; one stream synchronisation per step")
+                    "pinned host memory; uploads and readbacks on two copy streams with two buffers each, "
+                    "overlapping the neighbouring steps' kernels; the host waits for each step's outputs")
     else:
-        calls = [(type_id(c["q"]), dev_xb.data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16], c["packed"].data_ptr(),
-                  c["rows"], c["k"], 1, c["region"].regions, world, rank, rank * c["rows"], c["n"], wsp, wsn, stream)
-                 for c, xo in zip(cfgs, xoff)]
+        calls = [[(type_id(c["q"]), dev_xb[b].data_ptr() + 2 * xo, _lib.DTYPE_CODES[torch.float16],
+                   c["packed"].data_ptr(), c["rows"], c["k"], 1, c["region"].regions, world, rank,
+                   rank * c["rows"], c["n"], wsp, wsn, stream)
+                  for c, xo in zip(cfgs, xoff)] for b in range(2)]
         ys = [c["region"].y.reshape(-1) for c in cfgs]
-        dev_yb = torch.empty(ny, dtype=torch.float32, device=dev)
-        qmvg = lib.gsq_qmv_gather
+        fn = lib.gsq_qmv_gather
 
-        def e2e_step():
-            dev_xb.copy_(host_xb, non_blocking=True)
-            for args_ in calls:
-                rc = qmvg(*args_)
+        def kernels(b):
+            for args_ in calls[b]:
+                rc = fn(*args_)
                 if rc:
                     _lib.check(rc)
-            torch.cat(ys, out=dev_yb)  # one kernel: the gathered outputs side by side
-            host_yb.copy_(dev_yb, non_blocking=True)
-            torch.cuda.current_stream(dev).synchronize()
+            torch.cat(ys, out=dev_yb[b])  # one kernel: the gathered outputs side by side
         e2e_path = ("activations of the step in one pinned host buffer -> one copy to the device -> one "
                     "gsq_qmv_gather C-ABI call per projection (this rank's rows, every rank's rows gathered) -> "
                     "the gathered outputs concatenated on the device (one kernel) and copied to one pinned host "
-                    "buffer; one stream synchronisation per step")
+                    "buffer; uploads and readbacks on two copy streams with two buffers each, overlapping the "
+                    "neighbouring steps' kernels; the host waits for each step's outputs")
+
+    def e2e_step(s):
+        b = s & 1
+        with torch.cuda.stream(up_st):
+            up_st.wait_event(ev_done[b])        # the kernels of step s - 2 have read this input buffer
+            dev_xb[b].copy_(host_xb, non_blocking=True)
+            ev_up[b].record(up_st)
+        main_st.wait_event(ev_up[b])
+        main_st.wait_event(ev_down[b])          # the outputs of step s - 2 have left this buffer
+        kernels(b)
+        ev_done[b].record(main_st)
+        with torch.cuda.stream(down_st):
+            down_st.wait_event(ev_done[b])
+            host_yb[b].copy_(dev_yb[b], non_blocking=True)
+            ev_down[b].record(down_st)
+        if s >= 1:
+            ev_down[b ^ 1].synchronize()         # step s - 1's outputs are on the host
+
+    def e2e_finish():
+        main_st.wait_stream(up_st)
+        main_st.wait_stream(down_st)
 
     log("per-configuration sweep done")
-    for _ in range(2):
-        e2e_step()
+    for s_ in range(2):
+        e2e_step(s_)
+    e2e_finish()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     log("e2e warm-up done")
-    e2e_steps = max(3, args.steps // 4)
+    e2e_steps = max(10, args.steps // 2)  # the pipeline's fill and drain are one step each
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     clocks.mark_start()
     t0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
+    for s_ in range(e2e_steps):
+        e2e_step(s_)
+    e2e_finish()
     t1.record()
     torch.cuda.synchronize()
     clocks.mark_end()
     device_ok(lib, dev, "the e2e steps")
     e2e_ms = t0.elapsed_time(t1)
+    host_last = host_yb[(e2e_steps - 1) & 1]
     # the host copy of the outputs is the library's result
     for c, yo in zip(cfgs, yoff):
         ref = matvec(c, c["x"]).reshape(-1).cpu()
-        if not torch.allclose(host_yb[yo:yo + ref.numel()], ref, rtol=1e-6, atol=0):
+        if not torch.allclose(host_last[yo:yo + ref.numel()], ref, rtol=1e-6, atol=0):
             raise RuntimeError("end-to-end outputs differ from the library call")
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev)
