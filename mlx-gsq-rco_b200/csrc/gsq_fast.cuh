@@ -468,6 +468,7 @@ template <> struct Fast<T_IQ1_M> {
 template <int T>
 struct MvDecode {
   static constexpr bool UNSIGNED = false;
+  static constexpr bool NIBBLE_ORDER = false;  // activations of a 32-group in natural order
   static constexpr bool SPLIT = Fast<T>::SPLIT;
   static constexpr int TAB_BYTES = Fast<T>::TAB_BYTES;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { Fast<T>::load_tables(tab, tid, nthr); }
@@ -479,9 +480,30 @@ struct MvDecode {
 
 static __device__ __align__(16) const int8_t kIq3xxsSigned[256 * 16 * 4] = GSQ_INIT_IQ3XXS_SIGNED;
 
+// IQ4_XS: the matvec stores the activations of every 32-group in the
+// order of the packed word's nibbles (byte 4tq + i of the group holds
+// element 4tq + i/2 (i even) or 16 + 4tq + i/2 (i odd), and byte 16 + 4tq + i
+// element 4tq + 2 + i/2 or 18 + 4tq + i/2), so the two lookups of a word
+// feed the MMA as they come and the two byte permutes that restore element
+// order (Fast<T_IQ4_XS>::entry) go away.  The MMA's sum is the same in any
+// k order that weights and activations share.
+template <>
+struct MvDecode<T_IQ4_XS> {
+  static constexpr bool UNSIGNED = false, SPLIT = false, NIBBLE_ORDER = true;
+  static constexpr int TAB_BYTES = Fast<T_IQ4_XS>::TAB_BYTES;
+  __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { Fast<T_IQ4_XS>::load_tables(tab, tid, nthr); }
+  __device__ static float xgroup_scale(int) { return 1.f; }
+  __device__ static void entry(const uint8_t* b, int c32, int tq, const uint8_t* tab, uint32_t& lo, uint32_t& hi) {
+    const uint4 kv = *reinterpret_cast<const uint4*>(tab);
+    const uint32_t w = ld32a4(b + 8 + 16 * c32 + 4 * tq);
+    lo = lut16(w, kv.x, kv.y, kv.z, kv.w);          // elements 4tq, 16+4tq, 4tq+1, 17+4tq
+    hi = lut16(w >> 16, kv.x, kv.y, kv.z, kv.w);    // elements 4tq+2, 18+4tq, 4tq+3, 19+4tq
+  }
+};
+
 template <>
 struct MvDecode<T_IQ3_XXS> {
-  static constexpr bool UNSIGNED = false, SPLIT = false;
+  static constexpr bool UNSIGNED = false, SPLIT = false, NIBBLE_ORDER = false;
   static constexpr int TAB_BYTES = 256 * 16 * 4;
   __device__ static void load_tables(uint8_t* tab, int tid, int nthr) { copy16(tab, kIq3xxsSigned, TAB_BYTES, tid, nthr); }
   __device__ static float xgroup_scale(int) { return 1.f; }
@@ -495,7 +517,7 @@ struct MvDecode<T_IQ3_XXS> {
 
 template <>
 struct MvDecode<T_Q4_K> {  // odd 32-groups are the high nibbles: 16 q <= 240
-  static constexpr bool UNSIGNED = true, SPLIT = false;
+  static constexpr bool UNSIGNED = true, SPLIT = false, NIBBLE_ORDER = false;
   static constexpr int TAB_BYTES = 0;
   __device__ static void load_tables(uint8_t*, int, int) {}
   __device__ static float xgroup_scale(int g) { return (g & 1) ? 0.0625f : 1.f; }
@@ -509,7 +531,7 @@ struct MvDecode<T_Q4_K> {  // odd 32-groups are the high nibbles: 16 q <= 240
 
 template <>
 struct MvDecode<T_Q2_K> {  // 32-group g reads bit plane g & 3: 4^p q <= 192
-  static constexpr bool UNSIGNED = true, SPLIT = false;
+  static constexpr bool UNSIGNED = true, SPLIT = false, NIBBLE_ORDER = false;
   static constexpr int TAB_BYTES = 0;
   __device__ static void load_tables(uint8_t*, int, int) {}
   __device__ static float xgroup_scale(int g) {

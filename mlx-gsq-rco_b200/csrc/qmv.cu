@@ -280,6 +280,20 @@ template <> __device__ __forceinline__ void unpack8<__nv_bfloat16>(const uint4 (
 // first (one round trip per CH * 256 chunks, a K = 20480 row at fp16), then
 // quantises them; the four lanes holding a 32-group combine max and sums with
 // shuffles.
+// Levels of one 32-group (words 0..7 = elements 4q..4q+3) into the nibble
+// order of MvDecode<T>::NIBBLE_ORDER formats: word tq = elements
+// 4tq, 16+4tq, 4tq+1, 17+4tq; word 4+tq = 4tq+2, 18+4tq, 4tq+3, 19+4tq.
+__device__ __forceinline__ void nibble_order(uint32_t (&hw)[8], uint32_t (&lw)[8]) {
+#pragma unroll
+  for (int tq = 0; tq < 4; tq++) {
+    const uint32_t h0 = hw[tq], h1 = hw[4 + tq], l0 = lw[tq], l1 = lw[4 + tq];
+    hw[tq] = __byte_perm(h0, h1, 0x5140u);
+    hw[4 + tq] = __byte_perm(h0, h1, 0x7362u);
+    lw[tq] = __byte_perm(l0, l1, 0x5140u);
+    lw[4 + tq] = __byte_perm(l0, l1, 0x7362u);
+  }
+}
+
 template <int T, int NB, bool SUMS, typename XT, int CH>
 __device__ __forceinline__ void quantise_round(const QmvArgs& a, int btile, int kb0, int KS, int per_row, int total,
                                                int base, int8_t* xq, float* xs, float* xsum) {
@@ -331,6 +345,24 @@ __device__ __forceinline__ void quantise_round(const QmvArgs& a, int btile, int 
       const uint32_t z23 = __byte_perm(t[4 * q + 2], t[4 * q + 3], 0x5140);
       lw[q] = __byte_perm(z01, z23, 0x5410) ^ 0x80808080u;
       hw[q] = __byte_perm(z01, z23, 0x7632);
+    }
+    if constexpr (MvDecode<T>::NIBBLE_ORDER) {
+      // This thread holds words 2lc, 2lc+1 of its 32-group (lc = chunk & 3);
+      // words q and q + 4 pair up, so chunk lc pairs with chunk lc ^ 2 (the
+      // thread two lanes away: consecutive chunks are consecutive threads).
+      const int lc = (base + threadIdx.x) & 3;
+#pragma unroll
+      for (int q = 0; q < 2; q++) {
+        const uint32_t ph = __shfl_xor_sync(0xffffffffu, hw[q], 2);
+        const uint32_t pl = __shfl_xor_sync(0xffffffffu, lw[q], 2);
+        if (lc < 2) {
+          hw[q] = __byte_perm(hw[q], ph, 0x5140u);
+          lw[q] = __byte_perm(lw[q], pl, 0x5140u);
+        } else {
+          hw[q] = __byte_perm(ph, hw[q], 0x7362u);
+          lw[q] = __byte_perm(pl, lw[q], 0x7362u);
+        }
+      }
     }
     if (c < total) {
       const int b = c >= per_row ? 1 : 0;
@@ -422,6 +454,7 @@ __device__ void quantise_staged(int groups, int KS, int8_t* xq, float* xs, float
       lw[q] = __byte_perm(z01, z23, 0x5410) ^ 0x80808080u;
       hw[q] = __byte_perm(z01, z23, 0x7632);
     }
+    if constexpr (MvDecode<T>::NIBBLE_ORDER) nibble_order(hw, lw);
     uint4* qh = reinterpret_cast<uint4*>(xq + gg * 32);
     uint4* ql = reinterpret_cast<uint4*>(xq + KS + gg * 32);
     qh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
