@@ -123,7 +123,7 @@ struct Mv<T_IQ2_XXS> {
                                uint32_t& hi, uint32_t& mlo, uint32_t& mhi) {
     const uint2 g = lds64(tab + 8 * ((r.grid[S] >> (8 * e)) & 255u));
     lo = g.x; hi = g.y;
-    sign_masks(ksign((r.aux[S] >> (7 * e)) & 127u), mlo, mhi);
+    ksign_masks((r.aux[S] >> (7 * e)) & 127u, mlo, mhi);
   }
   template <int S, int NB>
   __device__ static void unit(const uint8_t*, const Row<NB>& r, int, int C, int N, float xs, float, float& A, float&) {
