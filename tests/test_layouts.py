@@ -73,3 +73,25 @@ def test_packed_bytes_config_sizes():
     assert random_matrix("Q4_K", 4, 512).size == packed_bytes("Q4_K", 4, 512)
     with pytest.raises(ValueError):
         packed_bytes("Q4_K", 4, 500)
+
+
+def _prmt_sign_replicate(word: int) -> int:
+    """prmt.b32 d, word, 0, 0xBA98: every byte becomes 0xFF if its msb is set."""
+    return sum(0xFF << (8 * j) for j in range(4) if (word >> (8 * j + 7)) & 1)
+
+
+def test_ksign_masks_constant_matches_ksigns():
+    """gsq_fast.cuh's ksign_masks spreads the 7-bit sign index with one
+    64-bit multiply and takes the parity into bit 63; for every index the
+    byte masks must equal those of gguf-py's ksigns byte."""
+    import re
+    src = open(os.path.join(os.path.dirname(__file__), "..", "mlx-gsq-rco_b200", "csrc", "gsq_fast.cuh")).read()
+    body = src[src.index("void ksign_masks("):]
+    mult = int(re.search(r"\(uint64_t\)i7 \* (0x[0-9A-Fa-f]+)ull", body).group(1), 16)
+    ks = tables.ksigns()
+    for i7 in range(128):
+        t = (i7 * mult) & ((1 << 64) - 1)
+        hi = ((t >> 32) | ((bin(i7).count("1") << 31) & 0xFFFFFFFF)) & 0xFFFFFFFF
+        got = _prmt_sign_replicate(t & 0xFFFFFFFF) | (_prmt_sign_replicate(hi) << 32)
+        want = sum(0xFF << (8 * j) for j in range(8) if (int(ks[i7]) >> j) & 1)
+        assert got == want, i7
