@@ -80,7 +80,7 @@ def _worker(rank, world, port, qtype, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_row_parallel_gloo(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
