@@ -7,6 +7,10 @@ a packed matrix is one contiguous byte span ``[n*rb, (n+1)*rb)`` with
 rows with no repacking: rank r of P keeps rows ``[r*N/P, (r+1)*N/P)`` and
 computes its slice of y with the local QMV/QMM kernel; the slices are joined
 with one NCCL ``all_gather_into_tensor`` over NVLink.
+
+A projection can also split by 256-wide input blocks (``InputParallelLinear``):
+each rank multiplies its blocks of every row with its part of x, and the
+partial outputs are summed over the ranks.
 """
 from __future__ import annotations
 
@@ -15,6 +19,7 @@ import torch.distributed as dist
 
 from ..quant.layouts import QUANT_BLOCK_SIZES, type_id
 from ..runtime.store import PackedWeight
+from .heads import ffn_blocks, take_input_blocks
 
 
 def shard_bounds(n_rows: int, world: int, rank: int) -> tuple[int, int]:
@@ -124,3 +129,73 @@ class RowParallelLinear(torch.nn.Module):
         for r in self._regions.values():
             r.close()
         self._regions.clear()
+
+
+def block_bounds(in_features: int, world: int, rank: int) -> tuple[int, int]:
+    """256-wide input blocks [b0, b1) owned by ``rank``: as even as whole
+    blocks allow (the first ``blocks % world`` ranks hold one more)."""
+    r = ffn_blocks(in_features, world, rank)
+    return r.start, r.stop
+
+
+def reduce_partials(y: torch.Tensor, group=None) -> torch.Tensor:
+    """Sums the ranks' partial outputs in place (NCCL on CUDA tensors, the
+    group's backend otherwise); every rank returns the same sum."""
+    if dist.get_world_size(group) > 1:
+        dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
+    return y
+
+
+class InputParallelLinear(torch.nn.Module):
+    """A packed projection split by 256-wide input blocks across the ranks
+    of ``group``: the counterpart of ``RowParallelLinear`` for the
+    projection that reads a head-split block's local outputs (``heads.py``).
+
+    Rank r keeps every output row's input blocks ``blocks`` (by default an
+    even run, ``block_bounds``; a head plan's ``out_blocks`` otherwise) and
+    ``forward(x_local)`` multiplies them with its own inputs x_local (the
+    matching columns of the full input, ``local_columns``), in fp32, then
+    sums the partials over the ranks. Every rank returns the full
+    ``(..., out_features)`` output, in x_local's dtype unless ``out_dtype``
+    says otherwise."""
+
+    def __init__(self, weight: PackedWeight, group=None, blocks=None, bias: torch.Tensor | None = None,
+                 local_fn=None):
+        super().__init__()
+        from ..nn.linear import GSQLinear
+        self.group = group
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world, self.rank = world, rank
+        self.out_features, self.in_features = weight.logical_shape
+        if blocks is None:
+            blocks = range(*block_bounds(self.in_features, world, rank))
+        self.blocks = tuple(int(b) for b in blocks)
+        if not self.blocks:
+            raise ValueError("a rank needs at least one input block")
+        k_local = len(self.blocks) * 256
+        data = take_input_blocks(weight.data, weight.quantization_type, self.out_features, self.in_features,
+                                 self.blocks)
+        self.shard = PackedWeight(name=f"{weight.name}[{len(self.blocks)} input blocks]", data=data,
+                                  gguf_shape=(k_local, self.out_features),
+                                  logical_shape=(self.out_features, k_local),
+                                  quantization_type=weight.quantization_type,
+                                  quantization_type_id=weight.quantization_type_id,
+                                  num_elements=self.out_features * k_local, num_bytes=data.numel())
+        self.bias = bias
+        self.local = local_fn or GSQLinear(self.shard)
+        self._local_fn = local_fn is not None
+
+    def local_columns(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's inputs: the columns of the full input x that its blocks read."""
+        idx = torch.tensor([b * 256 + i for b in self.blocks for i in range(256)], device=x.device)
+        return x.index_select(-1, idx)
+
+    def forward(self, x_local: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        if x_local.shape[-1] != len(self.blocks) * 256:
+            raise ValueError("x_local must hold this rank's input columns")
+        y = self.local(x_local) if self._local_fn else self.local(x_local, out_dtype=torch.float32)
+        y = reduce_partials(y.float().contiguous(), self.group)
+        if self.bias is not None:
+            y = y + self.bias
+        return y.to(out_dtype or x_local.dtype)
