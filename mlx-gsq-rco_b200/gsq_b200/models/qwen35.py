@@ -173,6 +173,93 @@ def random_weights(cfg: Qwen35Config, device, seed: int = 0, type_mix: dict[str,
     return out
 
 
+def head_split_weights(weights: dict, cfg: Qwen35Config, world: int, rank: int) -> tuple[dict, Qwen35Config]:
+    """One rank's weights of the head-split layout (``parallel/heads.py``),
+    by GGUF name, and the rank's local configuration.
+
+    Each gated-DeltaNet layer keeps the rank's key heads and the value heads
+    that read them (``linear_attention_heads``). That covers its rows of
+    attn_qkv, attn_gate, ssm_alpha, ssm_beta and the conv taps, its entries
+    of ssm_a and ssm_dt.bias, and its input blocks of ssm_out. Each
+    attention layer keeps its query heads and their key/value heads
+    (``attention_heads``): its rows of attn_q, attn_k and attn_v, and its
+    input blocks of attn_output. Each FFN keeps a run of 256-wide blocks of
+    the intermediate width (``ffn_blocks``): those rows of ffn_gate and
+    ffn_up, and the same input blocks of ffn_down. Embedding, LM head and
+    norm weights are kept whole. Packed tensors are byte selections of the
+    payload (``take_rows`` / ``take_input_blocks``), on the payload's
+    device.
+
+    The local configuration has the rank's head counts and intermediate
+    width. Running the model on it, with the ranks' partial outputs of
+    ssm_out, attn_output and ffn_down summed before each residual add,
+    computes the whole model."""
+    from dataclasses import replace
+    from ..parallel.heads import attention_heads, ffn_blocks, linear_attention_heads, take_input_blocks, take_rows
+    cfg.check()
+    dk, dv, hd = cfg.linear_key_head_dim, cfg.linear_value_head_dim, cfg.head_dim
+    gdn = linear_attention_heads(cfg.linear_num_key_heads, cfg.linear_num_value_heads, world, rank, dv)
+    att = attention_heads(cfg.num_attention_heads, cfg.num_key_value_heads, world, rank, hd)
+    ffn = ffn_blocks(cfg.intermediate_size, world, rank)
+    inter = 256 * len(ffn)
+    local = replace(cfg, linear_num_key_heads=len(gdn.key_heads), linear_num_value_heads=len(gdn.value_heads),
+                    num_attention_heads=len(att.query_heads), num_key_value_heads=len(att.kv_heads),
+                    intermediate_size=inter)
+
+    def rows(name, idx):
+        w = weights[name]
+        n, k = w.logical_shape
+        data = take_rows(w.data, w.quantization_type, n, k, idx)
+        return PackedWeight.from_packed(f"{name}[rank {rank}/{world}]", data, w.quantization_type, (len(idx), k),
+                                        device=None)
+
+    def cols(name, blocks):
+        w = weights[name]
+        n, k = w.logical_shape
+        data = take_input_blocks(w.data, w.quantization_type, n, k, blocks)
+        return PackedWeight.from_packed(f"{name}[rank {rank}/{world}]", data, w.quantization_type,
+                                        (n, 256 * len(blocks)), device=None)
+
+    def plain(name, idx):
+        t = weights[name]
+        return t.index_select(0, torch.as_tensor(idx, dtype=torch.long, device=t.device)).contiguous()
+
+    ffn_rows = list(range(256 * ffn.start, 256 * ffn.stop))
+    out = {}
+    for name in ("token_embd.weight", "output_norm.weight", "output.weight"):
+        out[name] = weights[name]
+    for i in range(cfg.num_hidden_layers):
+        p = f"blk.{i}."
+        for n in ("attn_norm.weight", "post_attention_norm.weight"):
+            out[p + n] = weights[p + n]
+        out[p + "ffn_gate.weight"] = rows(p + "ffn_gate.weight", ffn_rows)
+        out[p + "ffn_up.weight"] = rows(p + "ffn_up.weight", ffn_rows)
+        out[p + "ffn_down.weight"] = cols(p + "ffn_down.weight", list(ffn))
+        if cfg.is_linear(i):
+            qkv = gdn.qkv_rows(dk, dv)
+            vh = list(gdn.value_heads)
+            out[p + "attn_qkv.weight"] = rows(p + "attn_qkv.weight", qkv)
+            out[p + "attn_gate.weight"] = rows(p + "attn_gate.weight", gdn.gate_rows(dv))
+            out[p + "ssm_out.weight"] = cols(p + "ssm_out.weight", gdn.out_blocks(dv))
+            out[p + "ssm_alpha.weight"] = plain(p + "ssm_alpha.weight", vh)
+            out[p + "ssm_beta.weight"] = plain(p + "ssm_beta.weight", vh)
+            conv = weights[p + "ssm_conv1d.weight"].reshape(-1, cfg.linear_conv_kernel_dim)  # [channel, tap]
+            out[p + "ssm_conv1d.weight"] = conv.index_select(
+                0, torch.as_tensor(qkv, dtype=torch.long, device=conv.device)).contiguous()
+            out[p + "ssm_a"] = plain(p + "ssm_a", vh)
+            out[p + "ssm_dt.bias"] = plain(p + "ssm_dt.bias", vh)
+            out[p + "ssm_norm.weight"] = weights[p + "ssm_norm.weight"]
+        else:
+            kv = att.kv_rows(hd)
+            out[p + "attn_q.weight"] = rows(p + "attn_q.weight", att.q_rows(hd))
+            out[p + "attn_k.weight"] = rows(p + "attn_k.weight", kv)
+            out[p + "attn_v.weight"] = rows(p + "attn_v.weight", kv)
+            out[p + "attn_output.weight"] = cols(p + "attn_output.weight", att.out_blocks(hd))
+            out[p + "attn_q_norm.weight"] = weights[p + "attn_q_norm.weight"]
+            out[p + "attn_k_norm.weight"] = weights[p + "attn_k_norm.weight"]
+    return out, local
+
+
 class _Packed:
     """A packed projection: flat uint8 payload of n rows x k inputs.
 

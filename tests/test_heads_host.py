@@ -13,6 +13,10 @@ Checked here:
     summed, equals the whole layer (float64 restatements of the
     gated-DeltaNet block, of the gated attention block and of the SwiGLU
     FFN, with rel-L2 <= 1e-12);
+  * the whole model (``head_split_weights``): a small Qwen3.5-hybrid model
+    with random packed weights (dequantised by the C oracle), run in float64
+    by 2 and 4 ranks' head-split weights in lockstep, gives the whole
+    model's prompt logits (rel-L2 <= 1e-10);
   * InputParallelLinear on 2 and 4 gloo ranks: the reduced partials equal
     the whole product on every rank.
 """
@@ -321,3 +325,75 @@ def test_input_parallel_gloo(world):
         p.join(timeout=120)
     results = sorted(q.get(timeout=5) for _ in range(world))
     assert results == [(r, True) for r in range(world)]
+
+
+# ------------------------- the whole model: head-split weights, float64
+
+def _model64(rank_weights, rank_cfgs, ids, dense):
+    """Prompt logits of the Qwen3.5-hybrid model from position 0, float64,
+    run by every rank's weights in lockstep: each block's output projection
+    (ssm_out, attn_output, ffn_down) is each rank's partial, summed over the
+    ranks before the residual add; embedding, norms and LM head are whole.
+    One rank with the whole weights is the whole model."""
+    cfg0 = rank_cfgs[0]
+    eps = cfg0.rms_norm_eps
+    W0 = rank_weights[0]
+    x = dense(W0["token_embd.weight"])[ids]
+    for i in range(cfg0.num_hidden_layers):
+        p = f"blk.{i}."
+        h = _rms(x, W0[p + "attn_norm.weight"].double().numpy(), eps)
+        d = 0.0
+        for W, c in zip(rank_weights, rank_cfgs):
+            if c.is_linear(i):
+                nk, nv = c.linear_num_key_heads, c.linear_num_value_heads
+                qkv, z = h @ dense(W[p + "attn_qkv.weight"]).T, h @ dense(W[p + "attn_gate.weight"]).T
+                a = h @ W[p + "ssm_alpha.weight"].double().numpy().T
+                b = h @ W[p + "ssm_beta.weight"].double().numpy().T
+                o = _gdn(qkv, z, a, b, W[p + "ssm_conv1d.weight"].double().numpy(), W[p + "ssm_a"].double().numpy(),
+                         W[p + "ssm_dt.bias"].double().numpy(), W[p + "ssm_norm.weight"].double().numpy(), nk, nv)
+                d = d + o @ dense(W[p + "ssm_out.weight"]).T
+            else:
+                pr = np.concatenate([h @ dense(W[p + n]).T for n in ("attn_q.weight", "attn_k.weight",
+                                                                     "attn_v.weight")], 1)
+                o = _attention(pr, c.num_attention_heads, c.num_key_value_heads,
+                               W[p + "attn_q_norm.weight"].double().numpy(),
+                               W[p + "attn_k_norm.weight"].double().numpy(), hd=c.head_dim, rot=c.rotary_dim,
+                               theta=c.rope_theta)
+                d = d + o @ dense(W[p + "attn_output.weight"]).T
+        x = x + d
+        h2 = _rms(x, W0[p + "post_attention_norm.weight"].double().numpy(), eps)
+        f = 0.0
+        for W in rank_weights:
+            g, u = h2 @ dense(W[p + "ffn_gate.weight"]).T, h2 @ dense(W[p + "ffn_up.weight"]).T
+            f = f + (_silu(g) * u) @ dense(W[p + "ffn_down.weight"]).T
+        x = x + f
+    return _rms(x, W0["output_norm.weight"].double().numpy(), eps) @ dense(W0["output.weight"]).T
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_head_split_weights_compute_the_whole_model(world, oracle_mod):
+    from gsq_b200.models import Qwen35Config, head_split_weights, random_weights, tensor_shapes
+    cfg = Qwen35Config(hidden_size=512, intermediate_size=1280, num_hidden_layers=4, num_attention_heads=8,
+                       num_key_value_heads=2, vocab_size=320, linear_num_value_heads=24, linear_num_key_heads=8)
+    weights = random_weights(cfg, "cpu", seed=1)
+    cache = {}
+
+    def dense(w):
+        key = id(w)
+        if key not in cache:
+            n, k = w.logical_shape
+            cache[key] = oracle_mod.dequantize_c(w.data.numpy(), w.quantization_type).reshape(n, k).astype(np.float64)
+        return cache[key]
+
+    ranks = [head_split_weights(weights, cfg, world, r) for r in range(world)]
+    for w, c in ranks:  # every local tensor has the shape the local configuration names
+        for name, shape in tensor_shapes(c).items():
+            got = w[name].logical_shape if hasattr(w[name], "logical_shape") else tuple(w[name].shape)
+            assert tuple(got) == tuple(shape), (name, got, shape)
+    assert sum(c.intermediate_size for _, c in ranks) == cfg.intermediate_size
+    assert sum(c.linear_num_value_heads for _, c in ranks) == cfg.linear_num_value_heads
+    ids = np.array([3, 17, 250, 99, 3])
+    whole = _model64([weights], [cfg], ids, dense)
+    split = _model64([w for w, _ in ranks], [c for _, c in ranks], ids, dense)
+    assert np.all(np.isfinite(whole))
+    assert _rel(split, whole) < 1e-10
