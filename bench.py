@@ -387,7 +387,7 @@ def embed_bench(dev, pk, lib, clocks, ts=(1, 182, 512)):
 
 
 def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, prefill_ms=(512, 2048),
-                batches=(1, 8, 64)):
+                batches=(1, 8, 64), layout="rows"):
     """The Qwen3.5-hybrid 27B decoder (64 layers: 48 gated-DeltaNet + 16
     gated GQA, hidden 5120, SwiGLU 17408, vocab 248320) with random-init
     packed weights of the config's type mix.  A ``prompt``-token prefill and
@@ -398,16 +398,23 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
     each timed region; every decode step reads all packed projections (12 GB,
     ~90x L2).  With ``world`` > 1 every packed projection is split by output
     rows over the ranks (the gathers fused into the matvec and the matmul
-    epilogue); times are the max over ranks."""
+    epilogue), or with ``layout`` "heads" each rank keeps its heads and FFN
+    blocks and the blocks' partial outputs are all-reduced; times are the
+    max over ranks."""
     import torch
     import torch.distributed as dist
-    from gsq_b200.models import Qwen35Config, build_qwen35, random_weights
+    from gsq_b200.models import Qwen35Config, build_qwen35, build_qwen35_head_split, random_weights
 
     cfg = Qwen35Config()
-    w = random_weights(cfg, dev, seed=0)  # the same bytes on every rank; each keeps its rows
+    w = random_weights(cfg, dev, seed=0)  # the same bytes on every rank; each keeps its part
     max_len = max((prompt,) + tuple(prefill_ms)) + decode_tokens + 16
-    model = build_qwen35(w, cfg, dev, max_len=max_len, max_batch=max(batches),
-                         group=dist.group.WORLD if world > 1 else None)
+    heads = layout == "heads" and world > 1
+    # packed bytes one decode token reads over all ranks: every projection and one embedding row
+    whole_bytes = sum(v.num_bytes for k, v in w.items() if hasattr(v, "num_bytes") and k != "token_embd.weight") \
+        + w["token_embd.weight"].num_bytes // cfg.vocab_size
+    build = build_qwen35_head_split if heads else build_qwen35
+    model = build(w, cfg, dev, max_len=max_len, max_batch=max(batches),
+                  group=dist.group.WORLD if world > 1 else None)
     del w
     torch.cuda.empty_cache()
     log("model built")
@@ -437,7 +444,7 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
 
     out = {"workload": "Qwen3.5-hybrid 27B (64 layers, 48 gated-DeltaNet + 16 GQA), random-init packed weights "
                        "(embedding/LM head Q6_K, FFN gate/up IQ2_XS|IQ2_S, down Q4_K, attention IQ3_S|IQ4_XS)",
-           "packed_bytes_per_token": model.packed_bytes_per_token()}
+           "packed_bytes_per_token": whole_bytes if heads else model.packed_bytes_per_token()}
     for T in (prompt,) + tuple(prefill_ms):
         ids = torch.randint(0, cfg.vocab_size, (T,), device=dev, generator=gen, dtype=torch.int32)
         model.prefill(ids)  # warm-up (workspaces, attention plans)
@@ -469,7 +476,11 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
                 "decode_note": "greedy decode after the prompt prefill; each step one CUDA-graph replay of the "
                                "whole step for the batch; roofline = packed weight bytes per step / time vs the "
                                "measured HBM copy peak" + (f" x {world} GPUs" if world > 1 else "")})
-    if world > 1:
+    if heads:
+        out["parallelism"] = (f"tp{world} head-split: each rank its gated-DeltaNet / attention heads and FFN "
+                              "blocks; the blocks' partial output projections summed by NCCL all-reduce; the LM "
+                              "head split by vocabulary rows, gathered in the matvec")
+    elif world > 1:
         out["parallelism"] = (f"tp{world}: every packed projection split by output rows; the row gathers fused "
                               "into the matvec (decode, batch 1) and the matmul epilogue (prefill, batch >= 8) "
                               "over NVLink")
@@ -495,6 +506,9 @@ def main():
     ap.add_argument("--no-qmm", action="store_true")
     ap.add_argument("--no-model", action="store_true")
     ap.add_argument("--no-embed", action="store_true")
+    ap.add_argument("--tp-layout", default="rows", choices=["rows", "heads"],
+                    help="model section with --gpus > 1: split every projection by output rows (default), or "
+                         "keep heads per rank and all-reduce the blocks' partial outputs")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -909,7 +923,7 @@ def main():
     model = None
     if not args.no_model:
         try:
-            model = model_bench(dev, pk, lib, clocks, world)
+            model = model_bench(dev, pk, lib, clocks, world, layout=args.tp_layout)
         except Exception as e:  # recorded in the line; the QMV and QMM results above still stand
             model = {"error": f"{type(e).__name__}: {e}"[:300]}
 

@@ -42,6 +42,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from .. import _lib
+from ..parallel.tp import reduce_partials
 from ..runtime.kernels import packed_embedding, quantized_matvec
 from ..runtime.store import PackedWeight
 
@@ -391,13 +392,23 @@ class Qwen35:
     (``gsq_qmv_gather``), prompts inside the matmul epilogue
     (``gsq_qmm_gather``; prompts of 2-7 tokens, an NCCL all-gather).
     Norms, the gated-DeltaNet and attention blocks run on every rank on the
-    gathered (identical) vectors."""
+    gathered (identical) vectors.
+
+    With ``reduce_group`` instead (the head-split layout,
+    ``build_qwen35_head_split``) the weights and ``cfg`` are one rank's
+    (``head_split_weights``): the blocks run on the rank's heads and
+    intermediate blocks, the partial outputs of ssm_out / attn_output /
+    ffn_down are summed over the ranks (NCCL all-reduce) before each
+    residual add, and the LM head is split by vocabulary rows and gathered
+    as with ``group``."""
 
     def __init__(self, weights: dict, cfg: Qwen35Config, device, max_len: int = 2304, group=None,
-                 max_batch: int = 1):
+                 max_batch: int = 1, reduce_group=None):
         cfg.check()
         if max_batch < 1:
             raise ValueError("max_batch must be at least 1")
+        if group is not None and reduce_group is not None:
+            raise ValueError("a model splits by output rows (group) or by heads (reduce_group), not both")
         self.cfg, self.dev, self.max_len = cfg, torch.device(device), max_len
         self.max_batch, self.batch = int(max_batch), 1
         self.eps = cfg.rms_norm_eps
@@ -436,6 +447,10 @@ class Qwen35:
                 L["v_cache"] = torch.zeros(max_batch, max_len, nkv, hd, device=self.dev)
             self.layers.append(L)
         self.world = dist.get_world_size(group) if group is not None else 1
+        self.reduce_group = reduce_group if reduce_group is not None and dist.get_world_size(reduce_group) > 1 \
+            else None
+        if self.reduce_group is not None:
+            self.lm_head.shard(self.reduce_group)  # vocabulary rows, gathered in the matvec (or by NCCL)
         self._prefill_regions = {}
         if self.world > 1:
             for pk in self._projections():
@@ -617,8 +632,12 @@ class Qwen35:
                 p = L["qkv"](h)
                 o = self._attn_decode(L, p) if pos0 is None else self._attn_prefill(L, p, pos0)
                 d = L["o"](o)
+            if self.reduce_group is not None:
+                d = reduce_partials(d, self.reduce_group)
             h2 = rmsnorm(x, d, L["post_norm"], self.eps)
             delta = L["down"](L["gate_up"].swiglu(h2))
+            if self.reduce_group is not None:
+                delta = reduce_partials(delta, self.reduce_group)
         return delta
 
     # ---- public ----
@@ -715,6 +734,19 @@ class Qwen35:
     @property
     def graph_logits(self) -> torch.Tensor:
         return self._graph_logits
+
+
+def build_qwen35_head_split(weights: dict, cfg: Qwen35Config | None = None, device="cuda", max_len: int = 2304,
+                            group=None, max_batch: int = 1) -> Qwen35:
+    """The model split by heads over the ranks of ``group``: this rank's
+    weights and configuration from ``head_split_weights``, the blocks'
+    partial outputs summed over the ranks (``Qwen35``'s ``reduce_group``).
+    Collective: every rank of the group builds its part."""
+    cfg = cfg or Qwen35Config()
+    world = dist.get_world_size(group) if group is not None else 1
+    rank = dist.get_rank(group) if group is not None else 0
+    local, local_cfg = head_split_weights(weights, cfg, world, rank)
+    return Qwen35(local, local_cfg, device, max_len=max_len, max_batch=max_batch, reduce_group=group)
 
 
 def build_qwen35(weights: dict, cfg: Qwen35Config | None = None, device="cuda", max_len: int = 2304,

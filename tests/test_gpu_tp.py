@@ -2,8 +2,9 @@
 holding its slice of a packed projection's rows, must reproduce the
 single-GPU result (matvec with the gather fused in, matmul with the gather
 fused into its epilogue, and the NCCL all-gather path), also over repeated
-calls and CUDA-graph replays of the fused gather.  Each world size is skipped
-when fewer GPUs are visible."""
+calls and CUDA-graph replays of the fused gather.  The model harness runs
+both split by output rows and in the head-split layout, against the same
+model on one GPU.  Each world size is skipped when fewer GPUs are visible."""
 import os
 import socket
 
@@ -259,3 +260,68 @@ def _model_worker(rank, world, port, q):
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_model_tensor_parallel(world):
     _spawn(_model_worker, world)
+
+
+def _model_heads_worker(rank, world, port, q):
+    """The harness in the head-split layout (each rank its heads and FFN
+    blocks, the blocks' partial outputs all-reduced) against the same model
+    on one GPU."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    from gsq_b200 import _lib
+    from gsq_b200.models import Qwen35Config, build_qwen35, build_qwen35_head_split, random_weights
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        # 16 key heads: two per rank at 8 ranks (whole 256-wide blocks of
+        # ssm_out); 18 FFN blocks: uneven over 4 and 8 ranks, at least 2 each
+        cfg = Qwen35Config(hidden_size=512, intermediate_size=4608, num_hidden_layers=4, num_attention_heads=8,
+                           num_key_value_heads=2, vocab_size=512, linear_num_value_heads=48,
+                           linear_num_key_heads=16)
+        w = random_weights(cfg, dev, seed=5)
+        one = build_qwen35(w, cfg, dev, max_len=64, max_batch=9)
+        hs = build_qwen35_head_split(w, cfg, dev, max_len=64, max_batch=9, group=dist.group.WORLD)
+        fails = []
+
+        def check(label, a, b, tol=1e-3):
+            e = float((a.float() - b.float()).norm() / b.float().norm())
+            if not e <= tol:
+                fails.append(f"{label}: {e:.3g}")
+
+        prompt = (torch.arange(12, dtype=torch.int32, device=dev) * 41) % cfg.vocab_size
+        check("prefill 12", hs.prefill(prompt), one.prefill(prompt))
+        long_prompt = (torch.arange(40, dtype=torch.int32, device=dev) * 17) % cfg.vocab_size
+        check("prefill 40", hs.prefill(long_prompt), one.prefill(long_prompt))
+        for t in (5, 77, 300):
+            check(f"decode {t}", hs.decode_step(t), one.decode_step(t))
+        hs.capture_decode()
+        one.capture_decode()
+        for i in range(3):
+            hs.replay_decode(1)
+            one.replay_decode(1)
+            check(f"graph step {i}", hs.graph_logits, one.graph_logits)
+            if int(hs.cur_id[0].item()) != int(one.cur_id[0].item()):
+                fails.append(f"graph step {i}: tokens differ")
+        hs.release_graph()
+        one.release_graph()
+        toks = [(13 * b + 3) % cfg.vocab_size for b in range(9)]
+        for m in (hs, one):
+            m.prefill(prompt)
+            m.fork(9)
+        check("batched decode 1", hs.decode_step(toks), one.decode_step(toks))
+        check("batched decode 2", hs.decode_step(toks), one.decode_step(toks))
+        torch.cuda.synchronize()
+        status = _lib.load().gsq_device_status(None)
+        if status:
+            fails.append(f"device status {status}")
+        hs.close()
+        q.put((rank, not fails, fails))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_model_head_split(world):
+    _spawn(_model_heads_worker, world)

@@ -115,3 +115,21 @@ def test_interleaved_join():
         _Packed([pa, PackedWeight.from_packed("c", random_matrix("IQ2_XS", 24, k, seed=5), "IQ2_XS", (24, k),
                                               device=None)], interleave=8)
 
+
+
+def test_head_split_build_on_one_rank():
+    """build_qwen35_head_split on one rank is the whole model (nothing to
+    reduce); a model takes one split, by rows or by heads."""
+    import torch
+    from gsq_b200.models import Qwen35, build_qwen35_head_split, random_weights
+    cfg = Qwen35Config(hidden_size=512, intermediate_size=1024, num_hidden_layers=4, num_attention_heads=8,
+                       num_key_value_heads=2, vocab_size=256, linear_num_value_heads=24, linear_num_key_heads=8)
+    w = random_weights(cfg, "cpu", seed=2)
+    m = build_qwen35_head_split(w, cfg, "cpu", max_len=16)
+    assert m.reduce_group is None and m.cfg == cfg
+    for L, i in zip(m.layers, range(cfg.num_hidden_layers)):
+        p = f"blk.{i}."
+        if L["linear"]:
+            assert torch.equal(L["qkvz"].data[:w[p + "attn_qkv.weight"].num_bytes], w[p + "attn_qkv.weight"].data)
+    with pytest.raises(ValueError):
+        Qwen35(w, cfg, "cpu", group=object(), reduce_group=object())
