@@ -185,10 +185,14 @@ class InputParallelLinear(torch.nn.Module):
         self.bias = bias
         self.local = local_fn or GSQLinear(self.shard)
         self._local_fn = local_fn is not None
+        self._columns: dict = {}  # column index tensor per device (local_columns)
 
     def local_columns(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's inputs: the columns of the full input x that its blocks read."""
-        idx = torch.tensor([b * 256 + i for b in self.blocks for i in range(256)], device=x.device)
+        idx = self._columns.get(x.device)
+        if idx is None:
+            idx = self._columns[x.device] = torch.tensor([b * 256 + i for b in self.blocks for i in range(256)],
+                                                         device=x.device)
         return x.index_select(-1, idx)
 
     def forward(self, x_local: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
