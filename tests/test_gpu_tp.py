@@ -2,9 +2,11 @@
 holding its slice of a packed projection's rows, must reproduce the
 single-GPU result (matvec with the gather fused in, matmul with the gather
 fused into its epilogue, and the NCCL all-gather path), also over repeated
-calls and CUDA-graph replays of the fused gather.  The model harness runs
-both split by output rows and in the head-split layout, against the same
-model on one GPU.  Each world size is skipped when fewer GPUs are visible."""
+calls and CUDA-graph replays of the fused gather.  A projection split by
+input blocks (partials all-reduced) must reproduce the whole product.  The
+model harness runs both split by output rows and in the head-split layout,
+against the same model on one GPU.  Each world size is skipped when fewer
+GPUs are visible."""
 import os
 import socket
 
@@ -190,6 +192,48 @@ def _spawn(target, world):
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_row_parallel(world):
     _spawn(_worker, world)
+
+
+def _input_parallel_worker(rank, world, port, q):
+    """InputParallelLinear: each rank's input blocks (an uneven run, and a
+    head plan's scattered blocks) with the partials all-reduced, against the
+    whole matrix on one GPU (matvec and matmul paths)."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    from gsq_b200.parallel import InputParallelLinear, linear_attention_heads
+    from gsq_b200.quant.synthetic import random_matrix_torch
+    from gsq_b200.runtime import PackedWeight
+    from gsq_b200.runtime.kernels import quantized_matvec
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    fails = []
+    try:
+        # ffn_down-like (uneven block runs) and ssm_out-like (a head plan's blocks)
+        cases = (("Q4_K", 640, 17 * 256, None),
+                 ("IQ4_XS", 512, 48 * 128, linear_attention_heads(16, 48, world, rank).out_blocks(128)))
+        for qtype, n, k, blocks in cases:
+            packed = random_matrix_torch(qtype, n, k, seed=4, device=dev)  # same bytes on every rank
+            w = PackedWeight.from_packed("w", packed, qtype, (n, k), device=dev)
+            layer = InputParallelLinear(w, blocks=blocks)
+            for rows in (1, 3, 40):
+                g = torch.Generator(device=dev).manual_seed(rows)
+                x = torch.randn(rows, k, device=dev, dtype=torch.float16, generator=g)
+                y = layer(layer.local_columns(x), out_dtype=torch.float32)
+                ref = quantized_matvec(x, packed, qtype=qtype, out_features=n, in_features=k,
+                                       out_dtype=torch.float32)
+                e = float((y - ref).norm() / ref.norm())
+                if not (y.shape == ref.shape and e <= 1e-3):
+                    fails.append(f"{qtype} rows {rows}: {e:.3g}")
+        q.put((rank, not fails, fails))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_input_parallel(world):
+    _spawn(_input_parallel_worker, world)
 
 
 def _model_worker(rank, world, port, q):
