@@ -415,6 +415,19 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
     build = build_qwen35_head_split if heads else build_qwen35
     model = build(w, cfg, dev, max_len=max_len, max_batch=max(batches),
                   group=dist.group.WORLD if world > 1 else None)
+    model_parity = None
+    if heads:
+        # The head-split model's prompt logits against the whole model on this
+        # GPU (every rank runs both; the head-split prefill is collective).
+        whole = build_qwen35(w, cfg, dev, max_len=64)
+        pids = (torch.arange(32, dtype=torch.int32, device=dev) * 7919) % cfg.vocab_size
+        err = torch.tensor([rel_l2(model.prefill(pids), whole.prefill(pids))], device=dev, dtype=torch.float64)
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+        whole.close()
+        del whole
+        model_parity = {"max_rel_l2": float(err.item()), "bar": PARITY_REL_L2, "ok": float(err.item()) <= PARITY_REL_L2,
+                        "against": "the whole model on one GPU: prompt logits of 32 tokens, max over ranks"}
+        log(f"model head-split parity {model_parity['max_rel_l2']:.2e}")
     del w
     torch.cuda.empty_cache()
     log("model built")
@@ -476,6 +489,8 @@ def model_bench(dev, pk, lib, clocks, world=1, prompt=182, decode_tokens=64, pre
                 "decode_note": "greedy decode after the prompt prefill; each step one CUDA-graph replay of the "
                                "whole step for the batch; roofline = packed weight bytes per step / time vs the "
                                "measured HBM copy peak" + (f" x {world} GPUs" if world > 1 else "")})
+    if model_parity is not None:
+        out["parity"] = model_parity
     if heads:
         out["parallelism"] = (f"tp{world} head-split: each rank its gated-DeltaNet / attention heads and FFN "
                               "blocks; the blocks' partial output projections summed by NCCL all-reduce; the LM "
@@ -934,6 +949,8 @@ def main():
     clocks.stop()
 
     parity["ok"] = parity["max_rel_l2"] <= PARITY_REL_L2 and parity.get("qmm_max_rel_l2", 0.0) <= PARITY_REL_L2
+    if isinstance(model, dict) and isinstance(model.get("parity"), dict) and not model["parity"]["ok"]:
+        parity["ok"] = False  # the head-split model disagreed with the whole model
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT,
